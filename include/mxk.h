@@ -1,0 +1,153 @@
+/*
+ * mxk.h -- C ABI of the B200 (sm_100a) MX-KMeans library, libmxkmeans.so.
+ *
+ * Every entry point returns an mxk_status; on failure mxk_last_error() returns a
+ * thread-local message.  Pointers named points/centroids/labels/... are DEVICE
+ * pointers owned by the caller unless the name says host_.  `stream` is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream).  Sizes are
+ * 64-bit where the reference used int, so N*D and N*K may exceed 2^31.
+ *
+ * Each entry point names the reference interface it replaces
+ * (ParCIS/MX-KMeans, include/kmeans.cuh and src/ ... file:line).  The C++
+ * drop-in header include/kmeans.cuh wraps these with the reference's exact
+ * signatures and exception behaviour.
+ */
+#ifndef MXK_H
+#define MXK_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MXK_OK = 0,
+    MXK_ERR_INVALID = 1,     /* bad argument (reference: std::invalid_argument) */
+    MXK_ERR_CUDA = 2,        /* CUDA runtime/driver error (reference: CUDA_CHECK) */
+    MXK_ERR_UNSUPPORTED = 3, /* shape or device outside what the kernels support */
+    MXK_ERR_NONFINITE = 4,   /* non-finite centroid shift (src/kmeans.cu:64) */
+    MXK_ERR_TIMEOUT = 5,     /* a bounded device wait gave up */
+    MXK_ERR_COMM = 6         /* NCCL error or unavailable */
+} mxk_status;
+
+/* Options of a Lloyd run.  Same fields and defaults as the reference's
+ * KMeansOptions (include/kmeans.cuh:11-16): 300, 0, 1e-4, 0. */
+typedef struct {
+    int max_iterations;
+    int fp32_iterations;
+    float tolerance;
+    int verbose;
+} mxk_options;
+
+const char* mxk_last_error(void);
+int mxk_version(void);
+/* Number of kernels this library launched since load (all devices). */
+uint64_t mxk_launch_count(void);
+
+/* ---- ops (include/kmeans.cuh:23-47) ------------------------------------ */
+
+/* compute_l2_norm, include/kmeans.cuh:23 / src/kernels/assignment.cu:7-16,60-63 */
+int mxk_compute_l2_norm(int64_t rows, int d, const float* points, float* norms, void* stream);
+
+/* quantize_rows, include/kmeans.cuh:42-43 / src/kernels/quantize.cu:13-72,111-123.
+ * bits in {4,6,8}; d % 32 == 0.  values: packed rows (rows*d*bits/8 bytes);
+ * scales: rows*(d/32) UE8M0 bytes, row-major; max_errors (optional, caller
+ * zeroed) receives the max squared reconstruction error per row.  pid (optional)
+ * maps output row r to source row pid[r]. */
+int mxk_quantize_rows(int bits, int64_t rows, int d, const float* points, const int* pid,
+                      void* values, uint8_t* scales, float* max_errors, void* stream);
+
+/* precompute_point_bounds, include/kmeans.cuh:35-36 / src/kernels/quantize.cu:74-98,125-128.
+ * upper: ceil(n/32)*96 floats. */
+int mxk_precompute_point_bounds(int64_t n, int d, const float* points, const float* norms,
+                                float* upper, void* stream);
+
+/* assign_precisions, include/kmeans.cuh:37-38 / src/kernels/quantize.cu:100-108,130-134 */
+int mxk_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc,
+                          float ec, int* precision, void* stream);
+
+/* gemm_mx, include/kmeans.cuh:46-47 / src/kernels/gemm.cu:348-363.
+ * out[m x n] (row-major FP32) = A[m x k] (packed MX{bits}) . B[n x k]^T (MXFP8),
+ * scales row-major per 32 features.  tcgen05 block-scaled MMA; k % 128 == 0. */
+int mxk_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales,
+                const uint8_t* b, const uint8_t* b_scales, float* out, void* stream);
+
+/* gemm_fp32, include/kmeans.cuh:45 / src/kernels/gemm.cu:365-380.
+ * out[m x n] = A[m x k] . B[n x k]^T in FP32 (no TF32). */
+int mxk_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,
+                  void* stream);
+
+/* assign_clusters, include/kmeans.cuh:31-33 / src/kernels/assignment.cu:19-57,65-71.
+ * labels[pid[r]] = argmin_c fmaf(-2, dots[r][c], pn[pid[r]] + cn[c]) (lowest index on
+ * ties); gaps[pid[r]] = largest - second largest distance (init -1e38 with pid,
+ * -1 without). */
+int mxk_assign_clusters(int64_t rows, int k, const float* point_norms, const float* centroid_norms,
+                        const float* dots, const int* pid, int* labels, float* gaps, void* stream);
+
+/* update_centroids, include/kmeans.cuh:24-25 / src/kernels/update.cu:7-31,41-52.
+ * centroids = per-cluster mean of points; empty clusters keep old_centroids. */
+int mxk_update_centroids(int64_t n, int d, int k, const float* points, const int* labels,
+                         const float* old_centroids, float* centroids, int* counts, void* stream);
+
+/* centroid_shift, include/kmeans.cuh:26-27 / src/kernels/update.cu:32-38,54-61.
+ * Writes sum((prev-cur)^2) to device_sum and (synchronously) to *host_result. */
+int mxk_centroid_shift(int64_t elements, const float* previous, const float* current,
+                       float* device_sum, float* host_result, void* stream);
+
+/* ---- fused hot op (replaces gemm_mx + assign_clusters, src/kmeans.cu:54-56) ---- */
+
+/* Nearest centroid of `rows` quantized points against k MXFP8 centroids with no
+ * N x K product buffer: tcgen05 MMA into TMEM, distance fmaf(-2,dot,pn+cn) and
+ * lowest-index argmin in the epilogue.  Writes labels[pid[r]] and, when gaps is
+ * not NULL, the two-largest gap (init -1e38) like assign_clusters. */
+int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, const uint8_t* a_scales,
+                        const uint8_t* b, const uint8_t* b_scales, const float* point_norms,
+                        const float* centroid_norms, const int* pid, int* labels, float* gaps,
+                        void* stream);
+
+/* ---- Lloyd driver --------------------------------------------------------- */
+
+/* kmeans_mixed, include/kmeans.cuh:20-21 / src/kmeans.cu:12-68.  Points n x d
+ * (d padded, % 128 == 0), centroids k x d in/out, labels n out.  *iterations
+ * receives the completed iteration count.  Synchronous on `stream`. */
+int mxk_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                     const mxk_options* options, int* iterations, void* stream);
+
+/* ---- multi-GPU (no counterpart in the reference, which is single-GPU) ------ */
+
+/* Row-sharded Lloyd: each rank holds n_local rows; centroids are replicated; per
+ * iteration the K x D sums and K counts are NCCL-allreduced.  comm comes from
+ * mxk_comm_init (one rank per GPU, any process layout). */
+int mxk_comm_unique_id(unsigned char id[128]);
+int mxk_comm_init(void** comm, int nranks, int rank, const unsigned char id[128]);
+int mxk_comm_destroy(void* comm);
+int mxk_kmeans_mixed_sharded(void* comm, int64_t n_local, int d, int k, const float* points,
+                             float* centroids, int* labels, const mxk_options* options,
+                             int* iterations, void* stream);
+
+/* ---- host-side helpers of the CLI (include/host_utils.hpp:40-141) -------- */
+
+/* K-Means++ (std::mt19937(seed) D^2 sampling) and farthest-first centroid
+ * initialisation on HOST arrays; same selections as the reference for a seed. */
+int mxk_host_init_kmeanspp(const float* points, int64_t n, int d, int k, uint32_t seed, float* out);
+int mxk_host_init_farthest(const float* points, int64_t n, int d, int k, float* out);
+/* Dense CSV with header, d features (+ optional ignored label column), zero
+ * padded to padded_d; rejects non-finite values and row-count mismatches. */
+int mxk_host_read_points(const char* path, int64_t n, int d, int padded_d, float* out);
+int mxk_host_write_labels(const char* path, const int* labels, int64_t n);
+
+/* ---- kernel timing (CUDA events around each launch on its stream) ---------- */
+int mxk_profile_enable(int on);
+/* Copies up to max entries of {name, launches, total_ms} for the current device. */
+typedef struct {
+    char name[48];
+    uint64_t launches;
+    double total_ms;
+} mxk_kernel_stat;
+int mxk_profile_read(mxk_kernel_stat* out, int max, int* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,176 @@
+// Host-side input/output and centroid initialisation of the mxkmeans CLI.
+//
+// Interface-compatible with ParCIS/MX-KMeans include/host_utils.hpp:1-141:
+//   * CSV: a header row, then rows of d features and optionally one ignored
+//     trailing label column; values must parse completely as finite floats; the
+//     row count must equal --n-samples; features are zero-padded to padded_d.
+//   * labels: "clusters" header, one label per line.
+//   * K-Means++ (D^2 sampling with std::mt19937(seed), the first index from
+//     uniform_int_distribution<int>(0, n-1), each next index by a
+//     uniform_real_distribution<double>(0, total) draw against the running sum of
+//     double squared distances) and farthest-first (from row 0, float distances,
+//     first maximum).  The draw sequence and the distance arithmetic are kept as
+//     in the reference so a seed selects the same centroids.
+#pragma once
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <fstream>
+#include <limits>
+#include <random>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace mxk_cli {
+
+inline std::vector<std::string> csv_cells(const std::string& line) {
+    std::vector<std::string> out;
+    size_t start = 0;
+    while (true) {
+        const size_t comma = line.find(',', start);
+        if (comma == std::string::npos) {
+            if (start < line.size()) out.push_back(line.substr(start));
+            break;
+        }
+        out.push_back(line.substr(start, comma - start));
+        start = comma + 1;
+    }
+    if (!line.empty() && line.back() == ',') out.emplace_back();
+    return out;
+}
+
+inline float parse_float(const std::string& text) {
+    size_t used = 0;
+    const float v = std::stof(text, &used);
+    if (!std::isfinite(v) || text.find_first_not_of(" \t\r", used) != std::string::npos)
+        throw std::invalid_argument("Invalid finite number: " + text);
+    return v;
+}
+
+inline int parse_int(const std::string& text) {
+    size_t used = 0;
+    const int v = std::stoi(text, &used);
+    if (used != text.size()) throw std::invalid_argument("Invalid integer: " + text);
+    return v;
+}
+
+inline bool blank(const std::string& line) { return line.find_first_not_of(" \t\r") == std::string::npos; }
+
+inline std::vector<float> read_points(const std::string& path, int64_t n, int d, int padded_d) {
+    std::ifstream in(path);
+    if (!in) throw std::runtime_error("Cannot open input: " + path);
+    std::string line;
+    if (!std::getline(in, line)) throw std::runtime_error("Input is empty");
+    const size_t columns = csv_cells(line).size();
+    if (columns != size_t(d) && columns != size_t(d) + 1)
+        throw std::runtime_error("CSV header must contain d features and optionally one label column");
+    std::vector<float> points(size_t(n) * padded_d, 0.0f);
+    int64_t row = 0;
+    while (std::getline(in, line)) {
+        if (blank(line)) continue;
+        if (row >= n) throw std::runtime_error("CSV contains more rows than --n-samples");
+        const auto cells = csv_cells(line);
+        if (cells.size() != columns)
+            throw std::runtime_error("Wrong column count at data row " + std::to_string(row + 1));
+        float* dst = points.data() + size_t(row) * padded_d;
+        for (int j = 0; j < d; ++j) {
+            try {
+                dst[j] = parse_float(cells[j]);
+            } catch (const std::exception&) {
+                throw std::runtime_error("Invalid feature at data row " + std::to_string(row + 1) + ", column " +
+                                         std::to_string(j + 1));
+            }
+        }
+        ++row;
+    }
+    if (in.bad()) throw std::runtime_error("Error while reading input: " + path);
+    if (row != n) throw std::runtime_error("CSV row count does not match --n-samples");
+    return points;
+}
+
+inline void write_labels(const std::string& path, const std::vector<int>& labels) {
+    std::ofstream out(path);
+    if (!out) throw std::runtime_error("Cannot open output: " + path);
+    out << "clusters\n";
+    for (int v : labels) out << v << '\n';
+    out.close();
+    if (!out) throw std::runtime_error("Failed to write output: " + path);
+}
+
+// Squared distance of row p to a center, accumulated in double.
+inline double sq_dist_double(const float* row, const float* center, int d) {
+    double s = 0.0;
+    for (int j = 0; j < d; ++j) {
+        const double diff = double(row[j]) - center[j];
+        s += diff * diff;
+    }
+    return s;
+}
+
+inline std::vector<float> init_kmeanspp(const std::vector<float>& points, int64_t n, int d, int k, uint32_t seed) {
+    std::mt19937 rng(seed);
+    std::vector<float> centers(size_t(k) * d);
+    std::vector<double> dist(size_t(n), std::numeric_limits<double>::infinity());
+    std::vector<char> chosen(size_t(n), 0);
+    int64_t pick = std::uniform_int_distribution<int>(0, int(n - 1))(rng);
+    for (int c = 0; c < k; ++c) {
+        const float* src = points.data() + size_t(pick) * d;
+        std::copy(src, src + d, centers.begin() + size_t(c) * d);
+        chosen[pick] = 1;
+        double total = 0.0;
+        const float* center = centers.data() + size_t(c) * d;
+        for (int64_t p = 0; p < n; ++p) {
+            const double v = sq_dist_double(points.data() + size_t(p) * d, center, d);
+            dist[p] = chosen[p] ? 0.0 : std::min(dist[p], v);
+            total += dist[p];
+        }
+        if (c + 1 == k) break;
+        pick = -1;
+        if (total > 0.0) {
+            const double target = std::uniform_real_distribution<double>(0.0, total)(rng);
+            double run = 0.0;
+            for (int64_t p = 0; p < n; ++p) {
+                run += dist[p];
+                if (!chosen[p] && dist[p] > 0.0 && run > target) {
+                    pick = p;
+                    break;
+                }
+            }
+        }
+        if (pick < 0) {  // all remaining rows duplicate a center, or rounding at the end of the sum
+            for (int64_t p = 0; p < n; ++p)
+                if (!chosen[p]) {
+                    pick = p;
+                    break;
+                }
+        }
+    }
+    return centers;
+}
+
+inline std::vector<float> init_farthest(const std::vector<float>& points, int64_t n, int d, int k) {
+    std::vector<float> centers(size_t(k) * d);
+    std::vector<float> dist(size_t(n), std::numeric_limits<float>::max());
+    int64_t pick = 0;
+    for (int c = 0; c < k; ++c) {
+        const float* src = points.data() + size_t(pick) * d;
+        std::copy(src, src + d, centers.begin() + size_t(c) * d);
+        for (int64_t p = 0; p < n; ++p) {
+            const float* row = points.data() + size_t(p) * d;
+            float s = 0.0f;
+            for (int j = 0; j < d; ++j) {
+                const float diff = row[j] - src[j];
+                s += diff * diff;
+            }
+            dist[p] = std::min(dist[p], s);
+        }
+        dist[pick] = -1.0f;
+        pick = std::max_element(dist.begin(), dist.end()) - dist.begin();
+    }
+    return centers;
+}
+
+}  // namespace mxk_cli

@@ -1,0 +1,296 @@
+// Lloyd driver of MX-KMeans on one GPU or on row shards over several GPUs.
+//
+// Reference: ParCIS/MX-KMeans src/kmeans.cu:12-68 (kmeans_mixed).  Per iteration,
+// in the reference's order:
+//   previous = centroids; centroid norms;
+//   FP32 iteration (it < fp32_iterations): FP32 product + assignment; or
+//   MX iteration: centroids -> MXFP8 (+ max squared error); ec, lc; precision of
+//   every point (select_precision: always MXFP8); stable per-precision compaction;
+//   for bits in {4,6,8}: quantize the group's points, product, assignment;
+//   update (sums, counts, empty-cluster keep); shift; stop when shift <= tol.
+//
+// Differences of form, not of result: ec/lc and the group sizes stay on the
+// device (no host round trips), the per-group quantize/GEMM read their row
+// counts from device memory, the product and assignment are one tcgen05 kernel
+// (no N x K buffer), workspaces come from the stream-ordered allocator, and the
+// shift is reduced in a fixed order so every rank of a sharded run sees the same
+// value.  The only host synchronization per iteration is the shift read-back the
+// stopping rule needs (as in the reference).
+//
+// The reference's precision policy ignores the two-largest distance gap
+// (include/precision.hpp:20-26), so the driver's fused assignment does not track
+// it; gaps stay at their initial zeros, exactly what select_precision receives
+// in the reference's first iteration and which it never reads.
+#include <dlfcn.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include <nccl.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mxk {
+
+// ---------------------------------------------------------------------------
+// NCCL, loaded on first use (the single-GPU library has no NCCL dependency).
+
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+static NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+#define MXK_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+        MXK_SYM(GetUniqueId, "ncclGetUniqueId");
+        MXK_SYM(CommInitRank, "ncclCommInitRank");
+        MXK_SYM(CommDestroy, "ncclCommDestroy");
+        MXK_SYM(CommAbort, "ncclCommAbort");
+        MXK_SYM(AllReduce, "ncclAllReduce");
+        MXK_SYM(GroupStart, "ncclGroupStart");
+        MXK_SYM(GroupEnd, "ncclGroupEnd");
+        MXK_SYM(GetErrorString, "ncclGetErrorString");
+#undef MXK_SYM
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.GroupStart &&
+                 api.GroupEnd && api.GetErrorString;
+    });
+    return api;
+}
+
+static int fail_nccl(const char* what, ncclResult_t r) {
+    return fail(MXK_ERR_COMM, std::string(what) + ": " + (nccl().GetErrorString ? nccl().GetErrorString(r) : "?"));
+}
+
+struct Comm {
+    ncclComm_t comm = nullptr;
+    int nranks = 1, rank = 0;
+};
+
+// ---------------------------------------------------------------------------
+// Workspace (stream-ordered allocations, released at the end of the call).
+
+namespace {
+
+struct Arena {
+    cudaStream_t stream;
+    std::vector<void*> ptrs;
+    explicit Arena(cudaStream_t s) : stream(s) {}
+    ~Arena() {
+        for (void* p : ptrs) cudaFreeAsync(p, stream);
+    }
+    template <typename T>
+    int alloc(T** out, int64_t count) {
+        void* p = nullptr;
+        const size_t bytes = sizeof(T) * (size_t)(count > 0 ? count : 1);
+        cudaError_t e = cudaMallocAsync(&p, bytes, stream);
+        if (e != cudaSuccess) return fail_cuda("cudaMallocAsync (kmeans workspace)", e);
+        ptrs.push_back(p);
+        *out = static_cast<T*>(p);
+        return MXK_OK;
+    }
+};
+
+constexpr int64_t kFp32ChunkBytes = 512ll << 20;  // dense product chunk of the FP32 iterations
+
+int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+              const mxk_options* options, int* iterations, cudaStream_t stream) {
+    MXK_REQUIRE(options && iterations, "kmeans_mixed: null options or iterations");
+    MXK_REQUIRE(k > 0 && d > 0 && n >= 0, "kmeans_mixed: require n >= 0, d > 0, k > 0");
+    MXK_REQUIRE(d % 128 == 0, "kmeans_mixed: d must be padded to a multiple of 128");
+    MXK_REQUIRE(points || n == 0, "kmeans_mixed: null points");
+    MXK_REQUIRE(centroids && (labels || n == 0), "kmeans_mixed: null centroids or labels");
+    MXK_REQUIRE(options->max_iterations > 0 && options->fp32_iterations >= 0 && options->tolerance >= 0.0f,
+                "Require maxiter > 0, fp32-iters >= 0, and tol >= 0");
+    clear_error();
+    *iterations = 0;
+    const int64_t kd = (int64_t)k * d;
+    Arena ws(stream);
+    float *pnorm = nullptr, *upper = nullptr, *gaps = nullptr, *cnorm = nullptr, *cerr = nullptr, *stats = nullptr,
+          *prev = nullptr, *sums = nullptr, *shift = nullptr;
+    int *precision = nullptr, *ids = nullptr, *gcount = nullptr, *cscratch = nullptr, *counts = nullptr;
+    uint8_t *qpoints = nullptr, *pscales = nullptr, *qcent = nullptr, *cscales = nullptr;
+    MXK_CHECK(ws.alloc(&pnorm, n));
+    MXK_CHECK(ws.alloc(&upper, ((n + 31) / 32) * 96));
+    MXK_CHECK(ws.alloc(&gaps, n));
+    MXK_CHECK(ws.alloc(&precision, n));
+    MXK_CHECK(ws.alloc(&ids, 3 * n));
+    MXK_CHECK(ws.alloc(&gcount, 4));
+    MXK_CHECK(ws.alloc(&cscratch, compaction_scratch_ints(n)));
+    MXK_CHECK(ws.alloc(&qpoints, n * d));
+    MXK_CHECK(ws.alloc(&pscales, n * (d / 32)));
+    MXK_CHECK(ws.alloc(&cnorm, k));
+    MXK_CHECK(ws.alloc(&cerr, k));
+    MXK_CHECK(ws.alloc(&stats, 2));
+    MXK_CHECK(ws.alloc(&qcent, kd));
+    MXK_CHECK(ws.alloc(&cscales, kd / 32));
+    MXK_CHECK(ws.alloc(&prev, kd));
+    MXK_CHECK(ws.alloc(&sums, kd));
+    MXK_CHECK(ws.alloc(&counts, k));
+    MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
+    float* dots = nullptr;
+    int64_t chunk_rows = 0;
+    if (options->fp32_iterations > 0 && n > 0) {
+        chunk_rows = std::max<int64_t>(128, kFp32ChunkBytes / (4 * (int64_t)k));
+        if (chunk_rows > n) chunk_rows = n;
+        MXK_CHECK(ws.alloc(&dots, chunk_rows * k));
+    }
+
+    // Once per run (kmeans.cu:24-27).
+    MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
+    MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
+    if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
+
+    const bool sharded = comm && comm->nranks > 1;
+    if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+    int result = options->max_iterations;
+    for (int it = 0; it < options->max_iterations; ++it) {
+        MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
+        MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
+        if (it < options->fp32_iterations) {
+            // kmeans.cu:31-34: FP32 product, assignment without pid (gap init -1).
+            for (int64_t r0 = 0; r0 < n; r0 += chunk_rows) {
+                const int64_t rows = std::min<int64_t>(chunk_rows, n - r0);
+                MXK_CHECK(launch_gemm_fp32(rows, k, d, points + r0 * d, centroids, dots, stream));
+                MXK_CHECK(launch_assign_clusters(rows, k, pnorm + r0, cnorm, dots, nullptr, labels + r0, gaps + r0,
+                                                 stream));
+            }
+            if (options->verbose && (!comm || comm->rank == 0))
+                std::fprintf(stderr, "iteration=%d precision=FP32\n", it + 1);
+        } else {
+            MXK_CUDA(cudaMemsetAsync(cerr, 0, sizeof(float) * k, stream));
+            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream));
+            MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
+            MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream));
+            MXK_CHECK(launch_group_compaction(n, precision, ids, gcount, cscratch, stream));
+            static const int group_bits[3] = {4, 6, 8};
+            for (int g = 0; g < 3; ++g) {
+                MXK_CHECK(launch_quantize(group_bits[g], n, d, points, ids + g * n, qpoints, pscales, nullptr,
+                                          gcount + g, stream));
+                MxArgmin am;
+                am.point_norms = pnorm;
+                am.centroid_norms = cnorm;
+                am.pid = ids + g * n;
+                am.labels = labels;
+                am.gaps = nullptr;
+                MXK_CHECK(launch_gemm_mx(group_bits[g], n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am,
+                                         gcount + g, stream));
+            }
+            if (options->verbose && (!comm || comm->rank == 0)) {
+                int h[3] = {0, 0, 0};
+                MXK_CUDA(cudaMemcpyAsync(h, gcount, sizeof(h), cudaMemcpyDeviceToHost, stream));
+                MXK_CUDA(cudaStreamSynchronize(stream));
+                std::fprintf(stderr, "iteration=%d fp4=%d fp6=%d fp8=%d\n", it + 1, h[0], h[1], h[2]);
+            }
+        }
+        // kmeans.cu:62-65
+        MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
+        MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
+        MXK_CHECK(launch_accumulate(n, d, k, points, labels, sums, counts, stream));
+        if (sharded) {
+            NcclApi& api = nccl();
+            ncclResult_t r = api.GroupStart();
+            if (r == ncclSuccess) r = api.AllReduce(sums, sums, (size_t)kd, ncclFloat32, ncclSum, comm->comm, stream);
+            if (r == ncclSuccess) r = api.AllReduce(counts, counts, (size_t)k, ncclInt32, ncclSum, comm->comm, stream);
+            ncclResult_t r2 = api.GroupEnd();
+            if (r != ncclSuccess) return fail_nccl("ncclAllReduce", r);
+            if (r2 != ncclSuccess) return fail_nccl("ncclGroupEnd", r2);
+        }
+        MXK_CHECK(launch_finalize(d, k, sums, counts, prev, centroids, shift, stream));
+        float host_shift = 0.0f;
+        MXK_CUDA(cudaMemcpyAsync(&host_shift, shift + shift_scratch_floats() - 1, sizeof(float), cudaMemcpyDeviceToHost,
+                                 stream));
+        MXK_CUDA(cudaStreamSynchronize(stream));
+        MXK_CHECK(check_device_error(stream));
+        if (!std::isfinite(host_shift))
+            return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");
+        if (host_shift <= options->tolerance) {
+            result = it + 1;
+            break;
+        }
+    }
+    *iterations = result;
+    return MXK_OK;
+}
+
+}  // namespace
+}  // namespace mxk
+
+extern "C" {
+
+int mxk_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                     const mxk_options* options, int* iterations, void* stream) {
+    return mxk::run_lloyd(nullptr, n, d, k, points, centroids, labels, options, iterations, mxk::as_stream(stream));
+}
+
+int mxk_comm_unique_id(unsigned char id[128]) {
+    mxk::NcclApi& api = mxk::nccl();
+    if (!api.ok) return mxk::fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+    ncclUniqueId uid;
+    ncclResult_t r = api.GetUniqueId(&uid);
+    if (r != ncclSuccess) return mxk::fail_nccl("ncclGetUniqueId", r);
+    static_assert(sizeof(uid.internal) == 128, "unexpected ncclUniqueId size");
+    std::memcpy(id, uid.internal, 128);
+    return MXK_OK;
+}
+
+int mxk_comm_init(void** comm, int nranks, int rank, const unsigned char id[128]) {
+    MXK_REQUIRE(comm && id && nranks >= 1 && rank >= 0 && rank < nranks, "comm_init: bad arguments");
+    mxk::NcclApi& api = mxk::nccl();
+    auto* c = new mxk::Comm();
+    c->nranks = nranks;
+    c->rank = rank;
+    if (nranks > 1) {
+        if (!api.ok) {
+            delete c;
+            return mxk::fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+        }
+        ncclUniqueId uid;
+        std::memcpy(uid.internal, id, 128);
+        ncclResult_t r = api.CommInitRank(&c->comm, nranks, uid, rank);
+        if (r != ncclSuccess) {
+            delete c;
+            return mxk::fail_nccl("ncclCommInitRank", r);
+        }
+    }
+    *comm = c;
+    return MXK_OK;
+}
+
+int mxk_comm_destroy(void* comm) {
+    auto* c = static_cast<mxk::Comm*>(comm);
+    if (!c) return MXK_OK;
+    int st = MXK_OK;
+    if (c->comm) {
+        ncclResult_t r = mxk::nccl().CommDestroy(c->comm);
+        if (r != ncclSuccess) st = mxk::fail_nccl("ncclCommDestroy", r);
+    }
+    delete c;
+    return st;
+}
+
+int mxk_kmeans_mixed_sharded(void* comm, int64_t n_local, int d, int k, const float* points, float* centroids,
+                             int* labels, const mxk_options* options, int* iterations, void* stream) {
+    MXK_REQUIRE(comm != nullptr, "kmeans_mixed_sharded: null communicator");
+    return mxk::run_lloyd(static_cast<mxk::Comm*>(comm), n_local, d, k, points, centroids, labels, options, iterations,
+                          mxk::as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// MX element and scale codecs used by the device kernels.
+//
+// Rules (the ones ParCIS/MX-KMeans gets from CUTLASS, include/kmeans.cuh:6-9,
+// and cuda_fp6.h, src/kernels/quantize.cu:89):
+//   * UE8M0 scale: the power of two at or above the value (round toward +inf),
+//     saturating to 2^127; hardware `cvt.rp.satfinite.ue8m0x2.f32`, the same
+//     instruction the reference's Scale(float) issues on Blackwell.
+//   * E4M3: round-to-nearest-even with saturation, `cvt.rn.satfinite.e4m3x2.f32`.
+//   * E2M3 / E2M1 / E3M2: round-to-nearest-even with saturation to the largest
+//     finite magnitude, computed in software below (the reference's CUTLASS
+//     sub-byte types also convert in software).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace mxk::dev {
+
+// UE8M0 byte for a non-negative value.
+__device__ __forceinline__ uint32_t ue8m0_encode(float v) {
+    uint16_t out;
+    asm("cvt.rp.satfinite.ue8m0x2.f32 %0, %1, %2;" : "=h"(out) : "f"(0.0f), "f"(v));
+    return out & 0xffu;
+}
+
+// 2^(e-127) as a float (e in 0..254); e == 255 is the NaN code.
+__device__ __forceinline__ float ue8m0_value(uint32_t e) {
+    if (e == 0) return __uint_as_float(0x00400000u);  // 2^-127 (subnormal)
+    if (e == 255) return __uint_as_float(0x7fc00000u);
+    return __uint_as_float(e << 23);
+}
+
+// Exact reciprocal of a UE8M0 scale: 2^(127-e).  Multiplying by it rounds
+// exactly like dividing by the scale (both are the correctly rounded x/2^(e-127)).
+__device__ __forceinline__ float ue8m0_reciprocal(uint32_t e) {
+    if (e == 255) return __uint_as_float(0x7fc00000u);
+    if (e == 254) return __uint_as_float(0x00400000u);  // 2^-127
+    return __uint_as_float((254u - e) << 23);
+}
+
+// Two E4M3 codes: low byte from `lo`, high byte from `hi`.
+__device__ __forceinline__ uint32_t e4m3x2_encode(float lo, float hi) {
+    uint16_t out;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(hi), "f"(lo));
+    return out;
+}
+
+// Value of one E4M3 code.
+__device__ __forceinline__ float e4m3_decode(uint32_t code) {
+    uint32_t h2;
+    uint16_t c = (uint16_t)(code & 0xffu);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
+}
+
+// Software round-to-nearest-even encoder for a small IEEE-like format with
+// MB mantissa bits, bias BIAS, sign at bit SIGN and largest magnitude MAXV.
+template <int MB, int BIAS, int SIGN>
+__device__ __forceinline__ uint32_t subbyte_encode(float x, float maxv, uint32_t maxcode, bool nan_signed) {
+    const uint32_t sign = __float_as_uint(x) >> 31;
+    const float a = fabsf(x);
+    if (isnan(x)) return (nan_signed ? sign << SIGN : 0u) | maxcode;
+    if (!(a <= 2.0f * maxv)) return (sign << SIGN) | maxcode;
+    constexpr int emin = 1 - BIAS;
+    int e = (int)((__float_as_uint(a) >> 23) & 0xffu) - 127;
+    if (e < emin) e = emin;
+    const float quantum = __uint_as_float((uint32_t)(e - MB + 127) << 23);
+    float r = rintf(a / quantum) * quantum;  // exact scaling; rintf ties to even
+    if (r > maxv) r = maxv;
+    if (r == 0.0f) return sign << SIGN;
+    const uint32_t rb = __float_as_uint(r);
+    const int re = (int)(rb >> 23) - 127;
+    uint32_t code;
+    if (re < emin) {
+        const float sub_quantum = __uint_as_float((uint32_t)(emin - MB + 127) << 23);
+        code = (uint32_t)(r / sub_quantum);
+    } else {
+        code = ((uint32_t)(re + BIAS) << MB) | ((rb >> (23 - MB)) & ((1u << MB) - 1u));
+    }
+    return (sign << SIGN) | code;
+}
+
+__device__ __forceinline__ uint32_t e2m3_encode(float x) { return subbyte_encode<3, 1, 5>(x, 7.5f, 0x1fu, true); }
+__device__ __forceinline__ uint32_t e2m1_encode(float x) { return subbyte_encode<1, 1, 3>(x, 6.0f, 0x7u, true); }
+__device__ __forceinline__ uint32_t e3m2_encode(float x) { return subbyte_encode<2, 3, 5>(x, 28.0f, 0x1fu, false); }
+
+template <int MB, int BIAS, int SIGN>
+__device__ __forceinline__ float subbyte_decode(uint32_t code) {
+    const uint32_t sign = (code >> SIGN) & 1u;
+    const uint32_t mag = code & ((1u << SIGN) - 1u);
+    const uint32_t e = mag >> MB, m = mag & ((1u << MB) - 1u);
+    float v;
+    if (e == 0)
+        v = (float)m * __uint_as_float((uint32_t)(1 - BIAS - MB + 127) << 23);
+    else
+        v = __uint_as_float(((e - BIAS + 127) << 23) | (m << (23 - MB)));
+    return sign ? -v : v;
+}
+
+__device__ __forceinline__ float e2m3_decode(uint32_t c) { return subbyte_decode<3, 1, 5>(c); }
+__device__ __forceinline__ float e2m1_decode(uint32_t c) { return subbyte_decode<1, 1, 3>(c); }
+__device__ __forceinline__ float e3m2_decode(uint32_t c) { return subbyte_decode<2, 3, 5>(c); }
+
+// Re-encode an E2M3 / E2M1 code as the E4M3 code of the same value (every
+// E2M3 and E2M1 value is exactly representable in E4M3).
+__device__ __forceinline__ uint32_t e2m3_to_e4m3(uint32_t c) {
+    const float v = e2m3_decode(c);
+    return e4m3x2_encode(v, 0.0f) & 0xffu;
+}
+__device__ __forceinline__ uint32_t e2m1_to_e4m3(uint32_t c) {
+    const float v = e2m1_decode(c);
+    return e4m3x2_encode(v, 0.0f) & 0xffu;
+}
+
+}  // namespace mxk::dev

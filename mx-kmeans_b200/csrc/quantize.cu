@@ -1,0 +1,452 @@
+// K1: MX quantization of point and centroid rows, plus the per-run point error
+// bounds, the precision policy and the per-precision compaction of point ids.
+//
+// Reference: ParCIS/MX-KMeans src/kernels/quantize.cu (quantize_kernel :13-72,
+// point_bounds_kernel :74-98, precision_kernel :100-108, launchers :111-134),
+// src/kernels/assignment.cu:7-16 (norms) and src/kmeans.cu:36-52 (centroid
+// statistics and group compaction).
+#include "common.cuh"
+#include "kernels.cuh"
+#include "mx_codec.cuh"
+#include "precision.hpp"
+
+namespace mxk {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float4 ldg4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
+// One thread owns 16 consecutive features of one output row: four 128-bit loads
+// in, one 128-bit (MXFP8), 96-bit (MXFP6) or 64-bit (MXFP4) store out.  The two
+// threads of a 32-feature block combine their maxima with one shuffle, derive the
+// UE8M0 scale exactly as the reference (Scale(amax/qmax) or 1 when amax == 0),
+// and multiply by the exact reciprocal of the scale.
+template <int BITS>
+__device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chunks, int d,
+                                               const float* __restrict__ points, const int* __restrict__ pid,
+                                               uint8_t* __restrict__ values, uint8_t* __restrict__ scales,
+                                               float* __restrict__ errors) {
+    const bool valid = g < total;
+    const int64_t row = valid ? g / chunks : 0;
+    const int chunk = valid ? (int)(g - row * chunks) : 0;
+    float x[16];
+    if (valid) {
+        const int64_t src = pid ? (int64_t)pid[row] : row;
+        const float* p = points + src * d + chunk * 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 v = ldg4(p + 4 * i);
+            x[4 * i] = v.x, x[4 * i + 1] = v.y, x[4 * i + 2] = v.z, x[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    constexpr float qmax = BITS == 8 ? 448.0f : (BITS == 6 ? 7.5f : 6.0f);
+    const uint32_t s = dev::ue8m0_encode(amax > 0.0f ? amax / qmax : 1.0f);
+    const float rcp = dev::ue8m0_reciprocal(s);
+    const float sval = dev::ue8m0_value(s);
+
+    uint32_t code[16];
+    if constexpr (BITS == 8) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+            const uint32_t two = dev::e4m3x2_encode(x[i] * rcp, x[i + 1] * rcp);
+            code[i] = two & 0xffu;
+            code[i + 1] = two >> 8;
+        }
+    } else if constexpr (BITS == 6) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) code[i] = dev::e2m3_encode(x[i] * rcp);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) code[i] = dev::e2m1_encode(x[i] * rcp);
+    }
+
+    float err = 0.0f;
+    if (errors) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float q;
+            if constexpr (BITS == 8)
+                q = dev::e4m3_decode(code[i]);
+            else if constexpr (BITS == 6)
+                q = dev::e2m3_decode(code[i]);
+            else
+                q = dev::e2m1_decode(code[i]);
+            const float diff = x[i] - q * sval;
+            err = fmaxf(err, diff * diff);
+        }
+        err = fmaxf(err, __shfl_xor_sync(kFull, err, 1));
+    }
+    if (!valid) return;
+
+    const int64_t elem = row * d + chunk * 16;
+    if constexpr (BITS == 8) {
+        uint4 w;
+        w.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
+        w.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
+        w.z = code[8] | (code[9] << 8) | (code[10] << 16) | (code[11] << 24);
+        w.w = code[12] | (code[13] << 8) | (code[14] << 16) | (code[15] << 24);
+        *reinterpret_cast<uint4*>(values + elem) = w;
+    } else if constexpr (BITS == 6) {
+        // Four 6-bit codes in three bytes, least significant bit first
+        // (quantize.cu:53-62): a 24-bit group c0 | c1<<6 | c2<<12 | c3<<18.
+        uint32_t g24[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            g24[j] = (code[4 * j] & 63u) | ((code[4 * j + 1] & 63u) << 6) | ((code[4 * j + 2] & 63u) << 12) |
+                     ((code[4 * j + 3] & 63u) << 18);
+        uint32_t* out = reinterpret_cast<uint32_t*>(values + (elem / 4) * 3);
+        out[0] = g24[0] | (g24[1] << 24);
+        out[1] = (g24[1] >> 8) | (g24[2] << 16);
+        out[2] = (g24[2] >> 16) | (g24[3] << 8);
+    } else {
+        // Low nibble = even feature (quantize.cu:48-51).
+        uint2 w;
+        w.x = (code[0] & 15u) | ((code[1] & 15u) << 4) | ((code[2] & 15u) << 8) | ((code[3] & 15u) << 12) |
+              ((code[4] & 15u) << 16) | ((code[5] & 15u) << 20) | ((code[6] & 15u) << 24) | ((code[7] & 15u) << 28);
+        w.y = (code[8] & 15u) | ((code[9] & 15u) << 4) | ((code[10] & 15u) << 8) | ((code[11] & 15u) << 12) |
+              ((code[12] & 15u) << 16) | ((code[13] & 15u) << 20) | ((code[14] & 15u) << 24) |
+              ((code[15] & 15u) << 28);
+        *reinterpret_cast<uint2*>(values + elem / 2) = w;
+    }
+    if ((chunk & 1) == 0) {
+        scales[row * (d >> 5) + (chunk >> 1)] = (uint8_t)s;
+        // Squared errors are non-negative, so integer order equals float order.
+        if (errors) atomicMax(reinterpret_cast<unsigned*>(errors + row), __float_as_uint(err));
+    }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256) quantize_kernel(int64_t rows, int d, const float* __restrict__ points,
+                                                       const int* __restrict__ pid, uint8_t* __restrict__ values,
+                                                       uint8_t* __restrict__ scales, float* __restrict__ errors,
+                                                       const int* __restrict__ rows_dev) {
+    const int64_t nrows = rows_dev ? (int64_t)*rows_dev : rows;
+    const int chunks = d >> 4;
+    const int64_t total = nrows * chunks;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;  // multiple of 32: block pairs stay in one warp
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
+        quantize_chunk<BITS>(base + threadIdx.x, total, chunks, d, points, pid, values, scales, errors);
+    }
+}
+
+// Sequential FMA sum of squares per row (assignment.cu:7-16: nvcc contracts
+// `sum += x * x`), staged through shared memory so global loads coalesce.
+__global__ void __launch_bounds__(256) l2_norm_kernel(int64_t rows, int d, const float* __restrict__ x,
+                                                      float* __restrict__ norms) {
+    __shared__ float tile[8][32][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * 32;
+    if (row0 >= rows) return;
+    float sum = 0.0f;
+    for (int f0 = 0; f0 < d; f0 += 32) {
+        const int f = f0 + lane;
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            const int64_t row = row0 + r;
+            tile[warp][r][lane] = (row < rows && f < d) ? x[row * d + f] : 0.0f;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum = fmaf(tile[warp][lane][j], tile[warp][lane][j], sum);
+        __syncwarp();
+    }
+    if (row0 + lane < rows) norms[row0 + lane] = sum;
+}
+
+// One warp per point; lane = feature within a 32-block.  FP4 (E2M1) and FP6
+// (E3M2, as the reference) reconstruction errors over features 1..31 of each
+// block (quantize.cu:74-98).
+__global__ void __launch_bounds__(256) point_bounds_kernel(int64_t n, int d, const float* __restrict__ points,
+                                                           const float* __restrict__ norms, float* __restrict__ upper) {
+    const int lane = threadIdx.x & 31;
+    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (p >= n) return;
+    float e4 = 0.0f, e6 = 0.0f;
+    for (int base = 0; base < d; base += 32) {
+        const float v = points[p * d + base + lane];
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+        const uint32_t s4 = dev::ue8m0_encode(amax > 0.0f ? amax / 6.0f : 1.0f);
+        const uint32_t s6 = dev::ue8m0_encode(amax > 0.0f ? amax / 7.5f : 1.0f);
+        if (lane >= 1) {
+            const float q4 = dev::e2m1_decode(dev::e2m1_encode(v * dev::ue8m0_reciprocal(s4)));
+            const float q6 = dev::e3m2_decode(dev::e3m2_encode(v * dev::ue8m0_reciprocal(s6)));
+            e4 = fmaxf(e4, fabsf(fmaf(q4, dev::ue8m0_value(s4), -v)));
+            e6 = fmaxf(e6, fabsf(fmaf(q6, dev::ue8m0_value(s6), -v)));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        e4 = fmaxf(e4, __shfl_xor_sync(kFull, e4, o));
+        e6 = fmaxf(e6, __shfl_xor_sync(kFull, e6, o));
+    }
+    if (lane == 0) {
+        const size_t tile = (size_t)(p / 32) * 96;
+        const int slot = (int)(p % 32);
+        const float nrm = norms[p];
+        upper[tile + slot] = nrm;
+        upper[tile + 32 + slot] = fmaf((float)d * e6, e6, nrm);
+        upper[tile + 64 + slot] = fmaf((float)d * e4, e4, nrm);
+    }
+}
+
+__global__ void __launch_bounds__(256) precision_kernel(int64_t n, int d, const float* __restrict__ upper,
+                                                        const float* __restrict__ gaps, float lc, float ec,
+                                                        const float* __restrict__ lc_ec_dev, int* __restrict__ precision,
+                                                        int* __restrict__ group_counts) {
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (lc_ec_dev) {
+        ec = lc_ec_dev[0];
+        lc = lc_ec_dev[1];
+    }
+    int prec = 0;
+    if (p < n) {
+        const size_t tile = (size_t)(p / 32) * 96;
+        const int slot = (int)(p % 32);
+        prec = select_precision(upper[tile + 64 + slot], upper[tile + 32 + slot], lc, ec, d, gaps[p]);
+        precision[p] = prec;
+    }
+    if (group_counts) {
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+            const unsigned m = __ballot_sync(kFull, p < n && prec == 4 + 2 * g);
+            if (m && lane == __ffs(m) - 1) atomicAdd(group_counts + g, __popc(m));
+        }
+    }
+}
+
+__global__ void centroid_stats_kernel(int k, const float* __restrict__ errors, const float* __restrict__ norms,
+                                      float* __restrict__ stats) {
+    __shared__ float se[32], sn[32];
+    float me = 0.0f, mn = 0.0f;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        me = fmaxf(me, errors[i]);
+        mn = fmaxf(mn, norms[i]);
+    }
+    for (int o = 16; o; o >>= 1) {
+        me = fmaxf(me, __shfl_xor_sync(kFull, me, o));
+        mn = fmaxf(mn, __shfl_xor_sync(kFull, mn, o));
+    }
+    if ((threadIdx.x & 31) == 0) se[threadIdx.x >> 5] = me, sn[threadIdx.x >> 5] = mn;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) me = fmaxf(me, se[w]), mn = fmaxf(mn, sn[w]);
+        stats[0] = sqrtf(me);
+        stats[1] = sqrtf(mn);
+    }
+}
+
+// ---- stable three-way compaction (thrust::copy_if per group, kmeans.cu:46-50)
+constexpr int kCompactBlock = 1024;  // elements per block (256 threads x 4)
+
+__global__ void __launch_bounds__(256) group_block_count_kernel(int64_t n, const int* __restrict__ precision,
+                                                                int* __restrict__ block_counts, int nblocks) {
+    __shared__ int cnt[3];
+    if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    int local[3] = {0, 0, 0};
+    const int64_t base = (int64_t)blockIdx.x * kCompactBlock;
+    for (int i = threadIdx.x; i < kCompactBlock; i += blockDim.x) {
+        const int64_t p = base + i;
+        if (p < n) {
+            const int v = precision[p];
+            local[0] += v == 4, local[1] += v == 6, local[2] += v == 8;
+        }
+    }
+    for (int g = 0; g < 3; ++g) {
+        int v = local[g];
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+        if ((threadIdx.x & 31) == 0 && v) atomicAdd(&cnt[g], v);
+    }
+    __syncthreads();
+    if (threadIdx.x < 3) block_counts[threadIdx.x * nblocks + blockIdx.x] = cnt[threadIdx.x];
+}
+
+// Exclusive scan of per-block counts for each group (one block, three warps).
+__global__ void group_scan_kernel(int* __restrict__ block_counts, int nblocks, int* __restrict__ group_counts) {
+    const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (g >= 3) return;
+    int* c = block_counts + (size_t)g * nblocks;
+    int carry = 0;
+    for (int b0 = 0; b0 < nblocks; b0 += 32) {
+        const int b = b0 + lane;
+        const int v = b < nblocks ? c[b] : 0;
+        int incl = v;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (b < nblocks) c[b] = carry + incl - v;
+        carry += __shfl_sync(kFull, incl, 31);
+    }
+    if (lane == 0) group_counts[g] = carry;
+}
+
+__global__ void __launch_bounds__(256) group_scatter_kernel(int64_t n, const int* __restrict__ precision,
+                                                            const int* __restrict__ block_offsets, int nblocks,
+                                                            int* __restrict__ ids) {
+    __shared__ int warp_tot[3][8];
+    __shared__ int running[3];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 3) running[threadIdx.x] = block_offsets[threadIdx.x * nblocks + blockIdx.x];
+    __syncthreads();
+    const int64_t base = (int64_t)blockIdx.x * kCompactBlock;
+    for (int i0 = 0; i0 < kCompactBlock; i0 += 256) {
+        const int64_t p = base + i0 + threadIdx.x;
+        const int v = p < n ? precision[p] : 0;
+        unsigned m[3];
+        for (int g = 0; g < 3; ++g) {
+            m[g] = __ballot_sync(kFull, v == 4 + 2 * g);
+            if (lane == 0) warp_tot[g][warp] = __popc(m[g]);
+        }
+        __syncthreads();
+        for (int g = 0; g < 3; ++g) {
+            if (v == 4 + 2 * g) {
+                int off = running[g];
+                for (int w = 0; w < warp; ++w) off += warp_tot[g][w];
+                off += __popc(m[g] & ((1u << lane) - 1u));
+                ids[(int64_t)g * n + off] = (int)p;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < 3) {
+            int t = 0;
+            for (int w = 0; w < 8; ++w) t += warp_tot[threadIdx.x][w];
+            running[threadIdx.x] += t;
+        }
+        __syncthreads();
+    }
+}
+
+bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+}  // namespace
+
+int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
+                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream) {
+    if (bits != 4 && bits != 6 && bits != 8) return fail(MXK_ERR_INVALID, "Precision must be 4, 6, or 8");
+    if (rows <= 0) return MXK_OK;
+    MXK_REQUIRE(d > 0 && d % 32 == 0, "quantize_rows: d must be a positive multiple of 32");
+    MXK_REQUIRE(points && values && scales, "quantize_rows: null pointer");
+    MXK_REQUIRE(aligned(points, 16), "quantize_rows: points must be 16-byte aligned");
+    MXK_REQUIRE(aligned(values, bits == 8 ? 16 : (bits == 4 ? 8 : 4)),
+                "quantize_rows: values must be aligned to the packed store width");
+    const int64_t threads = rows * (d / 16);
+    int64_t blocks = (threads + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 16;  // grid-stride beyond 16 CTAs per SM
+    if (blocks > cap) blocks = cap;
+    auto* out = static_cast<uint8_t*>(values);
+    LaunchScope scope("quantize_mx", stream);
+    switch (bits) {
+        case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
+        case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
+        default: quantize_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
+    }
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream) {
+    if (rows <= 0) return MXK_OK;
+    MXK_REQUIRE(d > 0 && x && norms, "compute_l2_norm: bad arguments");
+    const int64_t blocks = (rows + 255) / 256;
+    LaunchScope scope("l2_norm", stream);
+    l2_norm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, d, x, norms);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
+                        cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    MXK_REQUIRE(d > 0 && d % 32 == 0, "precompute_point_bounds: d must be a multiple of 32");
+    const int64_t blocks = (n * 32 + 255) / 256;
+    LaunchScope scope("point_bounds", stream);
+    point_bounds_kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, points, norms, upper);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc, float ec,
+                             const float* lc_ec_dev, int* precision, int* group_counts, cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    const int64_t blocks = (n + 255) / 256;
+    LaunchScope scope("assign_precisions", stream);
+    precision_kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, upper, gaps, lc, ec, lc_ec_dev, precision,
+                                                          group_counts);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_centroid_stats(int k, const float* errors, const float* norms, float* stats, cudaStream_t stream) {
+    LaunchScope scope("centroid_stats", stream);
+    centroid_stats_kernel<<<1, 1024, 0, stream>>>(k, errors, norms, stats);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int64_t compaction_scratch_ints(int64_t n) { return 3 * ((n + kCompactBlock - 1) / kCompactBlock) + 3; }
+
+int launch_group_compaction(int64_t n, const int* precision, int* ids, int* group_counts, int* scratch,
+                            cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    const int64_t nb = (n + kCompactBlock - 1) / kCompactBlock;
+    MXK_REQUIRE(nb < (1ll << 31), "compaction: too many points");
+    {
+        LaunchScope scope("group_count", stream);
+        group_block_count_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, scratch, (int)nb);
+        MXK_CUDA(cudaGetLastError());
+    }
+    {
+        LaunchScope scope("group_scan", stream);
+        group_scan_kernel<<<1, 96, 0, stream>>>(scratch, (int)nb, group_counts);
+        MXK_CUDA(cudaGetLastError());
+    }
+    {
+        LaunchScope scope("group_scatter", stream);
+        group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, scratch, (int)nb, ids);
+        MXK_CUDA(cudaGetLastError());
+    }
+    return MXK_OK;
+}
+
+}  // namespace mxk
+
+extern "C" {
+
+int mxk_compute_l2_norm(int64_t rows, int d, const float* points, float* norms, void* stream) {
+    return mxk::launch_l2_norm(rows, d, points, norms, mxk::as_stream(stream));
+}
+
+int mxk_quantize_rows(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
+                      uint8_t* scales, float* max_errors, void* stream) {
+    return mxk::launch_quantize(bits, rows, d, points, pid, values, scales, max_errors, nullptr,
+                                mxk::as_stream(stream));
+}
+
+int mxk_precompute_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
+                                void* stream) {
+    return mxk::launch_point_bounds(n, d, points, norms, upper, mxk::as_stream(stream));
+}
+
+int mxk_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc, float ec,
+                          int* precision, void* stream) {
+    return mxk::launch_assign_precisions(n, d, upper, gaps, lc, ec, nullptr, precision, nullptr,
+                                         mxk::as_stream(stream));
+}
+
+}  // extern "C"

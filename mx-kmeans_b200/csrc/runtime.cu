@@ -1,0 +1,194 @@
+// Host runtime of libmxkmeans: error reporting, launch accounting and kernel
+// timing, the per-device error word, and tensor-map encoding.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace mxk {
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_profiling{0};
+
+struct PendingTiming {
+    int device;
+    const char* name;
+    cudaEvent_t start, stop;
+};
+
+struct KernelStat {
+    int device;
+    std::string name;
+    uint64_t launches = 0;
+    double total_ms = 0.0;
+};
+
+std::mutex g_mutex;
+std::vector<PendingTiming> g_pending;
+std::vector<KernelStat> g_stats;
+unsigned* g_error_words[64] = {};
+
+void drain_pending_locked() {
+    for (auto& p : g_pending) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(p.stop) == cudaSuccess && cudaEventElapsedTime(&ms, p.start, p.stop) == cudaSuccess) {
+            KernelStat* st = nullptr;
+            for (auto& s : g_stats)
+                if (s.device == p.device && s.name == p.name) st = &s;
+            if (!st) {
+                g_stats.push_back(KernelStat{p.device, p.name});
+                st = &g_stats.back();
+            }
+            st->launches += 1;
+            st->total_ms += ms;
+        }
+        cudaEventDestroy(p.start);
+        cudaEventDestroy(p.stop);
+    }
+    g_pending.clear();
+}
+}  // namespace
+
+int fail(int status, const std::string& message) {
+    g_last_error = message;
+    return status;
+}
+
+int fail_cuda(const char* what, cudaError_t err) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(err);
+    return MXK_ERR_CUDA;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+LaunchScope::LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (g_profiling.load(std::memory_order_relaxed)) {
+        if (cudaEventCreate(&start) == cudaSuccess && cudaEventCreate(&stop) == cudaSuccess)
+            cudaEventRecord(start, stream);
+        else
+            start = stop = nullptr;
+    }
+}
+
+LaunchScope::~LaunchScope() {
+    if (start && stop) {
+        cudaEventRecord(stop, stream);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_pending.push_back(PendingTiming{dev, name, start, stop});
+    }
+}
+
+unsigned* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!g_error_words[dev]) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        g_error_words[dev] = static_cast<unsigned*>(p);
+    }
+    return g_error_words[dev];
+}
+
+int check_device_error(cudaStream_t stream) {
+    unsigned* w = device_error_word();
+    if (!w) return fail(MXK_ERR_CUDA, "cannot allocate the device error word");
+    unsigned host = 0;
+    MXK_CUDA(cudaMemcpyAsync(&host, w, sizeof(unsigned), cudaMemcpyDeviceToHost, stream));
+    MXK_CUDA(cudaStreamSynchronize(stream));
+    if (host) {
+        MXK_CUDA(cudaMemsetAsync(w, 0, sizeof(unsigned), stream));
+        if (host & (1u << MXK_ERR_TIMEOUT))
+            return fail(MXK_ERR_TIMEOUT, "a device-side wait timed out; the kernel unwound without finishing");
+        if (host & (1u << MXK_ERR_NONFINITE))
+            return fail(MXK_ERR_NONFINITE,
+                        "Non-finite distances: a label outside [0, k) (every distance +inf or NaN); check the input scale");
+        return fail(MXK_ERR_CUDA, "device error word set: " + std::to_string(host));
+    }
+    return MXK_OK;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                         uint32_t box_inner, uint32_t box_outer, CUtensorMapDataType dtype,
+                         CUtensorMapSwizzle swizzle) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            return fail(MXK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16)
+        return fail(MXK_ERR_UNSUPPORTED, "TMA operand base and row pitch must be 16-byte aligned");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MXK_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    return MXK_OK;
+}
+
+}  // namespace mxk
+
+extern "C" {
+
+const char* mxk_last_error(void) { return mxk::g_last_error.c_str(); }
+
+int mxk_version(void) { return 100; }
+
+uint64_t mxk_launch_count(void) { return mxk::g_launches.load(); }
+
+int mxk_profile_enable(int on) {
+    std::lock_guard<std::mutex> lock(mxk::g_mutex);
+    mxk::drain_pending_locked();
+    if (on) mxk::g_stats.clear();
+    mxk::g_profiling.store(on ? 1 : 0);
+    return MXK_OK;
+}
+
+int mxk_profile_read(mxk_kernel_stat* out, int max, int* count) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mxk::g_mutex);
+    mxk::drain_pending_locked();
+    int n = 0;
+    for (auto& s : mxk::g_stats) {
+        if (s.device != dev) continue;
+        if (out && n < max) {
+            std::memset(&out[n], 0, sizeof(mxk_kernel_stat));
+            std::strncpy(out[n].name, s.name.c_str(), sizeof(out[n].name) - 1);
+            out[n].launches = s.launches;
+            out[n].total_ms = s.total_ms;
+        }
+        ++n;
+    }
+    if (count) *count = n;
+    return MXK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,332 @@
+// K3: FP32 centroid update and convergence shift.
+//
+// Reference: ParCIS/MX-KMeans src/kernels/update.cu:7-61 -- per-cluster sums and
+// counts by one global atomicAdd per (point, feature), divide, keep the previous
+// center of an empty cluster, then sum((prev - cur)^2) by one atomicAdd per
+// element into a single float.
+//
+// Here: (a) when the K x D sums fit in shared memory, every CTA accumulates a
+// private copy with shared-memory atomics and flushes it once with vector
+// reductions; (b) otherwise each warp walks a contiguous run of points with
+// 128-bit loads, keeps a register sum while consecutive points share a label
+// and flushes it with one red.global.add.v4.f32 per 4 features on label change.
+// Counts are aggregated the same way.  The finalize kernel divides, applies the
+// empty-cluster rule and reduces the shift in a fixed order (bit-reproducible).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mxk {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float4 ldg_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// (b) global path.  Lane owns features 4*lane + 128*j, j < d/128 (d % 128 == 0).
+// A label outside [0, k) -- the argmin's INT_MAX when every distance of a
+// point is +inf or NaN -- is never used as an index: the point is skipped and
+// the error word records MXK_ERR_NONFINITE for the host to report.
+__device__ __forceinline__ bool bad_label(int lab, int k, unsigned* err) {
+    if ((unsigned)lab < (unsigned)k) return false;
+    if (err) atomicOr(err, 1u << MXK_ERR_NONFINITE);
+    return true;
+}
+
+template <int NJ>
+__global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, int k, const float* __restrict__ points,
+                                                              const int* __restrict__ labels, float* __restrict__ sums,
+                                                              int* __restrict__ counts, int64_t per_warp,
+                                                              unsigned* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t begin = warp * per_warp;
+    if (begin >= n) return;
+    const int64_t end = begin + per_warp < n ? begin + per_warp : n;
+    float4 acc[NJ];
+    int cur = -1;  // no open run
+    int run = 0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t pnt = begin; pnt < end; ++pnt) {
+        const int lab = labels[pnt];
+        if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
+        if (lab != cur) {
+            if (cur >= 0) {
+                float* dst = sums + (int64_t)cur * d + 4 * lane;
+#pragma unroll
+                for (int j = 0; j < NJ; ++j)
+                    red_add_v4(dst + 128 * j, acc[j]), acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (lane == 0) atomicAdd(counts + cur, run);
+            }
+            cur = lab;
+            run = 0;
+        }
+        const float* src = points + pnt * d + 4 * lane;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const float4 x = ldg_stream4(src + 128 * j);
+            acc[j].x += x.x, acc[j].y += x.y, acc[j].z += x.z, acc[j].w += x.w;
+        }
+        ++run;
+    }
+    if (cur < 0) return;
+    float* dst = sums + (int64_t)cur * d + 4 * lane;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) red_add_v4(dst + 128 * j, acc[j]);
+    if (lane == 0) atomicAdd(counts + cur, run);
+}
+
+// (a) privatized path: the CTA's copy of all K x D sums and K counts lives in
+// shared memory; one warp per point, float4 per lane.
+__global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int d, int k,
+                                                                 const float* __restrict__ points,
+                                                                 const int* __restrict__ labels, float* __restrict__ sums,
+                                                                 int* __restrict__ counts, unsigned* __restrict__ err) {
+    extern __shared__ float priv[];  // k*d sums, then k counts
+    int* pcount = reinterpret_cast<int*>(priv + (int64_t)k * d);
+    const int kd = k * d;
+    for (int i = threadIdx.x; i < kd + k; i += blockDim.x) priv[i] = 0.0f;  // int 0 has the same bits
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int vec_per_row = d >> 2;
+    for (int64_t pnt = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); pnt < n; pnt += (int64_t)gridDim.x * warps) {
+        const int lab = labels[pnt];
+        if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
+        const float* src = points + pnt * d;
+        float* dst = priv + (int64_t)lab * d;
+        for (int v = lane; v < vec_per_row; v += 32) {
+            const float4 x = ldg_stream4(src + 4 * v);
+            atomicAdd(dst + 4 * v, x.x);
+            atomicAdd(dst + 4 * v + 1, x.y);
+            atomicAdd(dst + 4 * v + 2, x.z);
+            atomicAdd(dst + 4 * v + 3, x.w);
+        }
+        if (lane == 0) atomicAdd(pcount + lab, 1);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < (kd >> 2); i += blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(priv)[i];
+        if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f) red_add_v4(sums + 4 * i, v);
+    }
+    for (int i = threadIdx.x; i < k; i += blockDim.x)
+        if (pcount[i]) atomicAdd(counts + i, pcount[i]);
+}
+
+// Generic fallback for d % 128 != 0 (API use with unpadded d).
+__global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* __restrict__ points,
+                                         const int* __restrict__ labels, float* __restrict__ sums,
+                                         int* __restrict__ counts, unsigned* __restrict__ err) {
+    const int64_t total = n * d;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / d;
+        const int f = (int)(i - row * d);
+        const int lab = labels[row];
+        if (bad_label(lab, k, f == 0 ? err : nullptr)) continue;
+        if (f == 0) atomicAdd(counts + lab, 1);
+        atomicAdd(sums + (int64_t)lab * d + f, points[i]);
+    }
+}
+
+// Divides, applies the empty-cluster rule, and writes this CTA's partial shift
+// (sum of (old - new)^2 over its grid-stride elements, reduced in a fixed order)
+// to partials[blockIdx.x].  The grid size is fixed by the shape, so the shift is
+// bit-identical on every GPU that runs it -- all ranks of a sharded run stop on
+// the same iteration without exchanging it.
+__global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float* __restrict__ sums,
+                                                       const int* __restrict__ counts, const float* __restrict__ old,
+                                                       float* __restrict__ centroids, float* __restrict__ partials) {
+    __shared__ float warp_sum[8];
+    const int64_t total = (int64_t)k * d;
+    float local = 0.0f;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int cnt = counts[i / d];
+        // An empty cluster keeps its previous center (update.cu:26-29).
+        const float v = cnt ? sums[i] / (float)cnt : old[i];
+        const float diff = old[i] - v;
+        centroids[i] = v;
+        local += diff * diff;
+    }
+    if (!partials) return;
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(kFull, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
+        partials[blockIdx.x] = s;
+    }
+}
+
+// Sums the per-CTA partials in a fixed order into out[0].
+__global__ void sum_partials_kernel(const float* __restrict__ partials, int count, float* __restrict__ out) {
+    __shared__ float warp_sum[32];
+    float local = 0.0f;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) local += partials[i];
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(kFull, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
+        out[0] = s;
+    }
+}
+
+__global__ void __launch_bounds__(256) shift_kernel(int64_t elements, const float* __restrict__ prev,
+                                                    const float* __restrict__ cur, float* __restrict__ partials) {
+    __shared__ float warp_sum[8];
+    float local = 0.0f;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < elements; i += (int64_t)gridDim.x * blockDim.x) {
+        const float diff = prev[i] - cur[i];
+        local += diff * diff;
+    }
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(kFull, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
+        partials[blockIdx.x] = s;
+    }
+}
+
+constexpr int kShiftBlocks = 256;  // fixed grid of the shift reduction (<= partial slots)
+
+}  // namespace
+
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, float* sums, int* counts,
+                      cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    MXK_REQUIRE(d > 0 && k > 0 && points && labels && sums && counts, "update_centroids: bad arguments");
+    const int sms = sm_count();
+    unsigned* err = device_error_word();
+    if (!err) return fail(MXK_ERR_CUDA, "update_centroids: cannot allocate the device error word");
+    const bool aligned = (reinterpret_cast<uintptr_t>(points) % 16 == 0) && (reinterpret_cast<uintptr_t>(sums) % 16 == 0);
+    const int64_t priv_bytes = ((int64_t)k * d + k) * 4;
+    int max_smem = 0, dev = 0;
+    MXK_CUDA(cudaGetDevice(&dev));
+    MXK_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (aligned && d % 4 == 0 && priv_bytes <= max_smem && priv_bytes <= 200 * 1024 && n >= (int64_t)k * 64) {
+        MXK_CUDA(cudaFuncSetAttribute(accumulate_private_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)priv_bytes));
+        LaunchScope scope("accumulate_private", stream);
+        accumulate_private_kernel<<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, sums, counts, err);
+        MXK_CUDA(cudaGetLastError());
+        return MXK_OK;
+    }
+    if (aligned && d % 128 == 0 && d <= 1024) {
+        const int64_t warps_total = (int64_t)sms * 64;  // 8 CTAs of 256 threads per SM
+        int64_t per_warp = (n + warps_total - 1) / warps_total;
+        if (per_warp < 16) per_warp = 16;
+        const int64_t warps = (n + per_warp - 1) / per_warp;
+        const int64_t blocks = (warps * 32 + 255) / 256;
+        LaunchScope scope("accumulate_runs", stream);
+        switch (d / 128) {
+#define MXK_ACC_CASE(J) \
+    case J: accumulate_runs_kernel<J><<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, per_warp, err); break;
+            MXK_ACC_CASE(1) MXK_ACC_CASE(2) MXK_ACC_CASE(3) MXK_ACC_CASE(4) MXK_ACC_CASE(5) MXK_ACC_CASE(6)
+            MXK_ACC_CASE(7) MXK_ACC_CASE(8)
+#undef MXK_ACC_CASE
+        }
+        MXK_CUDA(cudaGetLastError());
+        return MXK_OK;
+    }
+    LaunchScope scope("accumulate_scalar", stream);
+    accumulate_scalar_kernel<<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int64_t shift_scratch_floats() { return kShiftBlocks + 1; }
+
+int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream) {
+    const int64_t total = (int64_t)k * d;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > kShiftBlocks) blocks = kShiftBlocks;
+    {
+        LaunchScope scope("finalize", stream);
+        finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(d, k, sums, counts, old_centroids, centroids,
+                                                              shift_scratch);
+        MXK_CUDA(cudaGetLastError());
+    }
+    if (shift_scratch) {
+        LaunchScope scope("shift_total", stream);
+        sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks);
+        MXK_CUDA(cudaGetLastError());
+    }
+    return MXK_OK;
+}
+
+int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,
+                 cudaStream_t stream) {
+    int64_t blocks = (elements + 255) / 256;
+    if (blocks > kShiftBlocks) blocks = kShiftBlocks;
+    if (blocks < 1) blocks = 1;
+    {
+        LaunchScope scope("shift", stream);
+        shift_kernel<<<(unsigned)blocks, 256, 0, stream>>>(elements, previous, current, shift_scratch);
+        MXK_CUDA(cudaGetLastError());
+    }
+    LaunchScope scope("shift_total", stream);
+    sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+}  // namespace mxk
+
+extern "C" {
+
+int mxk_update_centroids(int64_t n, int d, int k, const float* points, const int* labels, const float* old_centroids,
+                         float* centroids, int* counts, void* stream) {
+    cudaStream_t s = mxk::as_stream(stream);
+    MXK_REQUIRE(d > 0 && k > 0, "update_centroids: bad arguments");
+    MXK_REQUIRE(centroids != old_centroids, "update_centroids: centroids and old_centroids must differ");
+    MXK_CUDA(cudaMemsetAsync(centroids, 0, sizeof(float) * (size_t)k * d, s));
+    MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * (size_t)k, s));
+    MXK_CHECK(mxk::launch_accumulate(n, d, k, points, labels, centroids, counts, s));
+    MXK_CHECK(mxk::launch_finalize(d, k, centroids, counts, old_centroids, centroids, nullptr, s));
+    // Reports labels outside [0, k) (skipped above) instead of writing past the
+    // sums as an unchecked index would.
+    return mxk::check_device_error(s);
+}
+
+int mxk_centroid_shift(int64_t elements, const float* previous, const float* current, float* device_sum,
+                       float* host_result, void* stream) {
+    cudaStream_t s = mxk::as_stream(stream);
+    MXK_REQUIRE(device_sum != nullptr, "centroid_shift: null device_sum");
+    float h = 0.0f;
+    if (elements > 0) {
+        float* scratch = nullptr;
+        MXK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), sizeof(float) * mxk::shift_scratch_floats(), s));
+        int st = mxk::launch_shift(elements, previous, current, scratch, s);
+        if (st == MXK_OK) {
+            cudaError_t e = cudaMemcpyAsync(device_sum, scratch + mxk::shift_scratch_floats() - 1, sizeof(float),
+                                            cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) st = mxk::fail_cuda("cudaMemcpyAsync", e);
+        }
+        cudaFreeAsync(scratch, s);
+        if (st != MXK_OK) return st;
+    } else {
+        MXK_CUDA(cudaMemsetAsync(device_sum, 0, sizeof(float), s));
+    }
+    MXK_CUDA(cudaMemcpyAsync(&h, device_sum, sizeof(float), cudaMemcpyDeviceToHost, s));
+    MXK_CUDA(cudaStreamSynchronize(s));
+    if (host_result) *host_result = h;
+    return MXK_OK;
+}
+
+}  // extern "C"

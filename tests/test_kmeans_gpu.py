@@ -1,0 +1,96 @@
+"""Lloyd driver parity (kmeans_mixed, src/kmeans.cu:12-68) on the GPU against
+the oracle and the reference's clustering checks (tests/cuda_checks.cu:142-168).
+
+Tolerances (north star): labels identical except where a point's top-2 distance
+gap is below 1e-5 of the distance scale; centroids and inertia within 1e-4
+relative."""
+import numpy as np
+import pytest
+
+from conftest import blobs
+
+pytestmark = pytest.mark.gpu
+
+
+def _to(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda:0")
+
+
+def _run(torch, mxk, x, c0, **opts):
+    xt, ct = _to(torch, x), _to(torch, c0)
+    lab = torch.full((x.shape[0],), -1, dtype=torch.int32, device="cuda:0")
+    it = mxk.kmeans_mixed(xt, ct, lab, mxk.Options(**opts))
+    return it, ct.cpu().numpy(), lab.cpu().numpy()
+
+
+def test_reference_clustering_checks(torch_cuda, mxk):
+    torch = torch_cuda
+    n, d, k = 35, 128, 4
+    x = np.zeros((n, d), np.float32)
+    x[:, 0] = (np.arange(n) % k) * 10
+    c = np.zeros((k, d), np.float32)
+    c[:, 0] = np.arange(k) * 10 + 1.0
+    it, _, lab = _run(torch, mxk, x, c, max_iterations=3, tolerance=0.0)
+    assert 2 <= it <= 3
+    assert np.array_equal(lab, np.arange(n) % k)
+    it, _, _ = _run(torch, mxk, x, c, max_iterations=1, tolerance=0.0)
+    assert it == 1
+
+
+def test_one_iteration_vs_oracle(torch_cuda, mxk, orc):
+    torch = torch_cuda
+    n, d, k = 30000, 128, 64
+    x = blobs(n, 96, 40, seed=3, spread=5.0, sigma=0.75)
+    c0 = x[np.random.default_rng(1).choice(n, k, replace=False)].copy()
+    it, cg, lg = _run(torch, mxk, x, c0, max_iterations=1, tolerance=0.0)
+    assert it == 1
+    shift, co, lo, dots = orc.lloyd_step(x, orc.l2_norm(x), c0, want_dots=True)
+    near, first, second = orc.top2(orc.l2_norm(x), orc.l2_norm(c0), dots)
+    diff = lg != lo
+    scale = orc.l2_norm(x) + orc.l2_norm(c0).max()
+    assert np.all((second - first)[diff] <= 1e-5 * scale[diff])
+    if not diff.any():
+        assert np.allclose(cg, co, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,d,k,iters", [(20000, 128, 32, 8), (8000, 256, 128, 5)])
+def test_full_run_vs_oracle(torch_cuda, mxk, orc, n, d, k, iters):
+    torch = torch_cuda
+    x = blobs(n, d, k, seed=n + d, spread=10.0, sigma=1.0)
+    c0 = x[np.random.default_rng(7).choice(n, k, replace=False)].copy()
+    it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=iters, tolerance=1e-4)
+    it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=iters, tolerance=1e-4)
+    ig, io = orc.inertia(x, cg, lg), orc.inertia(x, co, lo)
+    assert abs(ig - io) <= 1e-4 * io
+    agree = np.mean(lg == lo)
+    assert agree > 0.999
+    if np.array_equal(lg, lo):
+        assert it_g == it_o
+        assert np.allclose(cg, co, rtol=1e-4, atol=1e-4)
+
+
+def test_fp32_iterations(torch_cuda, mxk, orc):
+    torch = torch_cuda
+    n, d, k = 6000, 128, 16
+    x = blobs(n, 64, k, seed=5)
+    c0 = x[:k].copy()
+    it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=4, fp32_iterations=2, tolerance=0.0)
+    it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=4, fp32_iterations=2, tolerance=0.0)
+    assert it_g == it_o
+    assert np.mean(lg == lo) > 0.999
+    assert abs(orc.inertia(x, cg, lg) - orc.inertia(x, co, lo)) <= 1e-4 * orc.inertia(x, co, lo)
+
+
+def test_nonfinite_shift_raises(torch_cuda, mxk):
+    torch = torch_cuda
+    n, d, k = 256, 128, 4
+    x = np.full((n, d), 3e38, np.float32)
+    c0 = np.zeros((k, d), np.float32)
+    with pytest.raises(mxk.MxkError, match="Non-finite centroid shift"):
+        _run(torch, mxk, x, c0, max_iterations=2, tolerance=0.0)
+
+
+def test_rejects_unpadded_d(torch_cuda, mxk):
+    torch = torch_cuda
+    with pytest.raises(ValueError):
+        _run(torch, mxk, np.zeros((8, 96), np.float32), np.zeros((4, 96), np.float32), max_iterations=1)
