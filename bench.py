@@ -1,0 +1,387 @@
+"""Benchmark of the MX-KMeans Lloyd iteration on B200 (BASELINE.json metric:
+Lloyd point-iterations/sec; MX-GEMM fraction of tensor peak).
+
+Workload: BASELINE configs[3] -- N = 8,388,608 points, D = 96 zero-padded to
+128, K = 2048 clusters, seeded Gaussian blobs (centers U[-5,5]^96, sigma 0.75,
+seed 3), K-Means++ initial centroids, 20 Lloyd iterations with tol 0 (a run can
+stop earlier on an exactly unchanged shift; the reported rate uses the
+iterations actually run).  One step = one kmeans_mixed call over the whole
+dataset, from the same initial centroids (the reference CLI's timed unit,
+src/main.cu:115-123).  With --gpus N (torchrun, one rank per GPU) the points are
+row-sharded and every iteration NCCL-allreduces the K x D sums and K counts:
+strong scaling of the fixed N.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mx-kmeans_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+N_POINTS, D_RAW, D_PAD, K_CLUSTERS, ITERS, SEED = 8388608, 96, 128, 2048, 20, 3
+METRIC = "Lloyd point-iters/sec"
+UNIT = "point-iters/s"
+WORKLOAD = ("configs[3]: N=8388608, D=96 zero-padded to 128, K=2048, blobs centers U[-5,5]^96 sigma 0.75, "
+            "seed 3, K-Means++ init, 20 iterations (tol 0), MXFP8 points/centroids, FP32 update")
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="mxk", choices=["mxk", "reference"])
+    # profiling aids (the ncu commands under profiles/ use them; bench lines never do)
+    p.add_argument("--n", type=int, default=N_POINTS, help="points (default: configs[3]'s N)")
+    p.add_argument("--init", default="kmeans++", choices=["kmeans++", "random"],
+                   help="random = K distinct random rows (fast set-up for profiling runs)")
+    p.add_argument("--quick", action="store_true", help="skip the e2e and CPU-baseline legs")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ----------------------------------------------------------------------------- data
+
+def make_dataset(torch, n, device):
+    """Seeded blobs of configs[3] on the device (identical on every rank)."""
+    g = torch.Generator(device=device).manual_seed(SEED)
+    centers = torch.rand((K_CLUSTERS, D_RAW), generator=g, device=device) * 10.0 - 5.0
+    labels = torch.randint(0, K_CLUSTERS, (n,), generator=g, device=device)
+    x = torch.zeros((n, D_PAD), device=device)
+    chunk = 1 << 22
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        x[s:e, :D_RAW] = centers[labels[s:e]] + 0.75 * torch.randn((e - s, D_RAW), generator=g, device=device)
+    return x
+
+
+def kmeanspp_init(torch, x, k, seed):
+    """D^2-sampling K-Means++ on the device (same draw structure as the reference:
+    first index uniform, each next index with probability proportional to the
+    squared distance to the nearest chosen center).  Untimed set-up."""
+    g = torch.Generator(device=x.device).manual_seed(seed)
+    n = x.shape[0]
+    pn = (x * x).sum(1)
+    centers = torch.empty((k, x.shape[1]), device=x.device)
+    idx = int(torch.randint(0, n, (1,), generator=g, device=x.device).item())
+    dist = torch.full((n,), float("inf"), device=x.device)
+    for c in range(k):
+        centers[c] = x[idx]
+        cvec = x[idx]
+        d = (pn - 2.0 * (x @ cvec) + (cvec * cvec).sum()).clamp_min_(0.0)
+        dist = torch.minimum(dist, d)
+        dist[idx] = 0.0
+        if c + 1 == k:
+            break
+        idx = int(torch.multinomial(dist, 1, generator=g).item())
+    return centers
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of this rank's GPU during the
+    timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def physical_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+# ----------------------------------------------------------------------------- CPU legs
+
+def cpu_sample_rate(fn_name, n_total):
+    """Time an oracle Lloyd iteration on the host cores over a bounded sample of
+    the workload (about 10-20 s of CPU work); -> (point-iters/s, sample text, cores)."""
+    import numpy as np
+    import oracle
+    threads = oracle.hardware_threads()
+    g = np.random.default_rng(SEED)
+    centers = g.uniform(-5, 5, (K_CLUSTERS, D_RAW)).astype(np.float32)
+
+    def sample(n):
+        x = np.zeros((n, D_PAD), np.float32)
+        x[:, :D_RAW] = centers[g.integers(0, K_CLUSTERS, n)] + 0.75 * g.standard_normal((n, D_RAW)).astype(np.float32)
+        return x
+
+    c0 = sample(K_CLUSTERS)
+
+    def run(x):
+        t = time.perf_counter()
+        if fn_name == "lloyd_fp32":
+            oracle.lloyd_fp32(x, c0, 1, 0.0, threads)
+        else:
+            oracle.lloyd_step(x, oracle.l2_norm(x), c0, threads)
+        return time.perf_counter() - t
+
+    n = 4096
+    t = run(sample(n))
+    target = 12.0
+    n2 = int(min(n_total, max(n, n * target / max(t, 1e-3))))
+    n2 = max(4096, n2 // 4096 * 4096)
+    t2 = run(sample(n2))
+    kind = "FP32 Lloyd (oracle port of the reference's host-visible algorithm)" if fn_name == "lloyd_fp32" else \
+        "MX Lloyd step (oracle port of kmeans_mixed: MXFP8 quantize, product, assign, update)"
+    return n2 / t2, f"1 iteration of {kind} over {n2} of the {n_total} points, K={K_CLUSTERS}, D={D_PAD}", threads
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    value, sample, cores = cpu_sample_rate("lloyd_step", args.n)
+    steps = []
+    for _ in range(args.steps):
+        steps.append(value)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "mxfp8+f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": ("the reference's Lloyd path is sm_120a-only CUDA (no CPU implementation); this arm times the "
+                     "oracle's C restatement of kmeans_mixed on the host cores")}
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(torch, dist, mxk, x, c_init, cent, labels, comm, opts, stream, barrier, world, n, rows, args):
+    """Same metric through the C ABI from pinned HOST buffers: each step copies the
+    rank's points and the initial centroids in, runs kmeans_mixed, and copies the
+    labels and final centroids out, all inside the timed region."""
+    x_host = x.cpu().pin_memory()
+    c_host = c_init.cpu().pin_memory()
+    lab_host = torch.empty(rows, dtype=torch.int32).pin_memory()
+    cent_host = torch.empty_like(c_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(1, min(args.steps, 3))
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        cent.copy_(c_host, non_blocking=True)
+        if comm is not None:
+            it = mxk.kmeans_mixed_sharded(comm, x_dev, cent, labels, opts)
+        else:
+            it = mxk.kmeans_mixed(x_dev, cent, labels, opts)
+        lab_host.copy_(labels, non_blocking=True)
+        cent_host.copy_(cent, non_blocking=True)
+        return it
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_iters = 0
+    for _ in range(e2e_steps):
+        e2e_iters += e2e_step()
+    e1.record(stream)
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=x.device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = n * e2e_iters / (float(te.item()) / 1e3)
+
+    return {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.numel() * 4 + c_init.numel() * 4),
+            "d2h_bytes_per_step": int(rows * 4 + c_init.numel() * 4), "steps": e2e_steps}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import mxk
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=dev)
+    mxk.load()
+    n = args.n
+    x_full = make_dataset(torch, n, dev)
+    if args.init == "kmeans++":
+        c_init = kmeanspp_init(torch, x_full, K_CLUSTERS, SEED)
+    else:
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        c_init = x_full[torch.randperm(n, generator=g, device=dev)[:K_CLUSTERS]].clone()
+    row0 = n // world * rank + min(rank, n % world)
+    rows = n // world + (1 if rank < n % world else 0)
+    x = x_full[row0:row0 + rows].contiguous()
+    del x_full
+    torch.cuda.empty_cache()
+    cent = torch.empty_like(c_init)
+    labels = torch.empty(rows, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    opts = mxk.Options(max_iterations=ITERS, tolerance=0.0)
+
+    comm = None
+    if world > 1:
+        uid = [mxk.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = mxk.Comm(world, rank, uid[0])
+
+    def step():
+        cent.copy_(c_init)
+        if comm is not None:
+            return mxk.kmeans_mixed_sharded(comm, x, cent, labels, opts)
+        return mxk.kmeans_mixed(x, cent, labels, opts)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+
+    # ---- timed region (device time, CUDA events on the launching stream)
+    sampler = ClockSampler(physical_index(local_rank))
+    sampler.start()
+    mxk.profile_enable(True)
+    launches0 = mxk.launch_count()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    iters = 0
+    for _ in range(args.steps):
+        iters += step()
+    ev1.record(stream)
+    barrier()
+    launches = mxk.launch_count() - launches0
+    stats = mxk.profile_read()
+    mxk.profile_enable(False)
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = n * iters / (ms_max / 1e3)
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = None
+    if not args.quick:
+        e2e = run_e2e(torch, dist, mxk, x, c_init, cent, labels, comm, opts, stream, barrier, world, n, rows, args)
+
+    # ---- roofline of the dominant kernel (fused MX GEMM + argmin)
+    pk, pk_kind = peaks()
+    gemm = stats.get("mx_gemm_argmin")
+    roofline = None
+    if gemm and gemm[0]:
+        per_launch_ms = gemm[1] / gemm[0]
+        # one launch per precision group per iteration; only the MXFP8 group is non-empty
+        launches_nonempty = iters
+        flops_per_iter = 2.0 * rows * K_CLUSTERS * D_PAD
+        achieved = flops_per_iter * launches_nonempty / (gemm[1] / 1e3) / 1e12
+        peak = 2.0 * pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": None,
+                    "kernel": "mx_gemm_argmin", "launch_ms_avg": per_launch_ms,
+                    "flops_per_iteration": flops_per_iter,
+                    "peak_source": f"2 x bf16_tflops_sustained of {pk_kind} MEASURED_PEAKS.json "
+                                   "(dense MXFP8 tensor rate is twice BF16)"}
+    kernel_ms = {k: {"launches": v[0], "total_ms": round(v[1], 3)} for k, v in sorted(stats.items(), key=lambda kv: -kv[1][1])}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.quick:
+        v, sample, cores = cpu_sample_rate("lloyd_fp32", n)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "mxfp8+f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "points": n, "dims": D_PAD, "clusters": K_CLUSTERS,
+                           "iterations_per_step": iters / args.steps, "parallelism": f"row-shard x{world}",
+                           "l2": "inputs (4.3 GB of points per step) larger than the 126 MB L2"},
+                "e2e": e2e,
+                "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+                "kernel_ms": kernel_ms}
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
