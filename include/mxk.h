@@ -95,6 +95,17 @@ int mxk_update_centroids(int64_t n, int d, int k, const float* points, const int
 int mxk_centroid_shift(int64_t elements, const float* previous, const float* current,
                        float* device_sum, float* host_result, void* stream);
 
+/* No counterpart in the reference.  The same convergence shift as
+ * mxk_centroid_shift for callers that cannot allocate device memory (a plugin
+ * inside a framework whose pool owns the device, a loop with a fixed memory
+ * budget): its scratch is a fixed device array inside the library (64 KB per
+ * GPU, held until exit), so the call allocates nothing.  elements <= 33,554,432,
+ * larger inputs return MXK_ERR_INVALID.  The first call on a device looks up the
+ * array's device address (make it before any stream capture); calls that overlap
+ * on the GPU share the array and race.  device_sum may be NULL. */
+int mxk_centroid_shift_noalloc(int64_t elements, const float* previous, const float* current,
+                               float* device_sum, float* host_result, void* stream);
+
 /* ---- fused hot op (replaces gemm_mx + assign_clusters, src/kmeans.cu:54-56) ---- */
 
 /* Nearest centroid of `rows` quantized points against k MXFP8 centroids with no

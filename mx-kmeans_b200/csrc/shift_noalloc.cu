@@ -1,0 +1,135 @@
+// Convergence shift, sum((previous - current)^2), for callers that cannot
+// allocate device memory.
+//
+// Some callers may not call cudaMalloc (or any allocator) at the point where
+// they need the shift: a plugin running inside a host framework whose memory
+// pool owns the whole device, a real-time loop with a fixed memory budget set up
+// once, or code that has handed every byte of the device to another allocator.
+// mxk_centroid_shift needs a small per-call scratch buffer for its per-CTA
+// partial sums and takes it from the stream-ordered allocator; this variant
+// keeps that scratch in a fixed device array compiled into the library instead.
+//
+// The scratch is a file-scope static __device__ array of kMaxPartials + 1
+// floats (64 KB + 4 bytes): one partial per 2048-element chunk plus the total.
+// Every GPU that loads the library holds this array until the process exits.
+// It bounds the input to kMaxElements = 16384 * 2048 = 33,554,432 elements
+// (every BASELINE configuration's K x D is far below it); larger inputs are
+// rejected with MXK_ERR_INVALID before any work is issued.
+//
+// All calls on a device share the one array and it keeps the previous call's
+// contents.  Each call overwrites exactly the partial slots it reads (one per
+// chunk, written before the total kernel reads them) and the total slot, so no
+// clearing is needed; but two calls whose kernels overlap on the GPU (different
+// streams, or different host threads on one device) race on the array and must
+// be serialized by the caller.
+//
+// The host never uses the array's symbol as a pointer: on a device's first
+// call, with that device current, cudaGetSymbolAddress gives the device
+// address, which is cached per device and passed to the kernels.  That first
+// call therefore does set-up work and should come before any stream capture.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace mxk {
+namespace {
+
+constexpr int kNoAllocChunk = 2048;  // elements per CTA (256 threads x 8)
+constexpr int kMaxPartials = 16384;
+constexpr int64_t kMaxElements = (int64_t)kMaxPartials * kNoAllocChunk;
+
+static __device__ __align__(256) float g_shift_scratch[kMaxPartials + 1];
+
+std::mutex g_scratch_mutex;
+float* g_scratch_ptr[64] = {};
+
+int scratch_address(float** out) {
+    int dev = 0;
+    MXK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MXK_ERR_UNSUPPORTED, "centroid_shift_noalloc: device ordinal >= 64");
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_shift_scratch);
+        if (e != cudaSuccess) return fail_cuda("cudaGetSymbolAddress(g_shift_scratch)", e);
+        g_scratch_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_scratch_ptr[dev];
+    return MXK_OK;
+}
+
+// One CTA per 2048-element chunk; each thread sums 8 elements in index order,
+// the CTA reduces in a fixed order and writes partials[blockIdx.x].
+__global__ void __launch_bounds__(256) shift_chunk_kernel(int64_t elements, const float* __restrict__ prev,
+                                                          const float* __restrict__ cur, float* __restrict__ partials) {
+    __shared__ float warp_sum[8];
+    const int64_t base = (int64_t)blockIdx.x * kNoAllocChunk + threadIdx.x;
+    float local = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNoAllocChunk / 256; ++j) {
+        const int64_t i = base + (int64_t)j * 256;
+        if (i < elements) {
+            const float diff = prev[i] - cur[i];
+            local += diff * diff;
+        }
+    }
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < 8; ++w) s += warp_sum[w];
+        partials[blockIdx.x] = s;
+    }
+}
+
+// Sums partials[0..count) in a fixed order into *total.
+__global__ void __launch_bounds__(1024) shift_partials_total_kernel(const float* __restrict__ partials, int count,
+                                                                    float* __restrict__ total) {
+    __shared__ float warp_sum[32];
+    float local = 0.0f;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) local += partials[i];
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
+        *total = s;
+    }
+}
+
+}  // namespace
+}  // namespace mxk
+
+extern "C" int mxk_centroid_shift_noalloc(int64_t elements, const float* previous, const float* current,
+                                          float* device_sum, float* host_result, void* stream) {
+    using namespace mxk;
+    MXK_REQUIRE(elements >= 0, "centroid_shift_noalloc: negative element count");
+    if (elements > kMaxElements)
+        return fail(MXK_ERR_INVALID, "centroid_shift_noalloc: " + std::to_string(elements) +
+                                         " elements exceed the fixed scratch limit of " +
+                                         std::to_string(kMaxElements) + " (use mxk_centroid_shift)");
+    MXK_REQUIRE(elements == 0 || (previous && current), "centroid_shift_noalloc: null input");
+    cudaStream_t s = as_stream(stream);
+    float* scratch = nullptr;
+    MXK_CHECK(scratch_address(&scratch));
+    float* total = scratch + kMaxPartials;
+    const int chunks = (int)((elements + kNoAllocChunk - 1) / kNoAllocChunk);
+    if (chunks > 0) {
+        LaunchScope scope("shift_noalloc", s);
+        shift_chunk_kernel<<<chunks, 256, 0, s>>>(elements, previous, current, scratch);
+        MXK_CUDA(cudaGetLastError());
+    }
+    {
+        LaunchScope scope("shift_noalloc_total", s);
+        shift_partials_total_kernel<<<1, 1024, 0, s>>>(scratch, chunks, total);
+        MXK_CUDA(cudaGetLastError());
+    }
+    if (device_sum) MXK_CUDA(cudaMemcpyAsync(device_sum, total, sizeof(float), cudaMemcpyDeviceToDevice, s));
+    float h = 0.0f;
+    MXK_CUDA(cudaMemcpyAsync(&h, total, sizeof(float), cudaMemcpyDeviceToHost, s));
+    MXK_CUDA(cudaStreamSynchronize(s));
+    if (host_result) *host_result = h;
+    return MXK_OK;
+}

@@ -56,6 +56,7 @@ SIGNATURES = {
     "mxk_assign_clusters": ([_I64, _I, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_update_centroids": ([_I64, _I, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_centroid_shift": ([_I64, _P, _P, _P, _P, _P], _I),
+    "mxk_centroid_shift_noalloc": ([_I64, _P, _P, _P, _P, _P], _I),
     "mxk_assign_mx_fused": ([_I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_kmeans_mixed": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_comm_unique_id": ([ctypes.c_char_p], _I),
