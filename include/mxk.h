@@ -111,11 +111,15 @@ int mxk_centroid_shift_noalloc(int64_t elements, const float* previous, const fl
 /* Nearest centroid of `rows` quantized points against k MXFP8 centroids with no
  * N x K product buffer: tcgen05 MMA into TMEM, distance fmaf(-2,dot,pn+cn) and
  * lowest-index argmin in the epilogue.  Writes labels[pid[r]] and, when gaps is
- * not NULL, the two-largest gap (init -1e38) like assign_clusters. */
+ * not NULL, the two-largest gap (init -1e38) like assign_clusters.
+ * start_hint (optional, one label per point, may alias labels): every 128-row
+ * tile sweeps the centroids starting at the 128-centroid tile of its first
+ * row's hint -- previous labels make the sweep find the minimum early; the
+ * result does not depend on the hint. */
 int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, const uint8_t* a_scales,
                         const uint8_t* b, const uint8_t* b_scales, const float* point_norms,
                         const float* centroid_norms, const int* pid, int* labels, float* gaps,
-                        void* stream);
+                        const int* start_hint, void* stream);
 
 /* ---- Lloyd driver --------------------------------------------------------- */
 

@@ -101,14 +101,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// One try_wait with a suspend-time hint: a waiting warp is parked by the
+// hardware until the phase completes (or ~1 ms passes) instead of spinning and
+// taking issue slots from the producer and MMA warps on its SM sub-partition.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     return done != 0;
 }
@@ -139,6 +142,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
             smem_addr(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned, size % 16 == 0),
+// completion signalled on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
@@ -207,6 +219,35 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// --- packed FP32 pairs and 3-input min (sm_100) ----------------------------
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+// (d0, d1) = fmaf(-2, (v0, v1), pn2 + (c0, c1)) with .f32x2 add and fma; every
+// lane is rounded exactly as the scalar add and fmaf would round it.
+__device__ __forceinline__ void dist2(uint32_t v0, uint32_t v1, uint64_t pn2, float c0, float c1, float& d0,
+                                      float& d1) {
+    asm("{\n\t.reg .b64 s, v, m, d;\n\t"
+        "mov.b64 s, {%3, %4};\n\t"
+        "add.rn.f32x2 s, %2, s;\n\t"
+        "mov.b64 v, {%5, %6};\n\t"
+        "mov.b64 m, {%7, %7};\n\t"
+        "fma.rn.f32x2 d, m, v, s;\n\t"
+        "mov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "l"(pn2), "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
+}
+
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 
 // Shared-memory matrix descriptor (tcgen05 "version 1" format):
 //   [0,14) start address >> 4, [16,30) leading byte offset >> 4,

@@ -10,9 +10,13 @@ namespace mxk {
 
 // ---- quantize.cu ------------------------------------------------------------
 // rows_dev (optional): device-resident row count that overrides `rows`, which
-// then only sizes the grid (an upper bound).
+// then only sizes the grid (an upper bound).  atoms: write the scales in the
+// tcgen05 atom layout (scale_atom_bytes(rows, d) bytes, d % 128 == 0) instead of
+// row-major [rows][d/32].
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
-                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream);
+                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream,
+                    bool atoms = false);
+inline int64_t scale_atom_bytes(int64_t rows, int d) { return (rows + 127) / 128 * (d / 128) * 512; }
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
 int launch_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
                         cudaStream_t stream);
@@ -23,10 +27,17 @@ int launch_assign_precisions(int64_t n, int d, const float* upper, const float* 
 int launch_centroid_stats(int k, const float* errors, const float* norms, float* stats, cudaStream_t stream);
 // Stable per-precision compaction of point ids (src/kmeans.cu:45-52).
 // ids: 3*n ints (groups 4, 6, 8 at offsets 0, n, 2n); group_counts: 3 ints.
-// scratch: compaction_scratch_ints(n) ints.
+// scratch: compaction_scratch_ints(n) ints.  order (optional, n ints): the
+// sequence to compact (element i is point order[i]); null = 0..n-1.
 int64_t compaction_scratch_ints(int64_t n);
-int launch_group_compaction(int64_t n, const int* precision, int* ids, int* group_counts, int* scratch,
-                            cudaStream_t stream);
+int launch_group_compaction(int64_t n, const int* precision, const int* order, int* ids, int* group_counts,
+                            int* scratch, cudaStream_t stream);
+
+// ---- order.cu -----------------------------------------------------------------
+// order = point indices 0..n-1 sorted by labels[] (counting sort over k keys;
+// order within a key is unspecified).  scratch: label_sort_scratch_ints(k) ints.
+int64_t label_sort_scratch_ints(int k);
+int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream);
 
 // ---- gemm_mx.cu ---------------------------------------------------------------
 struct MxArgmin {
@@ -35,12 +46,19 @@ struct MxArgmin {
     const int* pid = nullptr;
     int* labels = nullptr;
     float* gaps = nullptr;  // optional two-largest gap (init -1e38)
+    // optional label per point (may be `labels` itself, read before it is
+    // overwritten): each 128-row tile sweeps the centroids starting at the tile
+    // of its first row's hint; results do not depend on it
+    const int* start_hint = nullptr;
 };
 // Dense: out[m x n] = A . B^T.  Argmin: labels of the m rows against n centroids.
 // rows_dev (optional) = device-resident m (m is then an upper bound).
+// scale_atoms: both scale arrays are in the tcgen05 atom layout (see
+// launch_quantize), which the kernel fetches with bulk TMA copies; otherwise
+// they are row-major and gathered by the producer warp.
 int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales,
                    const uint8_t* b, const uint8_t* b_scales, float* out, const MxArgmin* argmin,
-                   const int* rows_dev, cudaStream_t stream);
+                   const int* rows_dev, cudaStream_t stream, bool scale_atoms = false);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,
@@ -51,9 +69,10 @@ int launch_assign_clusters(int64_t rows, int k, const float* point_norms, const 
                            const float* dots, const int* pid, int* labels, float* gaps, cudaStream_t stream);
 
 // ---- update.cu ---------------------------------------------------------------
-// sums (k x d) and counts (k) must be zeroed by the caller.
-int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, float* sums,
-                      int* counts, cudaStream_t stream);
+// sums (k x d) and counts (k) must be zeroed by the caller.  order (optional):
+// visit the points in this sequence (label-sorted orders make long label runs).
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
+                      float* sums, int* counts, cudaStream_t stream);
 // centroids = counts ? sums / counts : old.  If shift_scratch is not null
 // (shift_scratch_floats() floats), its last element receives sum((old - new)^2),
 // reduced in a fixed order (bit-reproducible).  sums and centroids may alias.

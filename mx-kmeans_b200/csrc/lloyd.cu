@@ -134,13 +134,19 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&ids, 3 * n));
     MXK_CHECK(ws.alloc(&gcount, 4));
     MXK_CHECK(ws.alloc(&cscratch, compaction_scratch_ints(n)));
+    int *order = nullptr, *sort_scratch = nullptr;
+    MXK_CHECK(ws.alloc(&order, n));
+    MXK_CHECK(ws.alloc(&sort_scratch, label_sort_scratch_ints(k)));
     MXK_CHECK(ws.alloc(&qpoints, n * d));
-    MXK_CHECK(ws.alloc(&pscales, n * (d / 32)));
+    MXK_CHECK(ws.alloc(&pscales, scale_atom_bytes(n, d)));
     MXK_CHECK(ws.alloc(&cnorm, k));
     MXK_CHECK(ws.alloc(&cerr, k));
     MXK_CHECK(ws.alloc(&stats, 2));
     MXK_CHECK(ws.alloc(&qcent, kd));
-    MXK_CHECK(ws.alloc(&cscales, kd / 32));
+    MXK_CHECK(ws.alloc(&cscales, scale_atom_bytes(k, d)));
+    // scale atoms of padding rows are never written; keep them finite
+    MXK_CUDA(cudaMemsetAsync(pscales, 0, (size_t)scale_atom_bytes(n, d), stream));
+    MXK_CUDA(cudaMemsetAsync(cscales, 0, (size_t)scale_atom_bytes(k, d), stream));
     MXK_CHECK(ws.alloc(&prev, kd));
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
@@ -162,6 +168,13 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
     int result = options->max_iterations;
     for (int it = 0; it < options->max_iterations; ++it) {
+        // From the second iteration on, visit points grouped by their previous
+        // label (order.cu); the first iteration keeps ascending point order.
+        const int* ord = nullptr;
+        if (it > 0 && n > 0) {
+            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream));
+            ord = order;
+        }
         MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
         if (it < options->fp32_iterations) {
@@ -176,22 +189,23 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 std::fprintf(stderr, "iteration=%d precision=FP32\n", it + 1);
         } else {
             MXK_CUDA(cudaMemsetAsync(cerr, 0, sizeof(float) * k, stream));
-            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream));
+            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream, true));
             MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
             MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream));
-            MXK_CHECK(launch_group_compaction(n, precision, ids, gcount, cscratch, stream));
+            MXK_CHECK(launch_group_compaction(n, precision, ord, ids, gcount, cscratch, stream));
             static const int group_bits[3] = {4, 6, 8};
             for (int g = 0; g < 3; ++g) {
                 MXK_CHECK(launch_quantize(group_bits[g], n, d, points, ids + g * n, qpoints, pscales, nullptr,
-                                          gcount + g, stream));
+                                          gcount + g, stream, true));
                 MxArgmin am;
                 am.point_norms = pnorm;
                 am.centroid_norms = cnorm;
                 am.pid = ids + g * n;
                 am.labels = labels;
                 am.gaps = nullptr;
+                am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
                 MXK_CHECK(launch_gemm_mx(group_bits[g], n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am,
-                                         gcount + g, stream));
+                                         gcount + g, stream, true));
             }
             if (options->verbose && (!comm || comm->rank == 0)) {
                 int h[3] = {0, 0, 0};
@@ -203,7 +217,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         // kmeans.cu:62-65
         MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
         MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
-        MXK_CHECK(launch_accumulate(n, d, k, points, labels, sums, counts, stream));
+        MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream));
         if (sharded) {
             NcclApi& api = nccl();
             ncclResult_t r = api.GroupStart();

@@ -101,6 +101,30 @@ __device__ __forceinline__ float e2m3_decode(uint32_t c) { return subbyte_decode
 __device__ __forceinline__ float e2m1_decode(uint32_t c) { return subbyte_decode<1, 1, 3>(c); }
 __device__ __forceinline__ float e3m2_decode(uint32_t c) { return subbyte_decode<2, 3, 5>(c); }
 
+// Hardware round trips through E2M1 and E3M2 (cvt.rn.satfinite encode, cvt to
+// f16x2 decode).  For finite inputs inside the format's range they equal the
+// software encoders above (round to nearest even); the point-bound kernel only
+// feeds them values scaled into range by their block scale.
+__device__ __forceinline__ float e2m1_round_trip(float x) {
+    uint32_t h2;
+    asm("{\n\t.reg .b8 q;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q, %2, %1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, q;\n\t}"
+        : "=r"(h2)
+        : "f"(x), "f"(0.0f));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
+}
+
+__device__ __forceinline__ float e3m2_round_trip(float x) {
+    uint32_t h2;
+    asm("{\n\t.reg .b16 q;\n\t"
+        "cvt.rn.satfinite.e3m2x2.f32 q, %2, %1;\n\t"
+        "cvt.rn.f16x2.e3m2x2 %0, q;\n\t}"
+        : "=r"(h2)
+        : "f"(x), "f"(0.0f));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
+}
+
 // Re-encode an E2M3 / E2M1 code as the E4M3 code of the same value (every
 // E2M3 and E2M1 value is exactly representable in E4M3).
 __device__ __forceinline__ uint32_t e2m3_to_e4m3(uint32_t c) {

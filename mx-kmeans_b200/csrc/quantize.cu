@@ -26,11 +26,20 @@ __device__ __forceinline__ float4 ldg4(const float* p) {
 // threads of a 32-feature block combine their maxima with one shuffle, derive the
 // UE8M0 scale exactly as the reference (Scale(amax/qmax) or 1 when amax == 0),
 // and multiply by the exact reciprocal of the scale.
+// Byte offset of the scale of (row, 32-feature block) in the tcgen05 atom layout:
+// one 512-byte atom per (128-row tile, 128-feature chunk), tile-major, holding
+// row r's four block scales at (r % 32) * 16 + (r / 32) * 4 + block % 4.
+__device__ __forceinline__ int64_t scale_atom_offset(int64_t row, int blk, int kchunks) {
+    const int64_t tile = row >> 7;
+    const int r = (int)(row & 127);
+    return ((tile * kchunks + (blk >> 2)) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + (blk & 3);
+}
+
 template <int BITS>
 __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chunks, int d,
                                                const float* __restrict__ points, const int* __restrict__ pid,
                                                uint8_t* __restrict__ values, uint8_t* __restrict__ scales,
-                                               float* __restrict__ errors) {
+                                               float* __restrict__ errors, bool atoms) {
     const bool valid = g < total;
     const int64_t row = valid ? g / chunks : 0;
     const int chunk = valid ? (int)(g - row * chunks) : 0;
@@ -121,7 +130,10 @@ __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chu
         *reinterpret_cast<uint2*>(values + elem / 2) = w;
     }
     if ((chunk & 1) == 0) {
-        scales[row * (d >> 5) + (chunk >> 1)] = (uint8_t)s;
+        if (atoms)
+            scales[scale_atom_offset(row, chunk >> 1, d >> 7)] = (uint8_t)s;
+        else
+            scales[row * (d >> 5) + (chunk >> 1)] = (uint8_t)s;
         // Squared errors are non-negative, so integer order equals float order.
         if (errors) atomicMax(reinterpret_cast<unsigned*>(errors + row), __float_as_uint(err));
     }
@@ -131,13 +143,13 @@ template <int BITS>
 __global__ void __launch_bounds__(256) quantize_kernel(int64_t rows, int d, const float* __restrict__ points,
                                                        const int* __restrict__ pid, uint8_t* __restrict__ values,
                                                        uint8_t* __restrict__ scales, float* __restrict__ errors,
-                                                       const int* __restrict__ rows_dev) {
+                                                       const int* __restrict__ rows_dev, bool atoms) {
     const int64_t nrows = rows_dev ? (int64_t)*rows_dev : rows;
     const int chunks = d >> 4;
     const int64_t total = nrows * chunks;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;  // multiple of 32: block pairs stay in one warp
     for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
-        quantize_chunk<BITS>(base + threadIdx.x, total, chunks, d, points, pid, values, scales, errors);
+        quantize_chunk<BITS>(base + threadIdx.x, total, chunks, d, points, pid, values, scales, errors, atoms);
     }
 }
 
@@ -165,42 +177,44 @@ __global__ void __launch_bounds__(256) l2_norm_kernel(int64_t rows, int d, const
     if (row0 + lane < rows) norms[row0 + lane] = sum;
 }
 
-// One warp per point; lane = feature within a 32-block.  FP4 (E2M1) and FP6
-// (E3M2, as the reference) reconstruction errors over features 1..31 of each
-// block (quantize.cu:74-98).
+// One thread per point, one 32-feature block at a time (eight 128-bit loads of
+// the block's contiguous 128 bytes): block maximum, the FP4 (E2M1) and FP6 (E3M2,
+// as the reference) scales, and the reconstruction errors of features 1..31
+// (quantize.cu:74-98: feature 0 of each block is skipped, an exact max either way).
 __global__ void __launch_bounds__(256) point_bounds_kernel(int64_t n, int d, const float* __restrict__ points,
                                                            const float* __restrict__ norms, float* __restrict__ upper) {
-    const int lane = threadIdx.x & 31;
-    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (p >= n) return;
+    const float* row = points + p * d;
     float e4 = 0.0f, e6 = 0.0f;
     for (int base = 0; base < d; base += 32) {
-        const float v = points[p * d + base + lane];
-        float amax = fabsf(v);
+        float x[32];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = ldg4(row + base + 4 * i);
+            x[4 * i] = v.x, x[4 * i + 1] = v.y, x[4 * i + 2] = v.z, x[4 * i + 3] = v.w;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
         const uint32_t s4 = dev::ue8m0_encode(amax > 0.0f ? amax / 6.0f : 1.0f);
         const uint32_t s6 = dev::ue8m0_encode(amax > 0.0f ? amax / 7.5f : 1.0f);
-        if (lane >= 1) {
-            const float q4 = dev::e2m1_decode(dev::e2m1_encode(v * dev::ue8m0_reciprocal(s4)));
-            const float q6 = dev::e3m2_decode(dev::e3m2_encode(v * dev::ue8m0_reciprocal(s6)));
-            e4 = fmaxf(e4, fabsf(fmaf(q4, dev::ue8m0_value(s4), -v)));
-            e6 = fmaxf(e6, fabsf(fmaf(q6, dev::ue8m0_value(s6), -v)));
+        const float r4 = dev::ue8m0_reciprocal(s4), r6 = dev::ue8m0_reciprocal(s6);
+        const float v4 = dev::ue8m0_value(s4), v6 = dev::ue8m0_value(s6);
+#pragma unroll
+        for (int j = 1; j < 32; ++j) {
+            const float q4 = dev::e2m1_round_trip(x[j] * r4);
+            const float q6 = dev::e3m2_round_trip(x[j] * r6);
+            e4 = fmaxf(e4, fabsf(fmaf(q4, v4, -x[j])));
+            e6 = fmaxf(e6, fabsf(fmaf(q6, v6, -x[j])));
         }
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        e4 = fmaxf(e4, __shfl_xor_sync(kFull, e4, o));
-        e6 = fmaxf(e6, __shfl_xor_sync(kFull, e6, o));
-    }
-    if (lane == 0) {
-        const size_t tile = (size_t)(p / 32) * 96;
-        const int slot = (int)(p % 32);
-        const float nrm = norms[p];
-        upper[tile + slot] = nrm;
-        upper[tile + 32 + slot] = fmaf((float)d * e6, e6, nrm);
-        upper[tile + 64 + slot] = fmaf((float)d * e4, e4, nrm);
-    }
+    const size_t tile = (size_t)(p / 32) * 96;
+    const int slot = (int)(p % 32);
+    const float nrm = norms[p];
+    upper[tile + slot] = nrm;
+    upper[tile + 32 + slot] = fmaf((float)d * e6, e6, nrm);
+    upper[tile + 64 + slot] = fmaf((float)d * e4, e4, nrm);
 }
 
 __global__ void __launch_bounds__(256) precision_kernel(int64_t n, int d, const float* __restrict__ upper,
@@ -253,7 +267,11 @@ __global__ void centroid_stats_kernel(int k, const float* __restrict__ errors, c
 // ---- stable three-way compaction (thrust::copy_if per group, kmeans.cu:46-50)
 constexpr int kCompactBlock = 1024;  // elements per block (256 threads x 4)
 
+// Element i of the sequence is point order[i] (or i without an order), so the
+// groups come out in the sequence's order -- ascending point index like the
+// reference's copy_if, or label-sorted when the driver passes that order.
 __global__ void __launch_bounds__(256) group_block_count_kernel(int64_t n, const int* __restrict__ precision,
+                                                                const int* __restrict__ order,
                                                                 int* __restrict__ block_counts, int nblocks) {
     __shared__ int cnt[3];
     if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
@@ -261,9 +279,9 @@ __global__ void __launch_bounds__(256) group_block_count_kernel(int64_t n, const
     int local[3] = {0, 0, 0};
     const int64_t base = (int64_t)blockIdx.x * kCompactBlock;
     for (int i = threadIdx.x; i < kCompactBlock; i += blockDim.x) {
-        const int64_t p = base + i;
-        if (p < n) {
-            const int v = precision[p];
+        const int64_t i_seq = base + i;
+        if (i_seq < n) {
+            const int v = precision[order ? (int64_t)order[i_seq] : i_seq];
             local[0] += v == 4, local[1] += v == 6, local[2] += v == 8;
         }
     }
@@ -297,6 +315,7 @@ __global__ void group_scan_kernel(int* __restrict__ block_counts, int nblocks, i
 }
 
 __global__ void __launch_bounds__(256) group_scatter_kernel(int64_t n, const int* __restrict__ precision,
+                                                            const int* __restrict__ order,
                                                             const int* __restrict__ block_offsets, int nblocks,
                                                             int* __restrict__ ids) {
     __shared__ int warp_tot[3][8];
@@ -306,8 +325,9 @@ __global__ void __launch_bounds__(256) group_scatter_kernel(int64_t n, const int
     __syncthreads();
     const int64_t base = (int64_t)blockIdx.x * kCompactBlock;
     for (int i0 = 0; i0 < kCompactBlock; i0 += 256) {
-        const int64_t p = base + i0 + threadIdx.x;
-        const int v = p < n ? precision[p] : 0;
+        const int64_t i_seq = base + i0 + threadIdx.x;
+        const int64_t p = i_seq < n ? (order ? (int64_t)order[i_seq] : i_seq) : 0;
+        const int v = i_seq < n ? precision[p] : 0;
         unsigned m[3];
         for (int g = 0; g < 3; ++g) {
             m[g] = __ballot_sync(kFull, v == 4 + 2 * g);
@@ -337,10 +357,11 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 }  // namespace
 
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
-                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream) {
+                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream, bool atoms) {
     if (bits != 4 && bits != 6 && bits != 8) return fail(MXK_ERR_INVALID, "Precision must be 4, 6, or 8");
     if (rows <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && d % 32 == 0, "quantize_rows: d must be a positive multiple of 32");
+    MXK_REQUIRE(!atoms || d % 128 == 0, "quantize_rows: the scale-atom layout needs d % 128 == 0");
     MXK_REQUIRE(points && values && scales, "quantize_rows: null pointer");
     MXK_REQUIRE(aligned(points, 16), "quantize_rows: points must be 16-byte aligned");
     MXK_REQUIRE(aligned(values, bits == 8 ? 16 : (bits == 4 ? 8 : 4)),
@@ -352,9 +373,9 @@ int launch_quantize(int bits, int64_t rows, int d, const float* points, const in
     auto* out = static_cast<uint8_t*>(values);
     LaunchScope scope("quantize_mx", stream);
     switch (bits) {
-        case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
-        case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
-        default: quantize_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev); break;
+        case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
+        case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
+        default: quantize_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
     }
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
@@ -374,7 +395,8 @@ int launch_point_bounds(int64_t n, int d, const float* points, const float* norm
                         cudaStream_t stream) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && d % 32 == 0, "precompute_point_bounds: d must be a multiple of 32");
-    const int64_t blocks = (n * 32 + 255) / 256;
+    MXK_REQUIRE(reinterpret_cast<uintptr_t>(points) % 16 == 0, "precompute_point_bounds: points must be 16-byte aligned");
+    const int64_t blocks = (n + 255) / 256;
     LaunchScope scope("point_bounds", stream);
     point_bounds_kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, points, norms, upper);
     MXK_CUDA(cudaGetLastError());
@@ -401,14 +423,14 @@ int launch_centroid_stats(int k, const float* errors, const float* norms, float*
 
 int64_t compaction_scratch_ints(int64_t n) { return 3 * ((n + kCompactBlock - 1) / kCompactBlock) + 3; }
 
-int launch_group_compaction(int64_t n, const int* precision, int* ids, int* group_counts, int* scratch,
-                            cudaStream_t stream) {
+int launch_group_compaction(int64_t n, const int* precision, const int* order, int* ids, int* group_counts,
+                            int* scratch, cudaStream_t stream) {
     if (n <= 0) return MXK_OK;
     const int64_t nb = (n + kCompactBlock - 1) / kCompactBlock;
     MXK_REQUIRE(nb < (1ll << 31), "compaction: too many points");
     {
         LaunchScope scope("group_count", stream);
-        group_block_count_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, scratch, (int)nb);
+        group_block_count_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb);
         MXK_CUDA(cudaGetLastError());
     }
     {
@@ -418,7 +440,7 @@ int launch_group_compaction(int64_t n, const int* precision, int* ids, int* grou
     }
     {
         LaunchScope scope("group_scatter", stream);
-        group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, scratch, (int)nb, ids);
+        group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb, ids);
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;
@@ -435,7 +457,7 @@ int mxk_compute_l2_norm(int64_t rows, int d, const float* points, float* norms, 
 int mxk_quantize_rows(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
                       uint8_t* scales, float* max_errors, void* stream) {
     return mxk::launch_quantize(bits, rows, d, points, pid, values, scales, max_errors, nullptr,
-                                mxk::as_stream(stream));
+                                mxk::as_stream(stream), false);
 }
 
 int mxk_precompute_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,

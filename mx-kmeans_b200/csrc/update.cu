@@ -45,7 +45,8 @@ __device__ __forceinline__ bool bad_label(int lab, int k, unsigned* err) {
 
 template <int NJ>
 __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, int k, const float* __restrict__ points,
-                                                              const int* __restrict__ labels, float* __restrict__ sums,
+                                                              const int* __restrict__ labels,
+                                                              const int* __restrict__ order, float* __restrict__ sums,
                                                               int* __restrict__ counts, int64_t per_warp,
                                                               unsigned* __restrict__ err) {
     const int lane = threadIdx.x & 31;
@@ -58,7 +59,8 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
     int run = 0;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int64_t pnt = begin; pnt < end; ++pnt) {
+    for (int64_t i = begin; i < end; ++i) {
+        const int64_t pnt = order ? (int64_t)order[i] : i;
         const int lab = labels[pnt];
         if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
         if (lab != cur) {
@@ -91,7 +93,8 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
 // shared memory; one warp per point, float4 per lane.
 __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int d, int k,
                                                                  const float* __restrict__ points,
-                                                                 const int* __restrict__ labels, float* __restrict__ sums,
+                                                                 const int* __restrict__ labels,
+                                                                 const int* __restrict__ order, float* __restrict__ sums,
                                                                  int* __restrict__ counts, unsigned* __restrict__ err) {
     extern __shared__ float priv[];  // k*d sums, then k counts
     int* pcount = reinterpret_cast<int*>(priv + (int64_t)k * d);
@@ -101,7 +104,8 @@ __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int 
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int vec_per_row = d >> 2;
-    for (int64_t pnt = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); pnt < n; pnt += (int64_t)gridDim.x * warps) {
+    for (int64_t i = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); i < n; i += (int64_t)gridDim.x * warps) {
+        const int64_t pnt = order ? (int64_t)order[i] : i;
         const int lab = labels[pnt];
         if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
         const float* src = points + pnt * d;
@@ -206,8 +210,8 @@ constexpr int kShiftBlocks = 256;  // fixed grid of the shift reduction (<= part
 
 }  // namespace
 
-int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, float* sums, int* counts,
-                      cudaStream_t stream) {
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, float* sums,
+                      int* counts, cudaStream_t stream) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && k > 0 && points && labels && sums && counts, "update_centroids: bad arguments");
     const int sms = sm_count();
@@ -218,11 +222,15 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
     int max_smem = 0, dev = 0;
     MXK_CUDA(cudaGetDevice(&dev));
     MXK_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    if (aligned && d % 4 == 0 && priv_bytes <= max_smem && priv_bytes <= 200 * 1024 && n >= (int64_t)k * 64) {
+    // A label-sorted visiting order makes the run kernel's flushes rare, which
+    // beats per-element shared-memory atomics; without one, privatize when the
+    // sums fit in shared memory.
+    if (!order && aligned && d % 4 == 0 && priv_bytes <= max_smem && priv_bytes <= 200 * 1024 && n >= (int64_t)k * 64) {
         MXK_CUDA(cudaFuncSetAttribute(accumulate_private_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)priv_bytes));
         LaunchScope scope("accumulate_private", stream);
-        accumulate_private_kernel<<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, sums, counts, err);
+        accumulate_private_kernel<<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, order, sums, counts,
+                                                                             err);
         MXK_CUDA(cudaGetLastError());
         return MXK_OK;
     }
@@ -235,7 +243,9 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
         LaunchScope scope("accumulate_runs", stream);
         switch (d / 128) {
 #define MXK_ACC_CASE(J) \
-    case J: accumulate_runs_kernel<J><<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, per_warp, err); break;
+    case J: accumulate_runs_kernel<J><<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, order, sums, counts, \
+                                                                       per_warp, err);                              \
+        break;
             MXK_ACC_CASE(1) MXK_ACC_CASE(2) MXK_ACC_CASE(3) MXK_ACC_CASE(4) MXK_ACC_CASE(5) MXK_ACC_CASE(6)
             MXK_ACC_CASE(7) MXK_ACC_CASE(8)
 #undef MXK_ACC_CASE
@@ -297,7 +307,7 @@ int mxk_update_centroids(int64_t n, int d, int k, const float* points, const int
     MXK_REQUIRE(centroids != old_centroids, "update_centroids: centroids and old_centroids must differ");
     MXK_CUDA(cudaMemsetAsync(centroids, 0, sizeof(float) * (size_t)k * d, s));
     MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * (size_t)k, s));
-    MXK_CHECK(mxk::launch_accumulate(n, d, k, points, labels, centroids, counts, s));
+    MXK_CHECK(mxk::launch_accumulate(n, d, k, points, labels, nullptr, centroids, counts, s));
     MXK_CHECK(mxk::launch_finalize(d, k, centroids, counts, old_centroids, centroids, nullptr, s));
     // Reports labels outside [0, k) (skipped above) instead of writing past the
     // sums as an unchecked index would.

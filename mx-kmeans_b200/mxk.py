@@ -57,7 +57,7 @@ SIGNATURES = {
     "mxk_update_centroids": ([_I64, _I, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_centroid_shift": ([_I64, _P, _P, _P, _P, _P], _I),
     "mxk_centroid_shift_noalloc": ([_I64, _P, _P, _P, _P, _P], _I),
-    "mxk_assign_mx_fused": ([_I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "mxk_assign_mx_fused": ([_I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_kmeans_mixed": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_comm_unique_id": ([ctypes.c_char_p], _I),
     "mxk_comm_init": ([ctypes.POINTER(_P), _I, _I, ctypes.c_char_p], _I),
@@ -146,10 +146,10 @@ def assign_clusters(rows, k, point_norms, centroid_norms, dots, labels, gaps, pi
 
 
 def assign_mx_fused(bits, rows, k, d, a, a_scales, b, b_scales, point_norms, centroid_norms, labels, gaps=None,
-                    pid=None, stream=None):
+                    pid=None, start_hint=None, stream=None):
     check(load().mxk_assign_mx_fused(bits, rows, k, d, _ptr(a), _ptr(a_scales), _ptr(b), _ptr(b_scales),
                                      _ptr(point_norms), _ptr(centroid_norms), _ptr(pid), _ptr(labels), _ptr(gaps),
-                                     _stream(stream)))
+                                     _ptr(start_hint), _stream(stream)))
 
 
 def update_centroids(points, labels, old_centroids, centroids, counts, stream=None):

@@ -129,3 +129,79 @@ def test_empty_and_tiny(torch_cuda, mxk, orc):
         mxk.gemm_mx(8, 4, 4, 96, torch.zeros(512, dtype=torch.uint8, device="cuda:0"),
                     torch.zeros(16, dtype=torch.uint8, device="cuda:0"), torch.zeros(512, dtype=torch.uint8, device="cuda:0"),
                     torch.zeros(16, dtype=torch.uint8, device="cuda:0"), torch.zeros(16, device="cuda:0"))
+
+
+@pytest.mark.parametrize("k", [136, 1000, 9000])
+def test_fused_ties_and_tails(torch_cuda, mxk, orc, k):
+    """Duplicated centroids (exact distance ties inside a 32-column chunk, across
+    the four column quarters and across 128-column tiles) must resolve to the
+    lowest index like assign_clusters; k not a multiple of 32/128 exercises the
+    tail path; k > 8192 reads the centroid norms from global memory."""
+    torch = torch_cuda
+    n, d = 3000, 128
+    g = np.random.default_rng(k)
+    c = (g.standard_normal((k, d)) * 2).astype(np.float32)
+    for dup in [(3, 7), (5, 40), (17, 100), (2, 131), (60, k - 1)]:
+        if dup[1] < k:
+            c[dup[1]] = c[dup[0]]
+    x = c[g.integers(0, k, n)] + 0.01 * g.standard_normal((n, d)).astype(np.float32)
+    x[:50] = c[7]  # exactly on a duplicated centroid
+    xv, xs = _quantized(orc, 8, x.astype(np.float32))
+    cv, cs = _quantized(orc, 8, c)
+    pn, cn = _norms(torch, mxk, x.astype(np.float32)), _norms(torch, mxk, c)
+    X, XS, C, CS = _to(torch, xv), _to(torch, xs), _to(torch, cv), _to(torch, cs)
+    dots = torch.empty((n, k), dtype=torch.float32, device="cuda:0")
+    mxk.gemm_mx(8, n, k, d, X, XS, C, CS, dots)
+    lab_dense = torch.empty(n, dtype=torch.int32, device="cuda:0")
+    gap_dense = torch.empty(n, dtype=torch.float32, device="cuda:0")
+    mxk.assign_clusters(n, k, pn, cn, dots, lab_dense, gap_dense)
+    lab_f = torch.empty(n, dtype=torch.int32, device="cuda:0")
+    gap_f = torch.empty(n, dtype=torch.float32, device="cuda:0")
+    mxk.assign_mx_fused(8, n, k, d, X, XS, C, CS, pn, cn, lab_f, gap_f)
+    lab_ng = torch.empty(n, dtype=torch.int32, device="cuda:0")
+    perm = torch.from_numpy(g.permutation(n).astype(np.int32)).to("cuda:0")
+    # with a pid permutation the labels land at pid[row]; rows are then the
+    # permuted points, so feed the permuted quantized rows
+    Xp, XSp = X.view(n, d)[perm.long()].contiguous(), XS.view(n, d // 32)[perm.long()].contiguous()
+    mxk.assign_mx_fused(8, n, k, d, Xp, XSp, C, CS, pn, cn, lab_ng, None, pid=perm)
+    torch.cuda.synchronize()
+    assert torch.equal(lab_f, lab_dense)
+    assert torch.equal(gap_f, gap_dense)
+    assert torch.equal(lab_ng, lab_dense)
+    assert np.all(lab_dense.cpu().numpy()[:50] == 3)
+
+
+def test_start_hint_does_not_change_results(torch_cuda, mxk, orc):
+    """Labels and gaps are the same whatever tile the centroid sweep starts at:
+    random hints, hints equal to the true labels, and no hint, on data with exact
+    ties (duplicated centroids in different 128-centroid tiles)."""
+    torch = torch_cuda
+    n, d, k = 4000, 128, 640
+    g = np.random.default_rng(5)
+    c = (g.standard_normal((k, d)) * 2).astype(np.float32)
+    c[600:] = c[:40]
+    c[300:310] = c[10:20]
+    x = c[g.integers(0, k, n)] + 0.05 * g.standard_normal((n, d)).astype(np.float32)
+    x[:200] = c[15]
+    xv, xs = _quantized(orc, 8, x.astype(np.float32))
+    cv, cs = _quantized(orc, 8, c)
+    pn, cn = _norms(torch, mxk, x.astype(np.float32)), _norms(torch, mxk, c)
+    X, XS, C, CS = _to(torch, xv), _to(torch, xs), _to(torch, cv), _to(torch, cs)
+    ref_l = torch.empty(n, dtype=torch.int32, device="cuda:0")
+    ref_g = torch.empty(n, dtype=torch.float32, device="cuda:0")
+    mxk.assign_mx_fused(8, n, k, d, X, XS, C, CS, pn, cn, ref_l, ref_g)
+    torch.cuda.synchronize()
+    hints = [torch.from_numpy(g.integers(0, k, n).astype(np.int32)).cuda(),
+             ref_l.clone(),
+             torch.full((n,), k - 1, dtype=torch.int32, device="cuda:0"),
+             torch.full((n,), -7, dtype=torch.int32, device="cuda:0")]
+    for hint in hints:
+        lab = torch.empty(n, dtype=torch.int32, device="cuda:0")
+        gap = torch.empty(n, dtype=torch.float32, device="cuda:0")
+        mxk.assign_mx_fused(8, n, k, d, X, XS, C, CS, pn, cn, lab, gap, start_hint=hint)
+        lab2 = torch.empty(n, dtype=torch.int32, device="cuda:0")
+        mxk.assign_mx_fused(8, n, k, d, X, XS, C, CS, pn, cn, lab2, None, start_hint=hint)
+        torch.cuda.synchronize()
+        assert torch.equal(lab, ref_l) and torch.equal(lab2, ref_l)
+        assert torch.equal(gap, ref_g)
+    assert np.all(ref_l.cpu().numpy()[:200] == 15)

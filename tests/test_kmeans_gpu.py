@@ -97,3 +97,25 @@ def test_rejects_unpadded_d(torch_cuda, mxk):
     torch = torch_cuda
     with pytest.raises(ValueError):
         _run(torch, mxk, np.zeros((8, 96), np.float32), np.zeros((4, 96), np.float32), max_iterations=1)
+
+
+def test_duplicate_centroids_keep_lowest_index(torch_cuda, mxk, orc):
+    """Exact distance ties between duplicated centroids resolve to the lowest
+    index in every iteration, including the ones whose sweep over centroid tiles
+    starts at the previous label's tile.  Integer-valued clusters whose points sit
+    exactly on their centers keep every mean exact, so duplicates stay duplicates."""
+    torch = torch_cuda
+    n_per, d, k = 40, 128, 256
+    g = np.random.default_rng(21)
+    base = g.integers(-8, 9, size=(200, d)).astype(np.float32)
+    x = np.repeat(base, n_per, axis=0)
+    x = x[g.permutation(len(x))]
+    c0 = np.zeros((k, d), np.float32)
+    c0[:200] = base
+    c0[200:] = base[:56]          # duplicates with higher indices (other centroid tile)
+    c0[137] = base[5]             # and one inside the second tile
+    it, cg, lg = _run(torch, mxk, x, c0, max_iterations=3, tolerance=0.0)
+    assert not np.any(lg >= 200), "a tie went to the higher duplicate index"
+    assert not np.any(lg == 137)
+    it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=3, tolerance=0.0)
+    assert np.array_equal(lg, lo)
