@@ -116,6 +116,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// Non-blocking test of an mbarrier phase (never suspends).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (after flagging the error
 // word and the CTA-wide abort flag) if the phase does not complete in time or
 // another thread of the CTA has already aborted.
@@ -132,6 +145,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             return false;
         }
     }
+}
+
+// mbar_wait for a phase that has usually completed already: a non-suspending
+// test first (cheaper for a single issuing thread), then the bounded wait.
+__device__ __forceinline__ bool mbar_wait_lean(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned* err_word) {
+    if (mbar_test(bar, parity)) return true;
+    return mbar_wait(bar, parity, abort_flag, err_word);
 }
 
 // 2D tiled TMA load (global -> shared), completion signalled on `bar`.
@@ -272,6 +293,8 @@ __host__ __device__ constexpr uint32_t mx_idesc(uint32_t a_fmt, uint32_t b_fmt, 
     return (sf_id << 4) | (a_fmt << 7) | (b_fmt << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24) |
            (sf_id << 29);
 }
+// The scale-factor selector bits of an instruction descriptor (A and B byte sf_id).
+__host__ __device__ constexpr uint32_t mx_idesc_sf(uint32_t sf_id) { return (sf_id << 4) | (sf_id << 29); }
 constexpr uint32_t kFmtE4M3 = 0;
 
 }  // namespace mxk::dev

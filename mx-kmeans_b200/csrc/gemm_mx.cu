@@ -10,7 +10,7 @@
 // a dense store (gemm_mx API) or, fused, the distance fmaf(-2,dot,pn+cn) and the
 // lowest-index argmin (+ optional two-largest gap) so that no N x K buffer exists.
 //
-// Structure (one persistent CTA per SM, 320 threads):
+// Structure (one persistent CTA per SM, 448 threads):
 //   warp 0      producer: TMA (SWIZZLE_128B) of a 128-row point tile (all K,
 //               resident while every centroid tile streams past) and of 128-row
 //               x 128-byte centroid chunks through a ring as deep as shared
@@ -19,13 +19,20 @@
 //               row-major API scales are converted once per call).
 //   warp 1      TMEM allocator and the single MMA-issuing thread: tcgen05.cp of
 //               the scale atoms into TMEM, tcgen05.mma kind::mxf8f6f4
-//               block_scale (M=128, N=128, K=32) into a double-buffered TMEM
-//               accumulator, tcgen05.commit to release smem stages / publish tiles.
-//   warps 2-17  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lane
-//               quadrant w%4, 32-column quarter (w-2)/4), then dense store or
-//               argmin: packed f32x2 distances, a 3-input-min tree per 32
-//               columns and an index search only when that chunk improves the
-//               row's running minimum.
+//               block_scale (M=128, N=128, K=32) into a three-stage TMEM
+//               accumulator ring (columns 0-383; scales in 384-451), one
+//               tcgen05.commit per tile.
+//   warps 2-13  epilogue, one warp per (TMEM lane quadrant w%4, accumulator
+//               stage (w-2)/4): each drains every third 128-column tile for its
+//               32 rows, then dense store or argmin: packed f32x2 distances, a
+//               3-input-min tree per 32 columns and an index search only when a
+//               32-column chunk can change the row's running minimum.  The warp
+//               that drains a row tile's first (hinted) centroid tile publishes
+//               its per-row minimum to the other two warps of its quadrant, so
+//               that they too start from the likely winner and rarely search;
+//               the warp that drains the last tile merges the three partial
+//               results and writes the label.  The quadrant-0 warp of a stage
+//               also frees the tile's centroid-ring slots once the tile is full.
 #include <cstring>
 
 #include "common.cuh"
@@ -35,20 +42,27 @@
 namespace mxk {
 namespace {
 
-constexpr int kBM = 128;           // points per tile = TMEM lanes
-constexpr int kBN = 128;           // centroids per accumulator tile
-constexpr int kChunk = 128;        // K bytes per chunk = one SWIZZLE_128B row
-constexpr int kTileBytes = kBM * kChunk;  // 16 KB
-constexpr int kSfAtom = 512;       // 128 rows x 4 scale bytes
-constexpr int kMaxBStages = 12;   // centroid-chunk ring depth: as many as shared memory holds
-constexpr int kAccStages = 2;
-constexpr int kEpiWarps = 16;     // 4 per TMEM lane quadrant, one 32-column quarter each
+constexpr int kBM = kPointTileRows;      // points per tile = TMEM lanes
+constexpr int kBN = kCentroidTileRows;   // centroids per accumulator tile (MMA N)
+constexpr int kChunk = 128;              // K bytes per chunk = one SWIZZLE_128B row
+constexpr int kATileBytes = kBM * kChunk;   // 16 KB
+constexpr int kBTileBytes = kBN * kChunk;   // 24 KB
+constexpr int kSfAtom = 512;             // 128 rows x 4 scale bytes
+constexpr int kBAtoms = (kBN + 127) / 128;  // scale atoms per centroid-tile chunk
+constexpr int kMaxBStages = 12;          // centroid-chunk ring depth: as many as shared memory holds
+constexpr int kAccStages = 2;            // 2 x 192 accumulator columns
+constexpr int kEpiPerQuad = 3;           // epilogue warps per TMEM lane quadrant
+constexpr int kSliceCols = kBN / kEpiPerQuad;  // 64 accumulator columns per epilogue warp
+constexpr int kEpiWarps = 4 * kEpiPerQuad;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-constexpr int kMaxSmemNorms = 8192;  // centroid norms staged in shared memory up to this k
-constexpr int kMaxChunks = 8;      // K <= 1024
+constexpr int kMaxSmemNorms = 8192;      // centroid norms staged in shared memory up to this k
+constexpr int kMaxChunks = 8;            // K <= 1024
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfaCol = 256;  // 4 columns per K chunk
-constexpr uint32_t kSfbCol = 320;
+constexpr uint32_t kSfaCol = kAccStages * kBN;  // 384: 4 columns per K chunk (<= 32)
+constexpr uint32_t kSfbCol = kSfaCol + 64;       // 448: 4 columns per scale atom
+constexpr int kNumBars = 64;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
+static_assert(kSliceCols == 64 && kBN % 32 == 0, "each epilogue warp drains two 32-column chunks");
+static_assert(kSfbCol + 4 * kBAtoms <= kTmemCols, "TMEM budget");
 
 struct GemmParams {
     int64_t m;
@@ -65,6 +79,8 @@ struct GemmParams {
     int out_vec;  // out is 16-byte aligned and n % 4 == 0 (vector stores)
     int cn_smem;  // number of centroid norms staged in shared memory (0 = read from global)
     int b_stages; // depth of the centroid-chunk ring (<= kMaxBStages)
+    int epi_release;  // ring slots are freed by the epilogue per tile (ring holds >= 2 tiles),
+                      // else by the MMA thread per chunk
     const float* pn;
     const float* cn;
     const int* pid;
@@ -74,21 +90,33 @@ struct GemmParams {
     unsigned* err;
 };
 
+// Position in a ring of n slots whose use count crosses a phase every n uses.
+struct RingPos {
+    int slot;
+    uint32_t phase;
+    int n;
+    __device__ __forceinline__ void advance(int k) {
+        slot += k;
+        while (slot >= n) slot -= n, phase ^= 1u;
+    }
+};
+
 struct SmemLayout {
-    uint32_t a_off, b_off, sfa_off, sfb_off, merge_off, cn_off, bar_off, total;
+    uint32_t a_off, b_off, sfa_off, sfb_off, merge_off, seed_off, cn_off, bar_off, total;
 };
 
 // cn_floats: centroid norms staged in shared memory (0 when read from global).
 __host__ __device__ inline SmemLayout smem_layout(int kchunks, int a_stages, int cn_floats, int b_stages) {
     SmemLayout s;
-    s.a_off = 0;
-    s.b_off = s.a_off + a_stages * kchunks * kTileBytes;
-    s.sfa_off = s.b_off + b_stages * kTileBytes;
+    s.a_off = 0;  // every operand tile starts on a 1024-byte boundary (SWIZZLE_128B atoms)
+    s.b_off = s.a_off + a_stages * kchunks * kATileBytes;
+    s.sfa_off = s.b_off + b_stages * kBTileBytes;
     s.sfb_off = s.sfa_off + a_stages * kchunks * kSfAtom;
-    s.merge_off = s.sfb_off + b_stages * kSfAtom;                  // 3 quarters x 128 rows x 16 B
-    s.cn_off = s.merge_off + 3 * kBM * 16;
+    s.merge_off = s.sfb_off + b_stages * kBAtoms * kSfAtom;  // [2 buffers][2 depositors][128 rows] x 16 B
+    s.seed_off = s.merge_off + 2 * 2 * kBM * 16;              // [2 buffers][3 warps][128 rows] x 8 B
+    s.cn_off = s.seed_off + 2 * kEpiPerQuad * kBM * 8;
     s.bar_off = s.cn_off + (uint32_t)((cn_floats * 4 + 15) / 16 * 16);
-    s.total = s.bar_off + 40 * 8 + 64;  // 4 + 2*12 + 2*2 + 3 barriers, then the TMEM slot
+    s.total = s.bar_off + kNumBars * 8 + 64;
     return s;
 }
 
@@ -131,21 +159,27 @@ __device__ void fill_a_subbyte(uint8_t* dst, const GemmParams& p, int64_t row0, 
     }
 }
 
-// Row-major scales [rows][k/32] -> tcgen05 scale atoms: one 512-byte atom per
-// (128-row tile, 128-feature chunk), tile-major, row r's four block scales at
-// (r % 32) * 16 + (r / 32) * 4 + block % 4; rows past `rows` get 0 (2^-127).
-__global__ void __launch_bounds__(256) scales_to_atoms_kernel(int64_t rows, int kchunks, const uint8_t* __restrict__ src,
+// Row-major scales [rows][k/32] -> tcgen05 scale atoms for tiles of tile_rows
+// rows: ceil(tile_rows / 128) 512-byte atoms per (tile, 128-feature chunk),
+// tile-major, slice row r's four block scales at (r % 32) * 16 + (r / 32) * 4 +
+// block % 4; rows past `rows` (and slice rows past the tile) get 0 (2^-127).
+__global__ void __launch_bounds__(256) scales_to_atoms_kernel(int64_t rows, int kchunks, int tile_rows,
+                                                              const uint8_t* __restrict__ src,
                                                               uint8_t* __restrict__ atoms, int64_t n_words) {
+    const int per_tile = (tile_rows + 127) >> 7;
     for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < n_words; w += (int64_t)gridDim.x * blockDim.x) {
-        // word w = atom a, 32-bit slot (lane l, row group i): rows r = l + 32 i
+        // word w = atom a, 32-bit slot (lane l, row group i): slice rows r = l + 32 i
         const int64_t a = w >> 7;
         const int slot = (int)(w & 127);
         const int l = slot >> 2, i = slot & 3;
-        const int64_t tile = a / kchunks;
-        const int kc = (int)(a - tile * kchunks);
-        const int64_t row = tile * 128 + l + 32 * i;
+        const int64_t tk = a / per_tile;  // (tile, chunk) pair
+        const int slice = (int)(a - tk * per_tile);
+        const int64_t tile = tk / kchunks;
+        const int kc = (int)(tk - tile * kchunks);
+        const int rr = slice * 128 + l + 32 * i;
+        const int64_t row = tile * tile_rows + rr;
         uint32_t v = 0;
-        if (row < rows) v = *reinterpret_cast<const uint32_t*>(src + row * (int64_t)kchunks * 4 + 4 * kc);
+        if (rr < tile_rows && row < rows) v = *reinterpret_cast<const uint32_t*>(src + row * (int64_t)kchunks * 4 + 4 * kc);
         reinterpret_cast<uint32_t*>(atoms)[w] = v;
     }
 }
@@ -165,6 +199,86 @@ __device__ __forceinline__ int sweep_start(const GemmParams& p, int64_t tile, in
     return lab / kBN;
 }
 
+// Running (distance, index) minimum and two largest distances of one row.
+struct RowMin {
+    float first, largest, next;
+    int best;
+};
+
+// Folds 32 consecutive columns c0..c0+31 (all < n) of one row into `m`:
+// distances fmaf(-2, dot, pn + cn) two at a time (add/fma .f32x2, each lane
+// rounded exactly like the scalar operations), a 3-input-min tree, and an index
+// search only when the chunk minimum can change the running minimum (smaller,
+// or equal, resolved by the lower index as insert_distance does).  NaN
+// distances never compare, as in the reference.
+template <bool kGaps>
+__device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const float* cn, uint64_t pn2, int c0,
+                                               RowMin& m) {
+    float dist[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 cv = *reinterpret_cast<const float4*>(cn + j);
+        dev::dist2(v[j], v[j + 1], pn2, cv.x, cv.y, dist[j], dist[j + 1]);
+        dev::dist2(v[j + 2], v[j + 3], pn2, cv.z, cv.w, dist[j + 2], dist[j + 3]);
+    }
+    if constexpr (kGaps) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            m.next = fmaxf(m.next, fminf(m.largest, dist[j]));
+            m.largest = fmaxf(m.largest, dist[j]);
+        }
+    }
+    float m3[11];
+#pragma unroll
+    for (int t = 0; t < 10; ++t) m3[t] = dev::min3f(dist[3 * t], dist[3 * t + 1], dist[3 * t + 2]);
+    m3[10] = fminf(dist[30], dist[31]);
+    const float ma = dev::min3f(m3[0], m3[1], m3[2]);
+    const float mb = dev::min3f(m3[3], m3[4], m3[5]);
+    const float mc = dev::min3f(m3[6], m3[7], m3[8]);
+    const float cm = fminf(dev::min3f(ma, mb, mc), fminf(m3[9], m3[10]));
+    if (cm <= m.first) {
+        int idx = 31;
+#pragma unroll
+        for (int j = 30; j >= 0; --j) idx = dist[j] == cm ? j : idx;
+        const int cand = c0 + idx;
+        if (cm < m.first || cand < m.best) {
+            m.first = cm;
+            m.best = cand;
+        }
+    }
+}
+
+// Columns c0.. of a 32-column chunk that runs past n: one column at a time.
+template <bool kGaps>
+__device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const float* cn, float pn, int c0, int64_t n,
+                                            RowMin& m) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (c0 + j < n) {
+            const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cn[j]);
+            if (dist < m.first || (dist == m.first && c0 + j < m.best)) {
+                m.first = dist;
+                m.best = c0 + j;
+            }
+            if constexpr (kGaps) {
+                m.next = fmaxf(m.next, fminf(m.largest, dist));
+                m.largest = fmaxf(m.largest, dist);
+            }
+        }
+    }
+}
+
+// Lexicographic (distance, index) minimum and two-largest merge of a partial
+// result (d, b, l, nx) into m.
+template <bool kGaps>
+__device__ __forceinline__ void merge_rowmin(RowMin& m, float d, int b, float l, float nx) {
+    if (d < m.first || (d == m.first && b < m.best)) m.first = d, m.best = b;
+    if constexpr (kGaps) {
+        m.next = fmaxf(fminf(m.largest, l), fmaxf(m.next, nx));
+        m.largest = fmaxf(m.largest, l);
+    }
+}
+
 template <bool kArgmin, bool kGaps>
 __global__ void __launch_bounds__(kThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -174,17 +288,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages);
     const int kBStages = p.b_stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-    uint64_t* a_full = bars;                // [2]
-    uint64_t* a_empty = bars + 2;           // [2]
-    uint64_t* b_full = bars + 4;            // [kMaxBStages]
+    uint64_t* a_full = bars;                 // [2]
+    uint64_t* a_empty = bars + 2;            // [2]
+    uint64_t* b_full = bars + 4;             // [kMaxBStages]
     uint64_t* b_empty = bars + 4 + kMaxBStages;
-    uint64_t* acc_full = bars + 4 + 2 * kMaxBStages;
+    uint64_t* acc_full = bars + 4 + 2 * kMaxBStages;  // [kAccStages]
     uint64_t* acc_empty = acc_full + kAccStages;
     uint64_t* drain = acc_empty + kAccStages;
-    uint64_t* merge_full = drain + 1;   // column-half hand-off of the argmin epilogue
-    uint64_t* merge_empty = drain + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 40) + 1;
+    uint64_t* merge_full = drain + 1;        // [q * 2 + row-tile parity] two depositing warps -> merging warp
+    uint64_t* merge_empty = merge_full + 8;  // [q * 2 + row-tile parity] merging warp has read the deposits
+    uint64_t* seed_bar = merge_empty + 8;    // [q] the quadrant's three first-tile minima are published
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
+    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 <= kNumBars, "barrier slots");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mrows = p.m_dev ? (int64_t)*p.m_dev : p.m;
@@ -194,10 +310,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) dev::mbar_init(&a_full[i], 1), dev::mbar_init(&a_empty[i], 1);
         for (int i = 0; i < kBStages; ++i) dev::mbar_init(&b_full[i], 1), dev::mbar_init(&b_empty[i], 1);
-        for (int i = 0; i < kAccStages; ++i) dev::mbar_init(&acc_full[i], 1), dev::mbar_init(&acc_empty[i], kEpiWarps);
+        for (int i = 0; i < kAccStages; ++i)
+            dev::mbar_init(&acc_full[i], 1), dev::mbar_init(&acc_empty[i], kEpiWarps);
         dev::mbar_init(drain, 1);
-        dev::mbar_init(merge_full, 3 * kEpiWarps / 4);   // quarters 1..3 deposit
-        dev::mbar_init(merge_empty, kEpiWarps / 4);      // quarter 0 has read
+        for (int i = 0; i < 8; ++i) {
+            dev::mbar_init(&merge_full[i], kEpiPerQuad - 1);
+            dev::mbar_init(&merge_empty[i], 1);
+        }
+        for (int q = 0; q < 4; ++q) dev::mbar_init(&seed_bar[q], kEpiPerQuad);
         *abort_flag = 0;
         dev::fence_barrier_init();
     }
@@ -217,103 +337,121 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        uint32_t bcount = 0;
+        RingPos bring{0, 0u, kBStages};
+        uint32_t issued = 0;
         int it = 0;
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
             if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
-            uint8_t* a_smem = smem + L.a_off + (uint32_t)as * p.kchunks * kTileBytes;
+            uint8_t* a_smem = smem + L.a_off + (uint32_t)as * p.kchunks * kATileBytes;
             uint8_t* sfa = smem + L.sfa_off + (uint32_t)as * p.kchunks * kSfAtom;
             if (lane == 0) {
-                const uint32_t bytes = (p.a_bits == 8 ? p.kchunks * kTileBytes : 0) + p.kchunks * kSfAtom;
+                const uint32_t bytes = (p.a_bits == 8 ? p.kchunks * kATileBytes : 0) + p.kchunks * kSfAtom;
                 if (bytes)
                     asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(dev::smem_addr(&a_full[as])),
                                  "r"(bytes));
                 if (p.a_bits == 8)
                     for (int kc = 0; kc < p.kchunks; ++kc)
-                        dev::tma_load_2d(a_smem + kc * kTileBytes, &tmap_a, kc * kChunk, (int32_t)(tile * kBM), &a_full[as]);
+                        dev::tma_load_2d(a_smem + kc * kATileBytes, &tmap_a, kc * kChunk, (int32_t)(tile * kBM),
+                                         &a_full[as]);
                 dev::bulk_load(sfa, p.a_scales + tile * p.kchunks * kSfAtom, (uint32_t)(p.kchunks * kSfAtom),
                                &a_full[as]);
             }
             if (p.a_bits != 8)
                 for (int kc = 0; kc < p.kchunks; ++kc)
-                    fill_a_subbyte(a_smem + kc * kTileBytes, p, tile * kBM, kc, mrows, lane);
+                    fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
             dev::fence_proxy_async();
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&a_full[as]);
-            const int ct0 = sweep_start(p, tile, mrows, tiles_n);
-            for (int i = 0; i < tiles_n && ok; ++i) {
-                const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
-                for (int kc = 0; kc < p.kchunks; ++kc, ++bcount) {
-                    const int bs = (int)(bcount % kBStages);
-                    const uint32_t bph = (bcount / kBStages) & 1u;
-                    if (!dev::mbar_wait(&b_empty[bs], bph ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                    if (lane == 0) {
-                        asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(dev::smem_addr(&b_full[bs])),
-                                     "r"((uint32_t)(kTileBytes + kSfAtom)));
-                        dev::tma_load_2d(smem + L.b_off + bs * kTileBytes, &tmap_b, kc * kChunk, ct * kBN, &b_full[bs]);
-                        dev::bulk_load(smem + L.sfb_off + bs * kSfAtom,
-                                       p.b_scales + ((int64_t)ct * p.kchunks + kc) * kSfAtom, kSfAtom, &b_full[bs]);
+            // Centroid chunks: one thread walks the ring.  A slot is handed back by
+            // the epilogue once the tile that read it has completed, or by the MMA
+            // thread's per-chunk commit when the ring holds less than two tiles.
+            if (lane == 0) {
+                const int ct0 = sweep_start(p, tile, mrows, tiles_n);
+                for (int i = 0; i < tiles_n && ok; ++i) {
+                    const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
+                    for (int kc = 0; kc < p.kchunks; ++kc) {
+                        if (!dev::mbar_wait(&b_empty[bring.slot], bring.phase ^ 1u, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        uint64_t* full = &b_full[bring.slot];
+                        dev::mbar_arrive_expect_tx(full, (uint32_t)(kBTileBytes + kBAtoms * kSfAtom));
+                        dev::tma_load_2d(smem + L.b_off + bring.slot * kBTileBytes, &tmap_b, kc * kChunk, ct * kBN,
+                                         full);
+                        dev::bulk_load(smem + L.sfb_off + bring.slot * kBAtoms * kSfAtom,
+                                       p.b_scales + ((int64_t)ct * p.kchunks + kc) * kBAtoms * kSfAtom,
+                                       kBAtoms * kSfAtom, full);
+                        ++issued;
+                        bring.advance(1);
                     }
-                    __syncwarp();
-                    if (lane == 0) dev::mbar_arrive(&b_full[bs]);
                 }
             }
+            ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
         }
         // Unwinding after an abort: wait (bounded) for the copies this warp
         // issued, so no TMA write lands in shared memory after the CTA exits.
         if (!ok && lane == 0) {
             volatile int no_abort = 0;
-            for (uint32_t c = bcount > kBStages ? bcount - kBStages : 0; c < bcount; ++c)
+            for (uint32_t c = issued > (uint32_t)kBStages ? issued - kBStages : 0; c < issued; ++c)
                 dev::mbar_wait(&b_full[c % kBStages], (c / kBStages) & 1u, &no_abort, nullptr);
             for (int j = it > p.a_stages ? it - p.a_stages : 0; j <= it; ++j)
                 dev::mbar_wait(&a_full[j % p.a_stages], (uint32_t)(j / p.a_stages) & 1u, &no_abort, nullptr);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // One thread issues every MMA (tcgen05.mma streams issued by two threads
+        // at once gave wrong products on B200).  Its own instruction latency --
+        // about 80 cycles per MMA and 250 per commit, the same for any N -- is
+        // what limits a tile, hence the wide 192-column tiles, one commit per
+        // tile, ring positions advanced incrementally and completed barriers
+        // detected with a non-suspending test first.
         if (lane == 0) {
-            uint32_t bcount = 0, acount = 0;
+            RingPos brd{0, 0u, kBStages};
+            int s = 0;           // accumulator stage of tile a = a % 2
+            uint32_t sph = 0;    // (a / 2) & 1
             int it = 0;
             bool ok = true;
+            const uint32_t idesc0 = dev::mx_idesc(dev::kFmtE4M3, dev::kFmtE4M3, kBM, kBN, 0);
             for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
-                const int as = it % p.a_stages;
-                const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
-                if (!dev::mbar_wait(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
+                const int as = p.a_stages == 2 ? (it & 1) : 0;
+                const uint32_t aph = (uint32_t)(p.a_stages == 2 ? (it >> 1) : it) & 1u;
+                if (!dev::mbar_wait_lean(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
                 dev::tc_fence_after();
-                const uint32_t a_base = dev::smem_addr(smem + L.a_off + (uint32_t)as * p.kchunks * kTileBytes);
+                const uint32_t a_base = dev::smem_addr(smem + L.a_off + (uint32_t)as * p.kchunks * kATileBytes);
                 const uint32_t sfa_base = dev::smem_addr(smem + L.sfa_off + (uint32_t)as * p.kchunks * kSfAtom);
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     dev::tc_copy_32x128b_x4(tmem + kSfaCol + 4 * kc,
                                             dev::smem_desc(sfa_base + kc * kSfAtom, 16, 128, dev::kLayoutNone));
-                for (int ct = 0; ct < tiles_n && ok; ++ct, ++acount) {
-                    const int accs = (int)(acount % kAccStages);
-                    const uint32_t accph = (acount / kAccStages) & 1u;
-                    if (!dev::mbar_wait(&acc_empty[accs], accph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                const uint64_t adesc0 = dev::smem_desc(a_base, 16, 1024, dev::kLayoutSwizzle128);
+                for (int i = 0; i < tiles_n && ok; ++i) {
+                    if (!dev::mbar_wait_lean(&acc_empty[s], sph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     dev::tc_fence_after();
-                    const uint32_t d_tmem = tmem + accs * kBN;
-                    for (int kc = 0; kc < p.kchunks; ++kc, ++bcount) {
-                        const int bs = (int)(bcount % kBStages);
-                        const uint32_t bph = (bcount / kBStages) & 1u;
-                        if (!dev::mbar_wait(&b_full[bs], bph, abort_flag, p.err)) { ok = false; break; }
-                        dev::tc_fence_after();
-                        const uint32_t b_addr = dev::smem_addr(smem + L.b_off + bs * kTileBytes);
-                        dev::tc_copy_32x128b_x4(tmem + kSfbCol,
-                                                dev::smem_desc(dev::smem_addr(smem + L.sfb_off + bs * kSfAtom), 16, 128,
-                                                               dev::kLayoutNone));
+                    const uint32_t d_tmem = tmem + (uint32_t)s * kBN;
+                    for (int kc = 0; kc < p.kchunks; ++kc) {
+                        if (!dev::mbar_wait_lean(&b_full[brd.slot], brd.phase, abort_flag, p.err)) { ok = false; break; }
+                        const uint32_t sfb = dev::smem_addr(smem + L.sfb_off + brd.slot * kBAtoms * kSfAtom);
 #pragma unroll
-                        for (int kb = 0; kb < 4; ++kb) {
-                            const uint64_t adesc =
-                                dev::smem_desc(a_base + kc * kTileBytes + kb * 32, 16, 1024, dev::kLayoutSwizzle128);
-                            const uint64_t bdesc = dev::smem_desc(b_addr + kb * 32, 16, 1024, dev::kLayoutSwizzle128);
-                            const uint32_t idesc = dev::mx_idesc(dev::kFmtE4M3, dev::kFmtE4M3, kBM, kBN, (uint32_t)kb);
-                            dev::tc_mma_mx(d_tmem, adesc, bdesc, idesc, (tmem + kSfaCol + 4 * kc) | ((uint32_t)kb << 30),
+                        for (int t = 0; t < kBAtoms; ++t)
+                            dev::tc_copy_32x128b_x4(tmem + kSfbCol + 4 * t,
+                                                    dev::smem_desc(sfb + t * kSfAtom, 16, 128, dev::kLayoutNone));
+                        // +32 bytes along K = +2 in a descriptor's address field
+                        const uint64_t adesc = adesc0 + (uint64_t)(kc * (kATileBytes >> 4));
+                        const uint64_t bdesc = dev::smem_desc(dev::smem_addr(smem + L.b_off + brd.slot * kBTileBytes),
+                                                              16, 1024, dev::kLayoutSwizzle128);
+#pragma unroll
+                        for (int kb = 0; kb < 4; ++kb)
+                            dev::tc_mma_mx(d_tmem, adesc + 2u * kb, bdesc + 2u * kb, idesc0 | dev::mx_idesc_sf((uint32_t)kb),
+                                           (tmem + kSfaCol + 4 * kc) | ((uint32_t)kb << 30),
                                            (tmem + kSfbCol) | ((uint32_t)kb << 30), (kc | kb) != 0);
-                        }
-                        dev::tc_commit(&b_empty[bs]);
+                        if (!p.epi_release) dev::tc_commit(&b_empty[brd.slot]);
+                        brd.advance(1);
                     }
-                    if (ok) dev::tc_commit(&acc_full[accs]);
+                    if (!ok) break;
+                    dev::tc_commit(&acc_full[s]);
+                    if (++s == kAccStages) s = 0, sph ^= 1u;
                 }
                 if (ok) dev::tc_commit(&a_empty[as]);
             }
@@ -325,14 +463,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue
-        const int q = warp & 3;          // TMEM lane quadrant this warp may access
-        const int h = (warp - 2) >> 2;   // 32-column quarter of each accumulator tile
+        // Warp (q, j): TMEM lane quadrant q = warp % 4 (the only lanes it may
+        // read), columns [64 j, 64 j + 64) of every accumulator tile.  All three
+        // warps of a quadrant drain each tile together, so a stage is held only
+        // for two 32-column loads.
+        const int q = warp & 3;
+        const int j = (warp - 2) >> 2;
         const int r = q * 32 + lane;     // row within the point tile
         float4* merge = reinterpret_cast<float4*>(smem + L.merge_off);
-        const float* cn_s = reinterpret_cast<const float*>(smem + L.cn_off);
-        uint32_t acount = 0, merge_count = 0;
+        float2* seed = reinterpret_cast<float2*>(smem + L.seed_off);
+        const float* cn_base = p.cn_smem ? reinterpret_cast<const float*>(smem + L.cn_off) : p.cn;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * kSliceCols);
+        // After each row tile's first (hinted) centroid tile the quadrant's three
+        // warps swap their running minima, so each then starts from the likely
+        // winner and rarely needs an index search.
+        const bool seeding = kArgmin && tiles_n >= 2;
+        // One warp hands the tile's centroid-ring slots back to the producer:
+        // acc_full means every MMA that read them has completed.
+        const bool releaser = p.epi_release && q == 0 && j == 0 && lane == 0;
+        RingPos rel{0, 0u, kBStages};
+        int s = 0;           // accumulator stage of the next tile
+        uint32_t sph = 0;
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x) {
+        int it = 0;
+        for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+            const int buf = it & 1;
             const int64_t grow = tile * kBM + r;
             const bool valid = grow < mrows;
             int64_t point = grow;
@@ -342,126 +497,86 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pn = p.pn[point];
             }
             const uint64_t pn2 = dev::pack2(pn, pn);
-            float first = __int_as_float(0x7f800000), largest = -1e38f, next = -1e38f;
-            int best = 0x7fffffff;
+            RowMin m{__int_as_float(0x7f800000), -1e38f, -1e38f, 0x7fffffff};
             const int ct0 = sweep_start(p, tile, mrows, tiles_n);
-            for (int i = 0; i < tiles_n; ++i, ++acount) {
+            for (int i = 0; i < tiles_n; ++i) {
                 const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
-                const int accs = (int)(acount % kAccStages);
-                const uint32_t accph = (acount / kAccStages) & 1u;
-                if (!dev::mbar_wait(&acc_full[accs], accph, abort_flag, p.err)) { ok = false; break; }
+                if (!dev::mbar_wait(&acc_full[s], sph, abort_flag, p.err)) { ok = false; break; }
                 dev::tc_fence_after();
-                uint32_t v[32];
-                dev::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + accs * kBN + h * 32, v);
+                if (releaser) {
+                    for (int kc = 0; kc < p.kchunks; ++kc) {
+                        dev::mbar_arrive(&b_empty[rel.slot]);
+                        rel.advance(1);
+                    }
+                }
+                uint32_t v[2][32];
+                dev::tmem_ld_32x32b_x32(lane_base + (uint32_t)s * kBN, v[0]);
+                dev::tmem_ld_32x32b_x32(lane_base + (uint32_t)s * kBN + 32, v[1]);
                 dev::tmem_wait_ld();
                 dev::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) dev::mbar_arrive(&acc_empty[accs]);
-                const int64_t c0 = (int64_t)ct * kBN + h * 32;
-                if constexpr (!kArgmin) {
-                    if (valid) {
-                        float* orow = p.out + grow * p.n;
-                        if (c0 + 32 <= p.n && p.out_vec) {
+                if (lane == 0) dev::mbar_arrive(&acc_empty[s]);
+                if (++s == kAccStages) s = 0, sph ^= 1u;
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(orow + c0 + j) =
-                                    make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-                        } else {
+                for (int sub = 0; sub < 2; ++sub) {
+                    const int cc = ct * kBN + j * kSliceCols + sub * 32;
+                    if constexpr (!kArgmin) {
+                        if (valid) {
+                            float* orow = p.out + grow * p.n;
+                            if (cc + 32 <= p.n && p.out_vec) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (c0 + j < p.n) orow[c0 + j] = __uint_as_float(v[j]);
-                        }
-                    }
-                } else if (c0 + 32 <= p.n) {
-                    // distances fmaf(-2, dot, pn + cn) two at a time (add/fma .f32x2, each
-                    // lane rounded exactly like the scalar operation)
-                    float dist[32];
+                                for (int c = 0; c < 32; c += 4)
+                                    *reinterpret_cast<float4*>(orow + cc + c) = make_float4(
+                                        __uint_as_float(v[sub][c]), __uint_as_float(v[sub][c + 1]),
+                                        __uint_as_float(v[sub][c + 2]), __uint_as_float(v[sub][c + 3]));
+                            } else {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 cv = p.cn_smem ? *reinterpret_cast<const float4*>(cn_s + c0 + j)
-                                                    : __ldg(reinterpret_cast<const float4*>(p.cn + c0 + j));
-                        dev::dist2(v[j], v[j + 1], pn2, cv.x, cv.y, dist[j], dist[j + 1]);
-                        dev::dist2(v[j + 2], v[j + 3], pn2, cv.z, cv.w, dist[j + 2], dist[j + 3]);
-                    }
-                    if constexpr (kGaps) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            next = fmaxf(next, fminf(largest, dist[j]));
-                            largest = fmaxf(largest, dist[j]);
-                        }
-                    }
-                    // Chunk minimum with 3-input mins.  The index search runs only
-                    // when the chunk can change the row's (distance, index) minimum:
-                    // a smaller distance, or an equal one (a tie resolved by the
-                    // lower index, as insert_distance does; rare after the first
-                    // chunk).  NaN distances never compare, as in the reference.
-                    float m3[11];
-#pragma unroll
-                    for (int t = 0; t < 10; ++t) m3[t] = dev::min3f(dist[3 * t], dist[3 * t + 1], dist[3 * t + 2]);
-                    m3[10] = fminf(dist[30], dist[31]);
-                    const float ma = dev::min3f(m3[0], m3[1], m3[2]);
-                    const float mb = dev::min3f(m3[3], m3[4], m3[5]);
-                    const float mc = dev::min3f(m3[6], m3[7], m3[8]);
-                    const float cm = fminf(dev::min3f(ma, mb, mc), fminf(m3[9], m3[10]));
-                    if (cm <= first) {
-                        int idx = 31;
-#pragma unroll
-                        for (int j = 30; j >= 0; --j) idx = dist[j] == cm ? j : idx;
-                        const int cand = (int)c0 + idx;
-                        if (cm < first || cand < best) {
-                            first = cm;
-                            best = cand;
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (c0 + j < p.n) {
-                            const float cnv = p.cn_smem ? cn_s[c0 + j] : __ldg(p.cn + c0 + j);
-                            const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cnv);
-                            if (dist < first || (dist == first && (int)(c0 + j) < best)) {
-                                first = dist;
-                                best = (int)(c0 + j);
-                            }
-                            if constexpr (kGaps) {
-                                next = fmaxf(next, fminf(largest, dist));
-                                largest = fmaxf(largest, dist);
+                                for (int c = 0; c < 32; ++c)
+                                    if (cc + c < p.n) orow[cc + c] = __uint_as_float(v[sub][c]);
                             }
                         }
+                    } else if (cc + 32 <= p.n) {
+                        argmin_chunk32<kGaps>(v[sub], cn_base + cc, pn2, cc, m);
+                    } else if (cc < p.n) {
+                        argmin_tail<kGaps>(v[sub], cn_base + cc, pn, cc, p.n, m);
+                    }
+                }
+                if (seeding && i == 0) {
+                    float2* mine = seed + (size_t)(buf * kEpiPerQuad) * kBM;
+                    mine[j * kBM + r] = make_float2(m.first, __int_as_float(m.best));
+                    __syncwarp();
+                    if (lane == 0) dev::mbar_arrive(&seed_bar[q]);
+                    if (!dev::mbar_wait(&seed_bar[q], (uint32_t)buf, abort_flag, p.err)) { ok = false; break; }
+#pragma unroll
+                    for (int o = 0; o < kEpiPerQuad; ++o) {
+                        if (o == j) continue;
+                        const float2 sd = mine[o * kBM + r];
+                        merge_rowmin<false>(m, sd.x, __float_as_int(sd.y), 0.0f, 0.0f);
                     }
                 }
             }
+            if (!ok) break;
             if constexpr (kArgmin) {
-                if (!ok) break;
-                // Combine the four column quarters of each row: lexicographic
-                // (distance, index) minimum and the two-largest merge.  The hand-off
-                // uses mbarriers with bounded waits (never an unbounded bar.sync).
-                const uint32_t mph = (uint32_t)(merge_count++) & 1u;
-                if (h != 0) {
-                    if (!dev::mbar_wait(merge_empty, mph ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                    merge[(h - 1) * kBM + r] = make_float4(first, __int_as_float(best), largest, next);
+                // Combine the three column slices of each row.  The hand-off uses
+                // mbarriers with bounded waits (never bar.sync).
+                const int hb = q * 2 + buf;
+                const uint32_t hph = (uint32_t)(it >> 1) & 1u;
+                float4* slots = merge + (size_t)buf * 2 * kBM;
+                if (j != 0) {
+                    if (!dev::mbar_wait(&merge_empty[hb], hph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                    slots[(j - 1) * kBM + r] = make_float4(m.first, __int_as_float(m.best), m.largest, m.next);
                     __syncwarp();
-                    if (lane == 0) dev::mbar_arrive(merge_full);
+                    if (lane == 0) dev::mbar_arrive(&merge_full[hb]);
                 } else {
-                    if (!dev::mbar_wait(merge_full, mph, abort_flag, p.err)) { ok = false; break; }
-                    float4 o[3];
-#pragma unroll
-                    for (int t = 0; t < 3; ++t) o[t] = merge[t * kBM + r];
+                    if (!dev::mbar_wait(&merge_full[hb], hph, abort_flag, p.err)) { ok = false; break; }
+                    const float4 o0 = slots[r], o1 = slots[kBM + r];
                     __syncwarp();
-                    if (lane == 0) dev::mbar_arrive(merge_empty);
+                    if (lane == 0) dev::mbar_arrive(&merge_empty[hb]);
                     if (valid) {
-#pragma unroll
-                        for (int t = 0; t < 3; ++t) {
-                            const int ob = __float_as_int(o[t].y);
-                            if (o[t].x < first || (o[t].x == first && ob < best)) first = o[t].x, best = ob;
-                            if constexpr (kGaps) {
-                                next = fmaxf(fminf(largest, o[t].z), fmaxf(next, o[t].w));
-                                largest = fmaxf(largest, o[t].z);
-                            }
-                        }
-                        p.labels[point] = best;
-                        if constexpr (kGaps) p.gaps[point] = largest - next;
+                        merge_rowmin<kGaps>(m, o0.x, __float_as_int(o0.y), o0.z, o0.w);
+                        merge_rowmin<kGaps>(m, o1.x, __float_as_int(o1.y), o1.z, o1.w);
+                        p.labels[point] = m.best;
+                        if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
                 }
             }
@@ -541,6 +656,9 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     if (!fits(p.a_stages, p.cn_smem, 2)) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: shared memory budget exceeded");
     p.b_stages = 2;
     while (p.b_stages < kMaxBStages && fits(p.a_stages, p.cn_smem, p.b_stages + 1)) ++p.b_stages;
+    // A slot freed only when its whole tile completes needs room for the next
+    // tile's chunks too; otherwise each chunk is freed by its own commit.
+    p.epi_release = p.b_stages >= 2 * p.kchunks;
     // At least 116 KB so that no second CTA shares the SM (each CTA holds all
     // 512 TMEM columns while it runs).
     const uint32_t smem_bytes =
@@ -555,14 +673,15 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     uint8_t* tmp_atoms = nullptr;
     if (!scale_atoms) {
         MXK_REQUIRE(!rows_dev, "gemm_mx: device-side row counts need atom-layout scales");
-        const int64_t a_bytes = (m + 127) / 128 * p.kchunks * kSfAtom;
-        const int64_t b_bytes = (n + 127) / 128 * p.kchunks * kSfAtom;
+        const int64_t a_bytes = scale_atom_bytes(m, k, kBM);
+        const int64_t b_bytes = scale_atom_bytes(n, k, kBN);
         MXK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp_atoms), (size_t)(a_bytes + b_bytes), stream));
         const int sms = sm_count();
         {
             LaunchScope scope("scales_to_atoms", stream);
-            scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(m, p.kchunks, a_scales, tmp_atoms, a_bytes / 4);
-            scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(n, p.kchunks, b_scales, tmp_atoms + a_bytes, b_bytes / 4);
+            scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(m, p.kchunks, kBM, a_scales, tmp_atoms, a_bytes / 4);
+            scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(n, p.kchunks, kBN, b_scales, tmp_atoms + a_bytes,
+                                                                b_bytes / 4);
         }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
@@ -597,8 +716,9 @@ extern "C" {
 
 int mxk_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales, const uint8_t* b,
                 const uint8_t* b_scales, float* out, void* stream) {
-    return mxk::launch_gemm_mx(bits, m, n, k, a, a_scales, b, b_scales, out, nullptr, nullptr,
-                               mxk::as_stream(stream));
+    MXK_CHECK(mxk::launch_gemm_mx(bits, m, n, k, a, a_scales, b, b_scales, out, nullptr, nullptr,
+                                  mxk::as_stream(stream)));
+    return mxk::check_device_error(mxk::as_stream(stream));
 }
 
 int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, const uint8_t* a_scales,
@@ -612,8 +732,9 @@ int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, con
     am.labels = labels;
     am.gaps = gaps;
     am.start_hint = start_hint;
-    return mxk::launch_gemm_mx(bits, rows, k, d, a, a_scales, b, b_scales, nullptr, &am, nullptr,
-                               mxk::as_stream(stream));
+    MXK_CHECK(mxk::launch_gemm_mx(bits, rows, k, d, a, a_scales, b, b_scales, nullptr, &am, nullptr,
+                                  mxk::as_stream(stream)));
+    return mxk::check_device_error(mxk::as_stream(stream));
 }
 
 }  // extern "C"

@@ -10,13 +10,23 @@ namespace mxk {
 
 // ---- quantize.cu ------------------------------------------------------------
 // rows_dev (optional): device-resident row count that overrides `rows`, which
-// then only sizes the grid (an upper bound).  atoms: write the scales in the
-// tcgen05 atom layout (scale_atom_bytes(rows, d) bytes, d % 128 == 0) instead of
-// row-major [rows][d/32].
+// then only sizes the grid (an upper bound).  atom_rows > 0: write the scales in
+// the tcgen05 atom layout for tiles of atom_rows rows (scale_atom_bytes(rows, d,
+// atom_rows) bytes, d % 128 == 0) instead of row-major [rows][d/32].
+//
+// Atom layout: rows form tiles of tile_rows (a point tile is kPointTileRows, a
+// centroid tile kCentroidTileRows); each (tile, 128-feature chunk) owns
+// ceil(tile_rows / 128) consecutive 512-byte atoms, one per 128-row slice of the
+// tile, holding slice row r's four block scales at (r % 32) * 16 + (r / 32) * 4 +
+// block % 4 -- the image tcgen05.cp .32x128b.warpx4 copies into TMEM.
+constexpr int kPointTileRows = 128;
+constexpr int kCentroidTileRows = 192;
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
                     uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream,
-                    bool atoms = false);
-inline int64_t scale_atom_bytes(int64_t rows, int d) { return (rows + 127) / 128 * (d / 128) * 512; }
+                    int atom_rows = 0);
+inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileRows) {
+    return (rows + tile_rows - 1) / tile_rows * (d / 128) * ((tile_rows + 127) / 128) * 512;
+}
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
 int launch_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
                         cudaStream_t stream);
@@ -53,9 +63,9 @@ struct MxArgmin {
 };
 // Dense: out[m x n] = A . B^T.  Argmin: labels of the m rows against n centroids.
 // rows_dev (optional) = device-resident m (m is then an upper bound).
-// scale_atoms: both scale arrays are in the tcgen05 atom layout (see
-// launch_quantize), which the kernel fetches with bulk TMA copies; otherwise
-// they are row-major and gathered by the producer warp.
+// scale_atoms: the point scales are in the atom layout for kPointTileRows and the
+// centroid scales for kCentroidTileRows (see launch_quantize), which the kernel
+// fetches with bulk copies; otherwise both are row-major and converted per call.
 int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales,
                    const uint8_t* b, const uint8_t* b_scales, float* out, const MxArgmin* argmin,
                    const int* rows_dev, cudaStream_t stream, bool scale_atoms = false);

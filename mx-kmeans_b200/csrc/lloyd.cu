@@ -143,10 +143,10 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&cerr, k));
     MXK_CHECK(ws.alloc(&stats, 2));
     MXK_CHECK(ws.alloc(&qcent, kd));
-    MXK_CHECK(ws.alloc(&cscales, scale_atom_bytes(k, d)));
+    MXK_CHECK(ws.alloc(&cscales, scale_atom_bytes(k, d, kCentroidTileRows)));
     // scale atoms of padding rows are never written; keep them finite
     MXK_CUDA(cudaMemsetAsync(pscales, 0, (size_t)scale_atom_bytes(n, d), stream));
-    MXK_CUDA(cudaMemsetAsync(cscales, 0, (size_t)scale_atom_bytes(k, d), stream));
+    MXK_CUDA(cudaMemsetAsync(cscales, 0, (size_t)scale_atom_bytes(k, d, kCentroidTileRows), stream));
     MXK_CHECK(ws.alloc(&prev, kd));
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
@@ -189,14 +189,15 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 std::fprintf(stderr, "iteration=%d precision=FP32\n", it + 1);
         } else {
             MXK_CUDA(cudaMemsetAsync(cerr, 0, sizeof(float) * k, stream));
-            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream, true));
+            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream,
+                                      kCentroidTileRows));
             MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
             MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream));
             MXK_CHECK(launch_group_compaction(n, precision, ord, ids, gcount, cscratch, stream));
             static const int group_bits[3] = {4, 6, 8};
             for (int g = 0; g < 3; ++g) {
                 MXK_CHECK(launch_quantize(group_bits[g], n, d, points, ids + g * n, qpoints, pscales, nullptr,
-                                          gcount + g, stream, true));
+                                          gcount + g, stream, kPointTileRows));
                 MxArgmin am;
                 am.point_norms = pnorm;
                 am.centroid_norms = cnorm;

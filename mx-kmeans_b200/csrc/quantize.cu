@@ -26,20 +26,24 @@ __device__ __forceinline__ float4 ldg4(const float* p) {
 // threads of a 32-feature block combine their maxima with one shuffle, derive the
 // UE8M0 scale exactly as the reference (Scale(amax/qmax) or 1 when amax == 0),
 // and multiply by the exact reciprocal of the scale.
-// Byte offset of the scale of (row, 32-feature block) in the tcgen05 atom layout:
-// one 512-byte atom per (128-row tile, 128-feature chunk), tile-major, holding
-// row r's four block scales at (r % 32) * 16 + (r / 32) * 4 + block % 4.
-__device__ __forceinline__ int64_t scale_atom_offset(int64_t row, int blk, int kchunks) {
-    const int64_t tile = row >> 7;
-    const int r = (int)(row & 127);
-    return ((tile * kchunks + (blk >> 2)) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + (blk & 3);
+// Byte offset of the scale of (row, 32-feature block) in the tcgen05 atom layout
+// for tiles of tile_rows rows: ceil(tile_rows / 128) 512-byte atoms per (tile,
+// 128-feature chunk), tile-major, slice row r's four block scales at
+// (r % 32) * 16 + (r / 32) * 4 + block % 4.
+__device__ __forceinline__ int64_t scale_atom_offset(int64_t row, int blk, int kchunks, int tile_rows) {
+    const int64_t tile = row / tile_rows;
+    const int rr = (int)(row - tile * tile_rows);
+    const int per_tile = (tile_rows + 127) >> 7;
+    const int r = rr & 127;
+    return (((tile * kchunks + (blk >> 2)) * per_tile + (rr >> 7)) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) +
+           (blk & 3);
 }
 
 template <int BITS>
 __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chunks, int d,
                                                const float* __restrict__ points, const int* __restrict__ pid,
                                                uint8_t* __restrict__ values, uint8_t* __restrict__ scales,
-                                               float* __restrict__ errors, bool atoms) {
+                                               float* __restrict__ errors, int atom_rows) {
     const bool valid = g < total;
     const int64_t row = valid ? g / chunks : 0;
     const int chunk = valid ? (int)(g - row * chunks) : 0;
@@ -130,8 +134,8 @@ __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chu
         *reinterpret_cast<uint2*>(values + elem / 2) = w;
     }
     if ((chunk & 1) == 0) {
-        if (atoms)
-            scales[scale_atom_offset(row, chunk >> 1, d >> 7)] = (uint8_t)s;
+        if (atom_rows)
+            scales[scale_atom_offset(row, chunk >> 1, d >> 7, atom_rows)] = (uint8_t)s;
         else
             scales[row * (d >> 5) + (chunk >> 1)] = (uint8_t)s;
         // Squared errors are non-negative, so integer order equals float order.
@@ -143,13 +147,13 @@ template <int BITS>
 __global__ void __launch_bounds__(256) quantize_kernel(int64_t rows, int d, const float* __restrict__ points,
                                                        const int* __restrict__ pid, uint8_t* __restrict__ values,
                                                        uint8_t* __restrict__ scales, float* __restrict__ errors,
-                                                       const int* __restrict__ rows_dev, bool atoms) {
+                                                       const int* __restrict__ rows_dev, int atom_rows) {
     const int64_t nrows = rows_dev ? (int64_t)*rows_dev : rows;
     const int chunks = d >> 4;
     const int64_t total = nrows * chunks;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;  // multiple of 32: block pairs stay in one warp
     for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
-        quantize_chunk<BITS>(base + threadIdx.x, total, chunks, d, points, pid, values, scales, errors, atoms);
+        quantize_chunk<BITS>(base + threadIdx.x, total, chunks, d, points, pid, values, scales, errors, atom_rows);
     }
 }
 
@@ -357,11 +361,12 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 }  // namespace
 
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
-                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream, bool atoms) {
+                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream, int atom_rows) {
     if (bits != 4 && bits != 6 && bits != 8) return fail(MXK_ERR_INVALID, "Precision must be 4, 6, or 8");
     if (rows <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && d % 32 == 0, "quantize_rows: d must be a positive multiple of 32");
-    MXK_REQUIRE(!atoms || d % 128 == 0, "quantize_rows: the scale-atom layout needs d % 128 == 0");
+    MXK_REQUIRE(atom_rows >= 0, "quantize_rows: negative atom tile height");
+    MXK_REQUIRE(!atom_rows || d % 128 == 0, "quantize_rows: the scale-atom layout needs d % 128 == 0");
     MXK_REQUIRE(points && values && scales, "quantize_rows: null pointer");
     MXK_REQUIRE(aligned(points, 16), "quantize_rows: points must be 16-byte aligned");
     MXK_REQUIRE(aligned(values, bits == 8 ? 16 : (bits == 4 ? 8 : 4)),
@@ -373,9 +378,9 @@ int launch_quantize(int bits, int64_t rows, int d, const float* points, const in
     auto* out = static_cast<uint8_t*>(values);
     LaunchScope scope("quantize_mx", stream);
     switch (bits) {
-        case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
-        case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
-        default: quantize_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atoms); break;
+        case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atom_rows); break;
+        case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atom_rows); break;
+        default: quantize_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atom_rows); break;
     }
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
