@@ -264,6 +264,30 @@ __device__ __forceinline__ void dist2(uint32_t v0, uint32_t v1, uint64_t pn2, fl
         : "l"(pn2), "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
 }
 
+// 16-byte shared-memory load through an explicit shared-window address.
+__device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
+    float4 r;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "r"(saddr));
+    return r;
+}
+__device__ __forceinline__ float lds_f1(uint32_t saddr) {
+    float r;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(saddr));
+    return r;
+}
+
+// (k0, k1) = fmaf(-2, (v0, v1), (c0, c1)) with one .f32x2 fma.
+__device__ __forceinline__ void key2(uint32_t v0, uint32_t v1, float c0, float c1, float& k0, float& k1) {
+    asm("{\n\t.reg .b64 c, v, m, d;\n\t"
+        "mov.b64 c, {%2, %3};\n\t"
+        "mov.b64 v, {%4, %5};\n\t"
+        "mov.b64 m, {%6, %6};\n\t"
+        "fma.rn.f32x2 d, m, v, c;\n\t"
+        "mov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(k0), "=f"(k1)
+        : "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
+}
+
 __device__ __forceinline__ float min3f(float a, float b, float c) {
     float r;
     asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));

@@ -10,29 +10,31 @@
 // a dense store (gemm_mx API) or, fused, the distance fmaf(-2,dot,pn+cn) and the
 // lowest-index argmin (+ optional two-largest gap) so that no N x K buffer exists.
 //
-// Structure (one persistent CTA per SM, 448 threads):
+// Structure (one persistent CTA per SM, 512 threads = 4 warpgroups):
 //   warp 0      producer: TMA (SWIZZLE_128B) of a 128-row point tile (all K,
-//               resident while every centroid tile streams past) and of 128-row
-//               x 128-byte centroid chunks through a ring as deep as shared
-//               memory allows; 1-D bulk copies of the matching 512-byte
-//               tcgen05 scale atoms (the quantizer writes scales in that layout;
-//               row-major API scales are converted once per call).
-//   warp 1      TMEM allocator and the single MMA-issuing thread: tcgen05.cp of
-//               the scale atoms into TMEM, tcgen05.mma kind::mxf8f6f4
-//               block_scale (M=128, N=128, K=32) into a three-stage TMEM
-//               accumulator ring (columns 0-383; scales in 384-451), one
-//               tcgen05.commit per tile.
-//   warps 2-13  epilogue, one warp per (TMEM lane quadrant w%4, accumulator
-//               stage (w-2)/4): each drains every third 128-column tile for its
-//               32 rows, then dense store or argmin: packed f32x2 distances, a
-//               3-input-min tree per 32 columns and an index search only when a
-//               32-column chunk can change the row's running minimum.  The warp
-//               that drains a row tile's first (hinted) centroid tile publishes
-//               its per-row minimum to the other two warps of its quadrant, so
-//               that they too start from the likely winner and rarely search;
-//               the warp that drains the last tile merges the three partial
-//               results and writes the label.  The quadrant-0 warp of a stage
-//               also frees the tile's centroid-ring slots once the tile is full.
+//               resident while every centroid tile streams past) and of
+//               192-row x 128-byte centroid chunks through a ring as deep as
+//               shared memory allows; 1-D bulk copies of the matching tcgen05
+//               scale atoms (the quantizer writes scales in that layout;
+//               row-major API scales are converted once per call).  The
+//               centroid scales of small problems are copied into TMEM once.
+//   warp 1      TMEM allocator and the single MMA-issuing thread:
+//               tcgen05.mma kind::mxf8f6f4 block_scale (M=128, N=192, K=32)
+//               into a two-stage TMEM accumulator ring (columns 0-383, scale
+//               factors in 384-511), one tcgen05.commit per tile.
+//   warps 2-3   idle (their warpgroup gives registers to the epilogue).
+//   warps 4-15  epilogue, warp (q = w % 4, j = (w - 4) / 4): TMEM lane quadrant
+//               q, columns [64 j, 64 j + 64) of every tile.  Dense store, or
+//               argmin: a cheap key fmaf(-2, dot, cn) screens each 32-column
+//               chunk and only chunks that can still win form the exact
+//               distances fmaf(-2, dot, pn + cn) (packed f32x2, 3-input-min
+//               tree, index search on improvement).  After each row tile's
+//               first (hinted) centroid tile the quadrant's three warps swap
+//               their minima; the j = 0 warp merges the three slices and writes
+//               the label.  One warp hands centroid-ring slots back to the
+//               producer once their tile's MMAs have completed.
+// Argmin kernels rebalance registers with setmaxnreg (warpgroup 0: 56,
+// epilogue warpgroups: 152).
 #include <cstring>
 
 #include "common.cuh"
@@ -54,15 +56,26 @@ constexpr int kAccStages = 2;            // 2 x 192 accumulator columns
 constexpr int kEpiPerQuad = 3;           // epilogue warps per TMEM lane quadrant
 constexpr int kSliceCols = kBN / kEpiPerQuad;  // 64 accumulator columns per epilogue warp
 constexpr int kEpiWarps = 4 * kEpiPerQuad;
-constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kEpiWarp0 = 4;             // warpgroup 0: producer, MMA issuer, two idle warps
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+// Register split (setmaxnreg, argmin kernels): launched at 128 per thread, the
+// first warpgroup drops to kLowRegs and the three epilogue warpgroups rise to
+// kHighRegs.  Per SM sub-partition (one warp of each warpgroup) that is
+// 56 + 3 * 152 = 512 = 4 * 128 registers per lane, exactly the launch budget.
+constexpr int kLaunchRegs = 128;
+constexpr int kLowRegs = 56;
+constexpr int kHighRegs = 152;
+static_assert(kLowRegs + 3 * kHighRegs == 4 * kLaunchRegs, "register split must equal the launch budget");
 constexpr int kMaxSmemNorms = 8192;      // centroid norms staged in shared memory up to this k
 constexpr int kMaxChunks = 8;            // K <= 1024
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfaCol = kAccStages * kBN;  // 384: 4 columns per K chunk (<= 32)
-constexpr uint32_t kSfbCol = kSfaCol + 64;       // 448: 4 columns per scale atom
+constexpr uint32_t kSfbCol = kSfaCol + 32;       // 416: centroid scales, 4 columns per atom
+constexpr int kSfbChunkCols = 4 * kBAtoms;       // TMEM columns per (centroid tile, K chunk)
+constexpr int kMaxResidentSfb = (512 - (int)kSfbCol) / kSfbChunkCols;  // 12 (tile, chunk) pairs
 constexpr int kNumBars = 64;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
 static_assert(kSliceCols == 64 && kBN % 32 == 0, "each epilogue warp drains two 32-column chunks");
-static_assert(kSfbCol + 4 * kBAtoms <= kTmemCols, "TMEM budget");
+static_assert(kSfbCol + kSfbChunkCols <= kTmemCols, "TMEM budget");
 
 struct GemmParams {
     int64_t m;
@@ -81,6 +94,9 @@ struct GemmParams {
     int b_stages; // depth of the centroid-chunk ring (<= kMaxBStages)
     int epi_release;  // ring slots are freed by the epilogue per tile (ring holds >= 2 tiles),
                       // else by the MMA thread per chunk
+    int sfb_resident; // every centroid scale atom sits in TMEM for the whole kernel (tiles_n *
+                      // kchunks <= kMaxResidentSfb); else each ring slot carries its tile's atoms
+    int sfb_atoms;    // scale atoms in the shared-memory centroid-scale region
     const float* pn;
     const float* cn;
     const int* pid;
@@ -106,17 +122,20 @@ struct SmemLayout {
 };
 
 // cn_floats: centroid norms staged in shared memory (0 when read from global).
-__host__ __device__ inline SmemLayout smem_layout(int kchunks, int a_stages, int cn_floats, int b_stages) {
+// sfb_atoms: centroid scale atoms held in shared memory -- all of them (resident
+// mode, staged once) or kBAtoms per ring slot.
+__host__ __device__ inline SmemLayout smem_layout(int kchunks, int a_stages, int cn_floats, int b_stages,
+                                                  int sfb_atoms) {
     SmemLayout s;
     s.a_off = 0;  // every operand tile starts on a 1024-byte boundary (SWIZZLE_128B atoms)
     s.b_off = s.a_off + a_stages * kchunks * kATileBytes;
     s.sfa_off = s.b_off + b_stages * kBTileBytes;
     s.sfb_off = s.sfa_off + a_stages * kchunks * kSfAtom;
-    s.merge_off = s.sfb_off + b_stages * kBAtoms * kSfAtom;  // [2 buffers][2 depositors][128 rows] x 16 B
+    s.merge_off = s.sfb_off + sfb_atoms * kSfAtom;           // [2 buffers][2 depositors][128 rows] x 16 B
     s.seed_off = s.merge_off + 2 * 2 * kBM * 16;              // [2 buffers][3 warps][128 rows] x 8 B
     s.cn_off = s.seed_off + 2 * kEpiPerQuad * kBM * 8;
     s.bar_off = s.cn_off + (uint32_t)((cn_floats * 4 + 15) / 16 * 16);
-    s.total = s.bar_off + kNumBars * 8 + 64;
+    s.total = s.bar_off + kNumBars * 8 + 128;  // barriers, then TMEM slot, abort flag, sweep starts, norm maxima
     return s;
 }
 
@@ -199,6 +218,22 @@ __device__ __forceinline__ int sweep_start(const GemmParams& p, int64_t tile, in
     return lab / kBN;
 }
 
+// Centroid norms: staged in shared memory (read with ld.shared through the
+// shared-window address) or read from global memory.
+template <bool kShared>
+struct NormSrc {
+    const float* g;   // global norms
+    uint32_t s;       // shared-window address of the staged norms
+    __device__ __forceinline__ float4 load4(int c) const {
+        if constexpr (kShared) return dev::lds_f4(s + 4u * (uint32_t)c);
+        else return __ldg(reinterpret_cast<const float4*>(g + c));
+    }
+    __device__ __forceinline__ float load1(int c) const {
+        if constexpr (kShared) return dev::lds_f1(s + 4u * (uint32_t)c);
+        else return __ldg(g + c);
+    }
+};
+
 // Running (distance, index) minimum and two largest distances of one row.
 struct RowMin {
     float first, largest, next;
@@ -211,13 +246,13 @@ struct RowMin {
 // search only when the chunk minimum can change the running minimum (smaller,
 // or equal, resolved by the lower index as insert_distance does).  NaN
 // distances never compare, as in the reference.
-template <bool kGaps>
-__device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const float* cn, uint64_t pn2, int c0,
+template <bool kGaps, class Norms>
+__device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, int c0,
                                                RowMin& m) {
     float dist[32];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-        const float4 cv = *reinterpret_cast<const float4*>(cn + j);
+        const float4 cv = cn.load4(c0 + j);
         dev::dist2(v[j], v[j + 1], pn2, cv.x, cv.y, dist[j], dist[j + 1]);
         dev::dist2(v[j + 2], v[j + 3], pn2, cv.z, cv.w, dist[j + 2], dist[j + 3]);
     }
@@ -248,14 +283,43 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const fl
     }
 }
 
+// argmin_chunk32 behind a cheap screen.  Keys k_j = fmaf(-2, dot_j, cn_j) need
+// one FP32 operation per column instead of two; the exact distances
+// d_j = fmaf(-2, dot_j, pn + cn_j) are formed only when the chunk could still
+// reach the row's running minimum.  Rounding bound: each d_j and k_j carries at
+// most a few units of 2^-24 of the magnitudes S = pn + max(cn) + |k_min| + |first|
+// and of its own excess over k_min, so d_j > first for every j in the chunk once
+// pn + k_min - 2^-20 * S > first.  Skipping then changes nothing: the result is
+// bit-identical to argmin_chunk32 alone.  NaN or infinite inputs fail the test
+// and take the exact path.  pc = pn + max(cn).
+template <class Norms>
+__device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2,
+                                                        float pn, float pc, int c0, RowMin& m) {
+    // keys folded into two running 3-input minima as they are formed (few live registers)
+    float ka = __int_as_float(0x7f800000), kb = ka;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 cv = cn.load4(c0 + j);
+        float k0, k1, k2, k3;
+        dev::key2(v[j], v[j + 1], cv.x, cv.y, k0, k1);
+        dev::key2(v[j + 2], v[j + 3], cv.z, cv.w, k2, k3);
+        ka = dev::min3f(ka, k0, k1);
+        kb = dev::min3f(kb, k2, k3);
+    }
+    const float kmin = fminf(ka, kb);
+    const float scale = pc + fabsf(kmin) + fabsf(m.first);
+    if (fmaf(-0x1p-20f, scale, pn + kmin) > m.first) return;
+    argmin_chunk32<false>(v, cn, pn2, c0, m);
+}
+
 // Columns c0.. of a 32-column chunk that runs past n: one column at a time.
-template <bool kGaps>
-__device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const float* cn, float pn, int c0, int64_t n,
+template <bool kGaps, class Norms>
+__device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms& cn, float pn, int c0, int64_t n,
                                             RowMin& m) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         if (c0 + j < n) {
-            const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cn[j]);
+            const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cn.load1(c0 + j));
             if (dist < m.first || (dist == m.first && c0 + j < m.best)) {
                 m.first = dist;
                 m.best = c0 + j;
@@ -265,6 +329,21 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const float
                 m.largest = fmaxf(m.largest, dist);
             }
         }
+    }
+}
+
+// One 32-column chunk of a row starting at column cc: screened fast path, the
+// exact path when gaps are needed, one column at a time past n.
+template <bool kGaps, class Norms>
+__device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, float pn, float pc,
+                                           int cc, int64_t n, RowMin& m) {
+    if (cc + 32 <= n) {
+        if constexpr (kGaps)
+            argmin_chunk32<true>(v, cn, pn2, cc, m);
+        else
+            argmin_chunk32_screened(v, cn, pn2, pn, pc, cc, m);
+    } else if (cc < n) {
+        argmin_tail<kGaps>(v, cn, pn, cc, n, m);
     }
 }
 
@@ -285,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages);
+    const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms);
     const int kBStages = p.b_stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* a_full = bars;                 // [2]
@@ -298,9 +377,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* merge_full = drain + 1;        // [q * 2 + row-tile parity] two depositing warps -> merging warp
     uint64_t* merge_empty = merge_full + 8;  // [q * 2 + row-tile parity] merging warp has read the deposits
     uint64_t* seed_bar = merge_empty + 8;    // [q] the quadrant's three first-tile minima are published
+    uint64_t* sfb_full = seed_bar + 4;       // resident centroid scales have landed in shared memory
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
-    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 <= kNumBars, "barrier slots");
+    volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [2] per A stage
+    float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 4;             // [kThreads / 32]
+    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 <= kNumBars, "barrier slots");
+    static_assert(4 + kThreads / 32 <= 32, "words after the barriers");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mrows = p.m_dev ? (int64_t)*p.m_dev : p.m;
@@ -318,13 +401,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             dev::mbar_init(&merge_empty[i], 1);
         }
         for (int q = 0; q < 4; ++q) dev::mbar_init(&seed_bar[q], kEpiPerQuad);
+        dev::mbar_init(sfb_full, 1);
         *abort_flag = 0;
         dev::fence_barrier_init();
     }
     if (warp == 1) dev::tmem_alloc(tmem_slot, kTmemCols);
-    if (kArgmin && p.cn_smem) {
+    if (kArgmin) {
+        // centroid norms -> shared memory (when they fit) and their maximum
         float* cn_s = reinterpret_cast<float*>(smem + L.cn_off);
-        for (int i = threadIdx.x; i < p.cn_smem; i += blockDim.x) cn_s[i] = p.cn[i];
+        float cmax = 0.0f;
+        for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
+            const float c = p.cn[i];
+            if (p.cn_smem) cn_s[i] = c;
+            cmax = c > cmax || c != c ? c : cmax;  // NaN propagates (and disables the screen)
+        }
+        for (int o = 16; o; o >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, cmax, o);
+            cmax = other > cmax || other != other ? other : cmax;
+        }
+        if (lane == 0) warp_cmax[warp] = cmax;
     }
     if (warp == 0 && lane == 0) {
         if (p.a_bits == 8) dev::prefetch_tensor_map(&tmap_a);
@@ -335,12 +430,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     dev::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    if (warp < kEpiWarp0) {
+    if constexpr (kArgmin) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         RingPos bring{0, 0u, kBStages};
         uint32_t issued = 0;
         int it = 0;
         bool ok = true;
+        if (p.sfb_resident && lane == 0) {
+            const uint32_t bytes = (uint32_t)(p.sfb_atoms * kSfAtom);
+            dev::mbar_arrive_expect_tx(sfb_full, bytes);
+            dev::bulk_load(smem + L.sfb_off, p.b_scales, bytes, sfb_full);
+        }
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
@@ -362,6 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.a_bits != 8)
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
+            const int ct0 = lane == 0 ? sweep_start(p, tile, mrows, tiles_n) : 0;
+            if (lane == 0) sweep0[as] = ct0;  // published to the MMA thread by the a_full arrival
             dev::fence_proxy_async();
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&a_full[as]);
@@ -369,7 +473,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the epilogue once the tile that read it has completed, or by the MMA
             // thread's per-chunk commit when the ring holds less than two tiles.
             if (lane == 0) {
-                const int ct0 = sweep_start(p, tile, mrows, tiles_n);
                 for (int i = 0; i < tiles_n && ok; ++i) {
                     const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
                     for (int kc = 0; kc < p.kchunks; ++kc) {
@@ -378,12 +481,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         uint64_t* full = &b_full[bring.slot];
-                        dev::mbar_arrive_expect_tx(full, (uint32_t)(kBTileBytes + kBAtoms * kSfAtom));
+                        dev::mbar_arrive_expect_tx(
+                            full, (uint32_t)(kBTileBytes + (p.sfb_resident ? 0 : kBAtoms * kSfAtom)));
                         dev::tma_load_2d(smem + L.b_off + bring.slot * kBTileBytes, &tmap_b, kc * kChunk, ct * kBN,
                                          full);
-                        dev::bulk_load(smem + L.sfb_off + bring.slot * kBAtoms * kSfAtom,
-                                       p.b_scales + ((int64_t)ct * p.kchunks + kc) * kBAtoms * kSfAtom,
-                                       kBAtoms * kSfAtom, full);
+                        if (!p.sfb_resident)
+                            dev::bulk_load(smem + L.sfb_off + bring.slot * kBAtoms * kSfAtom,
+                                           p.b_scales + ((int64_t)ct * p.kchunks + kc) * kBAtoms * kSfAtom,
+                                           kBAtoms * kSfAtom, full);
                         ++issued;
                         bring.advance(1);
                     }
@@ -415,7 +520,56 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             const uint32_t idesc0 = dev::mx_idesc(dev::kFmtE4M3, dev::kFmtE4M3, kBM, kBN, 0);
-            for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+            if (p.sfb_resident) {
+                // every (centroid tile, K chunk)'s scale atoms -> TMEM once
+                if (!dev::mbar_wait(sfb_full, 0, abort_flag, p.err)) ok = false;
+                const uint32_t base = dev::smem_addr(smem + L.sfb_off);
+                for (int t = 0; t < p.sfb_atoms && ok; ++t)
+                    dev::tc_copy_32x128b_x4(tmem + kSfbCol + 4 * t,
+                                            dev::smem_desc(base + t * kSfAtom, 16, 128, dev::kLayoutNone));
+            }
+            const bool fast = p.kchunks == 1 && p.sfb_resident && p.epi_release;
+            if (fast) {
+                // D = 128 hot loop: one K chunk per tile, resident centroid scales,
+                // ring slots freed by the epilogue -- per tile only the two
+                // barrier tests, four MMAs and one commit remain.
+                const uint64_t bdesc_base = dev::smem_desc(dev::smem_addr(smem + L.b_off), 16, 1024,
+                                                           dev::kLayoutSwizzle128);
+                const uint32_t sfa = tmem + kSfaCol;
+                int slot = 0;
+                uint32_t bph = 0;
+                for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+                    const int as = p.a_stages == 2 ? (it & 1) : 0;
+                    const uint32_t aph = (uint32_t)(p.a_stages == 2 ? (it >> 1) : it) & 1u;
+                    if (!dev::mbar_wait_lean(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
+                    dev::tc_fence_after();
+                    const uint32_t a_off = L.a_off + (uint32_t)as * kATileBytes;
+                    dev::tc_copy_32x128b_x4(sfa, dev::smem_desc(dev::smem_addr(smem + L.sfa_off + (uint32_t)as * kSfAtom),
+                                                                16, 128, dev::kLayoutNone));
+                    const uint64_t adesc = dev::smem_desc(dev::smem_addr(smem + a_off), 16, 1024, dev::kLayoutSwizzle128);
+                    int ct = sweep0[as];
+                    uint32_t sfb = tmem + kSfbCol + (uint32_t)(ct * kSfbChunkCols);
+                    for (int i = 0; i < tiles_n; ++i) {
+                        if (!dev::mbar_wait_lean(&acc_empty[s], sph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                        dev::tc_fence_after();
+                        if (!dev::mbar_wait_lean(&b_full[slot], bph, abort_flag, p.err)) { ok = false; break; }
+                        const uint64_t bdesc = bdesc_base + (uint64_t)(slot * (kBTileBytes >> 4));
+                        const uint32_t d = tmem + (s ? (uint32_t)kBN : 0u);
+#pragma unroll
+                        for (int kb = 0; kb < 4; ++kb)
+                            dev::tc_mma_mx(d, adesc + 2u * kb, bdesc + 2u * kb, idesc0 | dev::mx_idesc_sf((uint32_t)kb),
+                                           sfa | ((uint32_t)kb << 30), sfb | ((uint32_t)kb << 30), kb != 0);
+                        dev::tc_commit(&acc_full[s]);
+                        s ^= 1;
+                        sph ^= (uint32_t)(s == 0);
+                        if (++slot == kBStages) slot = 0, bph ^= 1u;
+                        if (++ct == tiles_n) ct = 0, sfb = tmem + kSfbCol;
+                        else sfb += kSfbChunkCols;
+                    }
+                    if (ok) dev::tc_commit(&a_empty[as]);
+                }
+            }
+            for (int64_t tile = blockIdx.x; tile < tiles_m && ok && !fast; tile += gridDim.x, ++it) {
                 const int as = p.a_stages == 2 ? (it & 1) : 0;
                 const uint32_t aph = (uint32_t)(p.a_stages == 2 ? (it >> 1) : it) & 1u;
                 if (!dev::mbar_wait_lean(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
@@ -426,17 +580,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     dev::tc_copy_32x128b_x4(tmem + kSfaCol + 4 * kc,
                                             dev::smem_desc(sfa_base + kc * kSfAtom, 16, 128, dev::kLayoutNone));
                 const uint64_t adesc0 = dev::smem_desc(a_base, 16, 1024, dev::kLayoutSwizzle128);
-                for (int i = 0; i < tiles_n && ok; ++i) {
+                int ct = sweep0[as];
+                for (int i = 0; i < tiles_n && ok; ++i, ct = ct + 1 == tiles_n ? 0 : ct + 1) {
                     if (!dev::mbar_wait_lean(&acc_empty[s], sph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     dev::tc_fence_after();
                     const uint32_t d_tmem = tmem + (uint32_t)s * kBN;
                     for (int kc = 0; kc < p.kchunks; ++kc) {
                         if (!dev::mbar_wait_lean(&b_full[brd.slot], brd.phase, abort_flag, p.err)) { ok = false; break; }
-                        const uint32_t sfb = dev::smem_addr(smem + L.sfb_off + brd.slot * kBAtoms * kSfAtom);
+                        uint32_t sfb_col = tmem + kSfbCol + (uint32_t)((ct * p.kchunks + kc) * kSfbChunkCols);
+                        if (!p.sfb_resident) {
+                            sfb_col = tmem + kSfbCol;
+                            const uint32_t sfb = dev::smem_addr(smem + L.sfb_off + brd.slot * kBAtoms * kSfAtom);
 #pragma unroll
-                        for (int t = 0; t < kBAtoms; ++t)
-                            dev::tc_copy_32x128b_x4(tmem + kSfbCol + 4 * t,
-                                                    dev::smem_desc(sfb + t * kSfAtom, 16, 128, dev::kLayoutNone));
+                            for (int t = 0; t < kBAtoms; ++t)
+                                dev::tc_copy_32x128b_x4(sfb_col + 4 * t,
+                                                        dev::smem_desc(sfb + t * kSfAtom, 16, 128, dev::kLayoutNone));
+                        }
                         // +32 bytes along K = +2 in a descriptor's address field
                         const uint64_t adesc = adesc0 + (uint64_t)(kc * (kATileBytes >> 4));
                         const uint64_t bdesc = dev::smem_desc(dev::smem_addr(smem + L.b_off + brd.slot * kBTileBytes),
@@ -445,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int kb = 0; kb < 4; ++kb)
                             dev::tc_mma_mx(d_tmem, adesc + 2u * kb, bdesc + 2u * kb, idesc0 | dev::mx_idesc_sf((uint32_t)kb),
                                            (tmem + kSfaCol + 4 * kc) | ((uint32_t)kb << 30),
-                                           (tmem + kSfbCol) | ((uint32_t)kb << 30), (kc | kb) != 0);
+                                           sfb_col | ((uint32_t)kb << 30), (kc | kb) != 0);
                         if (!p.epi_release) dev::tc_commit(&b_empty[brd.slot]);
                         brd.advance(1);
                     }
@@ -461,18 +620,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             dev::mbar_wait(drain, 0, &no_abort, p.err);
         }
         __syncwarp();
+    }
     } else {
         // ------------------------------------------------------------ epilogue
+        if constexpr (kArgmin) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
         // Warp (q, j): TMEM lane quadrant q = warp % 4 (the only lanes it may
         // read), columns [64 j, 64 j + 64) of every accumulator tile.  All three
         // warps of a quadrant drain each tile together, so a stage is held only
         // for two 32-column loads.
         const int q = warp & 3;
-        const int j = (warp - 2) >> 2;
+        const int j = (warp - kEpiWarp0) >> 2;
         const int r = q * 32 + lane;     // row within the point tile
         float4* merge = reinterpret_cast<float4*>(smem + L.merge_off);
         float2* seed = reinterpret_cast<float2*>(smem + L.seed_off);
-        const float* cn_base = p.cn_smem ? reinterpret_cast<const float*>(smem + L.cn_off) : p.cn;
+        const uint32_t cn_saddr = dev::smem_addr(smem + L.cn_off);
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * kSliceCols);
         // After each row tile's first (hinted) centroid tile the quadrant's three
         // warps swap their running minima, so each then starts from the likely
@@ -481,6 +642,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // One warp hands the tile's centroid-ring slots back to the producer:
         // acc_full means every MMA that read them has completed.
         const bool releaser = p.epi_release && q == 0 && j == 0 && lane == 0;
+        float cmax = 0.0f;
+        for (int w = 0; w < kThreads / 32; ++w) {
+            const float c = warp_cmax[w];
+            cmax = c > cmax || c != c ? c : cmax;
+        }
         RingPos rel{0, 0u, kBStages};
         int s = 0;           // accumulator stage of the next tile
         uint32_t sph = 0;
@@ -497,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pn = p.pn[point];
             }
             const uint64_t pn2 = dev::pack2(pn, pn);
+            const float pc = pn + cmax;
             RowMin m{__int_as_float(0x7f800000), -1e38f, -1e38f, 0x7fffffff};
             const int ct0 = sweep_start(p, tile, mrows, tiles_n);
             for (int i = 0; i < tiles_n; ++i) {
@@ -535,10 +702,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     if (cc + c < p.n) orow[cc + c] = __uint_as_float(v[sub][c]);
                             }
                         }
-                    } else if (cc + 32 <= p.n) {
-                        argmin_chunk32<kGaps>(v[sub], cn_base + cc, pn2, cc, m);
-                    } else if (cc < p.n) {
-                        argmin_tail<kGaps>(v[sub], cn_base + cc, pn, cc, p.n, m);
+                    } else if (p.cn_smem) {
+                        fold_chunk<kGaps>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m);
+                    } else {
+                        fold_chunk<kGaps>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m);
                     }
                 }
                 if (seeding && i == 0) {
@@ -649,7 +816,12 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     // Shared-memory plan: two point-tile stages when they fit, the centroid norms
     // when they fit, then as deep a centroid-chunk ring as the rest allows
     // (deeper rings keep more TMA bytes in flight per SM).
-    auto fits = [&](int as, int cn, int bs) { return (int)smem_layout(p.kchunks, as, cn, bs).total + 1024 <= max_smem; };
+    const int64_t tiles_n = (n + kBN - 1) / kBN;
+    p.sfb_resident = tiles_n * p.kchunks <= kMaxResidentSfb;
+    auto sfb_atoms = [&](int bs) { return p.sfb_resident ? (int)(tiles_n * p.kchunks * kBAtoms) : bs * kBAtoms; };
+    auto fits = [&](int as, int cn, int bs) {
+        return (int)smem_layout(p.kchunks, as, cn, bs, sfb_atoms(bs)).total + 1024 <= max_smem;
+    };
     p.cn_smem = (argmin && n <= kMaxSmemNorms) ? (int)n : 0;
     p.a_stages = fits(2, p.cn_smem, 4) ? 2 : 1;
     if (!fits(p.a_stages, p.cn_smem, 4)) p.cn_smem = 0;
@@ -659,10 +831,12 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     // A slot freed only when its whole tile completes needs room for the next
     // tile's chunks too; otherwise each chunk is freed by its own commit.
     p.epi_release = p.b_stages >= 2 * p.kchunks;
+    p.sfb_atoms = sfb_atoms(p.b_stages);
     // At least 116 KB so that no second CTA shares the SM (each CTA holds all
     // 512 TMEM columns while it runs).
     const uint32_t smem_bytes =
-        std::max<uint32_t>(smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages).total + 1024, 116u * 1024u);
+        std::max<uint32_t>(smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms).total + 1024,
+                           116u * 1024u);
     if ((int)smem_bytes > max_smem) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: shared memory budget exceeded");
 
     const int64_t tiles_m = (m + kBM - 1) / kBM;
@@ -694,6 +868,15 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
 
     auto launch = [&](auto kernel, const char* name) -> int {
         MXK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
+        if (argmin) {
+            // the setmaxnreg split assumes exactly kLaunchRegs registers at launch
+            cudaFuncAttributes attr{};
+            MXK_CUDA(cudaFuncGetAttributes(&attr, kernel));
+            if (attr.numRegs != kLaunchRegs)
+                return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: argmin kernel built with " + std::to_string(attr.numRegs) +
+                                                     " registers, the register split needs " +
+                                                     std::to_string(kLaunchRegs));
+        }
         LaunchScope scope(name, stream);
         kernel<<<grid, kThreads, smem_bytes, stream>>>(tmap_a, tmap_b, p);
         MXK_CUDA(cudaGetLastError());
