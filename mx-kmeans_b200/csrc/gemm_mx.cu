@@ -203,20 +203,11 @@ __global__ void __launch_bounds__(256) scales_to_atoms_kernel(int64_t rows, int 
     }
 }
 
-// First centroid tile of the sweep for point tile `tile`: the tile holding the
-// hint label of the tile's first row (the driver passes the previous
-// iteration's labels, and rows are ordered by them, so that tile usually holds
-// every row's nearest centroid and later chunks rarely improve a row).  Any
-// start gives the same result: ties are broken by index, not by sweep order.
-__device__ __forceinline__ int sweep_start(const GemmParams& p, int64_t tile, int64_t mrows, int tiles_n) {
-    if (!p.start_hint) return 0;
-    const int64_t row0 = tile * kBM;
-    if (row0 >= mrows) return 0;
-    const int64_t point = p.pid ? (int64_t)p.pid[row0] : row0;
-    const int lab = p.start_hint[point];
-    if (lab < 0 || (int64_t)lab >= p.n) return 0;
-    return lab / kBN;
-}
+// Sweep start: every 128-row point tile sweeps the centroid tiles beginning with
+// the one holding the hint label of its first row (the driver passes the
+// previous iteration's labels, and rows are ordered by them, so that tile usually
+// holds every row's nearest centroid and later chunks rarely improve a row).
+// Any start gives the same result: ties are broken by index, not by sweep order.
 
 // Centroid norms: staged in shared memory (read with ld.shared through the
 // shared-window address) or read from global memory.
@@ -443,7 +434,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             dev::mbar_arrive_expect_tx(sfb_full, bytes);
             dev::bulk_load(smem + L.sfb_off, p.b_scales, bytes, sfb_full);
         }
+        // Sweep starts come from two dependent global loads (the lead row's point
+        // id, then its hint); they are software-pipelined two row tiles ahead.
+        const int64_t step = gridDim.x;
+        auto lead_id = [&](int64_t t) -> int64_t {
+            if (!p.start_hint || t >= tiles_m || lane != 0) return -1;
+            return p.pid ? (int64_t)p.pid[t * kBM] : t * kBM;
+        };
+        auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        int hint_cur = hint_of(lead_id(blockIdx.x));
+        int64_t lead_nxt = lead_id(blockIdx.x + step);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+            const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
+            hint_cur = hint_of(lead_nxt);
+            lead_nxt = lead_id(tile + 2 * step);
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
             if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
@@ -464,7 +468,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.a_bits != 8)
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
-            const int ct0 = lane == 0 ? sweep_start(p, tile, mrows, tiles_n) : 0;
             if (lane == 0) sweep0[as] = ct0;  // published to the MMA thread by the a_full arrival
             dev::fence_proxy_async();
             __syncwarp();
@@ -652,20 +655,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t sph = 0;
         bool ok = true;
         int it = 0;
+        // Per-row-tile inputs (the row's point id and norm, the sweep start)
+        // come from dependent global loads; they are software-pipelined: ids
+        // two row tiles ahead, norms and hints one ahead, so no warp stalls on
+        // them while its accumulator stage waits to be drained.
+        const int64_t step = gridDim.x;
+        auto row_id = [&](int64_t t) -> int64_t {  // point id of this lane's row of tile t (-1: none)
+            const int64_t g = t * kBM + r;
+            if (!kArgmin || t >= tiles_m || g >= mrows) return -1;
+            return p.pid ? (int64_t)p.pid[g] : g;
+        };
+        auto lead_id = [&](int64_t t) -> int64_t {  // point id of tile t's first row (-1: no hint)
+            if (!p.start_hint || t >= tiles_m) return -1;
+            return p.pid ? (int64_t)p.pid[t * kBM] : t * kBM;
+        };
+        auto norm_of = [&](int64_t id) -> float { return id >= 0 ? p.pn[id] : 0.0f; };
+        auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        int64_t id_cur = row_id(blockIdx.x), lead_cur = lead_id(blockIdx.x);
+        float pn_cur = norm_of(id_cur);
+        int hint_cur = hint_of(lead_cur);
+        int64_t id_nxt = row_id(blockIdx.x + step), lead_nxt = lead_id(blockIdx.x + step);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int buf = it & 1;
             const int64_t grow = tile * kBM + r;
             const bool valid = grow < mrows;
-            int64_t point = grow;
-            float pn = 0.0f;
-            if (kArgmin && valid) {
-                point = p.pid ? (int64_t)p.pid[grow] : grow;
-                pn = p.pn[point];
-            }
+            const int64_t point = kArgmin && valid ? id_cur : grow;
+            const float pn = pn_cur;
+            const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
+            // issue the next row tiles' loads now; they are consumed an iteration later
+            const float pn_nxt = norm_of(id_nxt);
+            const int hint_nxt = hint_of(lead_nxt);
+            const int64_t id_nn = row_id(tile + 2 * step), lead_nn = lead_id(tile + 2 * step);
             const uint64_t pn2 = dev::pack2(pn, pn);
             const float pc = pn + cmax;
             RowMin m{__int_as_float(0x7f800000), -1e38f, -1e38f, 0x7fffffff};
-            const int ct0 = sweep_start(p, tile, mrows, tiles_n);
             for (int i = 0; i < tiles_n; ++i) {
                 const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
                 if (!dev::mbar_wait(&acc_full[s], sph, abort_flag, p.err)) { ok = false; break; }
@@ -684,9 +707,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) dev::mbar_arrive(&acc_empty[s]);
                 if (++s == kAccStages) s = 0, sph ^= 1u;
+                const int slice0 = ct * kBN + j * kSliceCols;
 #pragma unroll
                 for (int sub = 0; sub < 2; ++sub) {
-                    const int cc = ct * kBN + j * kSliceCols + sub * 32;
+                    const int cc = slice0 + sub * 32;
                     if constexpr (!kArgmin) {
                         if (valid) {
                             float* orow = p.out + grow * p.n;
@@ -747,6 +771,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            id_cur = id_nxt, lead_cur = lead_nxt, pn_cur = pn_nxt, hint_cur = hint_nxt;
+            id_nxt = id_nn, lead_nxt = lead_nn;
         }
     }
 
