@@ -281,8 +281,7 @@ def main():
     else:
         g = torch.Generator(device=dev).manual_seed(SEED)
         c_init = x_full[torch.randperm(n, generator=g, device=dev)[:K_CLUSTERS]].clone()
-    row0 = n // world * rank + min(rank, n % world)
-    rows = n // world + (1 if rank < n % world else 0)
+    row0, rows = mxk.shard_rows(n, world, rank)
     x = x_full[row0:row0 + rows].contiguous()
     del x_full
     torch.cuda.empty_cache()
@@ -291,11 +290,7 @@ def main():
     stream = torch.cuda.current_stream()
     opts = mxk.Options(max_iterations=ITERS, tolerance=0.0)
 
-    comm = None
-    if world > 1:
-        uid = [mxk.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        comm = mxk.Comm(world, rank, uid[0])
+    comm = mxk.bootstrap_comm() if world > 1 else None
 
     def step():
         cent.copy_(c_init)

@@ -194,6 +194,27 @@ class Comm:
             self.handle = ctypes.c_void_p()
 
 
+def shard_rows(n, world, rank):
+    """Rows of one rank in the row-sharded path: contiguous shards of n // world
+    rows, the first n % world ranks one row more.  -> (first_row, row_count)."""
+    if n < 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"shard_rows: bad arguments n={n} world={world} rank={rank}")
+    base, extra = divmod(n, world)
+    return rank * base + min(rank, extra), base + (1 if rank < extra else 0)
+
+
+def bootstrap_comm(group=None):
+    """This rank's NCCL communicator for kmeans_mixed_sharded.  Rank 0 creates the
+    unique id and broadcasts it over an initialized torch.distributed process group
+    (any backend, so a gloo group on the host works); a rank that never joins makes
+    the broadcast fail with the group's timeout instead of hanging.  -> Comm"""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    uid = [comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    return Comm(world, rank, uid[0])
+
+
 def kmeans_mixed_sharded(comm, points, centroids, labels, options=None, stream=None):
     opts = options or Options()
     iters = ctypes.c_int(0)
