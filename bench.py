@@ -48,6 +48,20 @@ def parse():
     return p.parse_args()
 
 
+def measured_traffic(rows):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one full-size fused-GEMM
+    launch, from the ncu capture summarised in profiles/ (scaled to `rows`: every
+    byte it counts is per point row); None if the summary is missing."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "mx_gemm_argmin_config4.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_full_launch:"):
+                return float(line.split(":")[1]) * rows / N_POINTS
+    except OSError:
+        pass
+    return None
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -341,15 +355,17 @@ def main():
     gemm = stats.get("mx_gemm_argmin")
     roofline = None
     if gemm and gemm[0]:
-        per_launch_ms = gemm[1] / gemm[0]
         # one launch per precision group per iteration; only the MXFP8 group is non-empty
         launches_nonempty = iters
         flops_per_iter = 2.0 * rows * K_CLUSTERS * D_PAD
         achieved = flops_per_iter * launches_nonempty / (gemm[1] / 1e3) / 1e12
         peak = 2.0 * pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        traffic = measured_traffic(rows)
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": None,
-                    "kernel": "mx_gemm_argmin", "launch_ms_avg": per_launch_ms,
+                    "frac": achieved / peak, "traffic": traffic,
+                    "traffic_unit": "DRAM bytes per non-empty launch (ncu capture scaled to these rows; "
+                                    "profiles/mx_gemm_argmin_config4.md)",
+                    "kernel": "mx_gemm_argmin", "ms_per_iteration": gemm[1] / max(iters, 1),
                     "flops_per_iteration": flops_per_iter,
                     "peak_source": f"2 x bf16_tflops_sustained of {pk_kind} MEASURED_PEAKS.json "
                                    "(dense MXFP8 tensor rate is twice BF16)"}
