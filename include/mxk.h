@@ -67,6 +67,13 @@ int mxk_precompute_point_bounds(int64_t n, int d, const float* points, const flo
 int mxk_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc,
                           float ec, int* precision, void* stream);
 
+/* Self-check, no reference counterpart: runs every float32 bit pattern through
+ * the division-free MXFP8 scale rule of mxk_assign_f32_fused's in-kernel
+ * quantizer and through ue8m0(amax / 448), the rule of quantize_rows
+ * (src/kernels/quantize.cu:33-43).  result: 2 device words, [0] = number of
+ * disagreements, [1] = smallest disagreeing pattern (all ones when none). */
+int mxk_check_mxfp8_scale_codec(unsigned long long* result, void* stream);
+
 /* gemm_mx, include/kmeans.cuh:46-47 / src/kernels/gemm.cu:348-363.
  * out[m x n] (row-major FP32) = A[m x k] (packed MX{bits}) . B[n x k]^T (MXFP8),
  * scales row-major per 32 features.  tcgen05 block-scaled MMA; k % 128 == 0. */
@@ -113,13 +120,23 @@ int mxk_centroid_shift_noalloc(int64_t elements, const float* previous, const fl
  * lowest-index argmin in the epilogue.  Writes labels[pid[r]] and, when gaps is
  * not NULL, the two-largest gap (init -1e38) like assign_clusters.
  * start_hint (optional, one label per point, may alias labels): every 128-row
- * tile sweeps the centroids starting at the 128-centroid tile of its first
+ * tile sweeps the centroids starting at the 192-centroid tile of its first
  * row's hint -- previous labels make the sweep find the minimum early; the
  * result does not depend on the hint. */
 int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, const uint8_t* a_scales,
                         const uint8_t* b, const uint8_t* b_scales, const float* point_norms,
                         const float* centroid_norms, const int* pid, int* labels, float* gaps,
                         const int* start_hint, void* stream);
+
+/* mxk_assign_mx_fused with the point quantization inside the kernel (no
+ * counterpart in the reference, whose Lloyd step runs quantize_rows and then the
+ * GEMM): `rows` FP32 points (points[pid[r]], or points[r] without pid; n_points
+ * rows of d floats) are MXFP8-encoded in shared memory with the bytes
+ * quantize_rows would produce, so the result equals quantize_rows(8, ...) followed
+ * by mxk_assign_mx_fused.  d must be 128. */
+int mxk_assign_f32_fused(int64_t rows, int k, int d, const float* points, int64_t n_points, const uint8_t* b,
+                         const uint8_t* b_scales, const float* point_norms, const float* centroid_norms,
+                         const int* pid, int* labels, float* gaps, const int* start_hint, void* stream);
 
 /* ---- Lloyd driver --------------------------------------------------------- */
 

@@ -165,6 +165,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// TMA gather of four rows (y0..y3) of a 2-D tensor map whose box is one row
+// high; the four box rows land consecutively at dst.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int32_t x, int32_t y0, int32_t y1,
+                                            int32_t y2, int32_t y3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_addr(bar))
+        : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned, size % 16 == 0),
 // completion signalled on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -270,6 +281,12 @@ __device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "r"(saddr));
     return r;
 }
+__device__ __forceinline__ void sts_u32(uint32_t saddr, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts_u8(uint32_t saddr, uint32_t v) {
+    asm volatile("st.shared.u8 [%0], %1;" ::"r"(saddr), "r"(v) : "memory");
+}
 __device__ __forceinline__ float lds_f1(uint32_t saddr) {
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(saddr));
@@ -286,6 +303,17 @@ __device__ __forceinline__ void key2(uint32_t v0, uint32_t v1, float c0, float c
         "mov.b64 {%0, %1}, d;\n\t}"
         : "=f"(k0), "=f"(k1)
         : "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
+}
+
+// (x0, x1) *= s with one .f32x2 multiply; each lane is rounded like the scalar multiply.
+__device__ __forceinline__ void mul2(float& x0, float& x1, float s) {
+    asm("{\n\t.reg .b64 v, m;\n\t"
+        "mov.b64 v, {%0, %1};\n\t"
+        "mov.b64 m, {%2, %2};\n\t"
+        "mul.rn.f32x2 v, v, m;\n\t"
+        "mov.b64 {%0, %1}, v;\n\t}"
+        : "+f"(x0), "+f"(x1)
+        : "f"(s));
 }
 
 __device__ __forceinline__ float min3f(float a, float b, float c) {

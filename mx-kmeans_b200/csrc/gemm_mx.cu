@@ -33,8 +33,8 @@
 //               their minima; the j = 0 warp merges the three slices and writes
 //               the label.  One warp hands centroid-ring slots back to the
 //               producer once their tile's MMAs have completed.
-// Argmin kernels rebalance registers with setmaxnreg (warpgroup 0: 56,
-// epilogue warpgroups: 152).
+// Argmin kernels rebalance registers with setmaxnreg (warpgroup 0: 80,
+// epilogue warpgroups: 144).
 #include <cstring>
 
 #include "common.cuh"
@@ -61,10 +61,10 @@ constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 // Register split (setmaxnreg, argmin kernels): launched at 128 per thread, the
 // first warpgroup drops to kLowRegs and the three epilogue warpgroups rise to
 // kHighRegs.  Per SM sub-partition (one warp of each warpgroup) that is
-// 56 + 3 * 152 = 512 = 4 * 128 registers per lane, exactly the launch budget.
+// 80 + 3 * 144 = 512 = 4 * 128 registers per lane, exactly the launch budget.
 constexpr int kLaunchRegs = 128;
-constexpr int kLowRegs = 56;
-constexpr int kHighRegs = 152;
+constexpr int kLowRegs = 80;
+constexpr int kHighRegs = 144;
 static_assert(kLowRegs + 3 * kHighRegs == 4 * kLaunchRegs, "register split must equal the launch budget");
 constexpr int kMaxSmemNorms = 8192;      // centroid norms staged in shared memory up to this k
 constexpr int kMaxChunks = 8;            // K <= 1024
@@ -97,6 +97,9 @@ struct GemmParams {
     int sfb_resident; // every centroid scale atom sits in TMEM for the whole kernel (tiles_n *
                       // kchunks <= kMaxResidentSfb); else each ring slot carries its tile's atoms
     int sfb_atoms;    // scale atoms in the shared-memory centroid-scale region
+    int fuse_x;       // the point tile is quantized in the kernel from FP32 rows (tmap_x, D = 128,
+                      // MXFP8): gathered by pid, encoded exactly as quantize_rows, no separate pass
+    int64_t xrows;    // rows of the FP32 point matrix (a gather at this row reads zeros)
     const float* pn;
     const float* cn;
     const int* pid;
@@ -118,18 +121,19 @@ struct RingPos {
 };
 
 struct SmemLayout {
-    uint32_t a_off, b_off, sfa_off, sfb_off, merge_off, seed_off, cn_off, bar_off, total;
+    uint32_t a_off, b_off, x_off, sfa_off, sfb_off, merge_off, seed_off, cn_off, bar_off, total;
 };
 
 // cn_floats: centroid norms staged in shared memory (0 when read from global).
 // sfb_atoms: centroid scale atoms held in shared memory -- all of them (resident
 // mode, staged once) or kBAtoms per ring slot.
 __host__ __device__ inline SmemLayout smem_layout(int kchunks, int a_stages, int cn_floats, int b_stages,
-                                                  int sfb_atoms) {
+                                                  int sfb_atoms, int fuse_x) {
     SmemLayout s;
     s.a_off = 0;  // every operand tile starts on a 1024-byte boundary (SWIZZLE_128B atoms)
     s.b_off = s.a_off + a_stages * kchunks * kATileBytes;
-    s.sfa_off = s.b_off + b_stages * kBTileBytes;
+    s.x_off = s.b_off + b_stages * kBTileBytes;   // FP32 staging of one point tile (fused quantize)
+    s.sfa_off = s.x_off + (fuse_x ? kBM * kChunk * 4 : 0);
     s.sfb_off = s.sfa_off + a_stages * kchunks * kSfAtom;
     s.merge_off = s.sfb_off + sfb_atoms * kSfAtom;           // [2 buffers][2 depositors][128 rows] x 16 B
     s.seed_off = s.merge_off + 2 * 2 * kBM * 16;              // [2 buffers][3 warps][128 rows] x 8 B
@@ -352,10 +356,10 @@ __device__ __forceinline__ void merge_rowmin(RowMin& m, float d, int b, float l,
 template <bool kArgmin, bool kGaps>
 __global__ void __launch_bounds__(kThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms);
+    const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms, p.fuse_x);
     const int kBStages = p.b_stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* a_full = bars;                 // [2]
@@ -369,11 +373,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* merge_empty = merge_full + 8;  // [q * 2 + row-tile parity] merging warp has read the deposits
     uint64_t* seed_bar = merge_empty + 8;    // [q] the quadrant's three first-tile minima are published
     uint64_t* sfb_full = seed_bar + 4;       // resident centroid scales have landed in shared memory
+    uint64_t* x_full = sfb_full + 1;         // [8] 16 FP32 rows of a quantizer warp gathered (fused quantize)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
     volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [2] per A stage
     float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 4;             // [kThreads / 32]
-    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 <= kNumBars, "barrier slots");
+    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 8 <= kNumBars, "barrier slots");
     static_assert(4 + kThreads / 32 <= 32, "words after the barriers");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -382,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tiles_n = (int)((p.n + kBN - 1) / kBN);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) dev::mbar_init(&a_full[i], 1), dev::mbar_init(&a_empty[i], 1);
+        // fused quantize: the two quantizer warps arrive
+        for (int i = 0; i < 2; ++i) dev::mbar_init(&a_full[i], p.fuse_x ? 2 : 1), dev::mbar_init(&a_empty[i], 1);
         for (int i = 0; i < kBStages; ++i) dev::mbar_init(&b_full[i], 1), dev::mbar_init(&b_empty[i], 1);
         for (int i = 0; i < kAccStages; ++i)
             dev::mbar_init(&acc_full[i], 1), dev::mbar_init(&acc_empty[i], kEpiWarps);
@@ -393,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int q = 0; q < 4; ++q) dev::mbar_init(&seed_bar[q], kEpiPerQuad);
         dev::mbar_init(sfb_full, 1);
+        for (int i = 0; i < 8; ++i) dev::mbar_init(&x_full[i], 1);
         *abort_flag = 0;
         dev::fence_barrier_init();
     }
@@ -413,7 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) warp_cmax[warp] = cmax;
     }
     if (warp == 0 && lane == 0) {
-        if (p.a_bits == 8) dev::prefetch_tensor_map(&tmap_a);
+        if (p.fuse_x) dev::prefetch_tensor_map(&tmap_x);
+        else if (p.a_bits == 8) dev::prefetch_tensor_map(&tmap_a);
         dev::prefetch_tensor_map(&tmap_b);
     }
     dev::tc_fence_before();
@@ -450,10 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             lead_nxt = lead_id(tile + 2 * step);
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
-            if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+            // (fused quantize: the quantizer warps own the point tile and its sweep start)
+            if (!p.fuse_x && !dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             uint8_t* a_smem = smem + L.a_off + (uint32_t)as * p.kchunks * kATileBytes;
             uint8_t* sfa = smem + L.sfa_off + (uint32_t)as * p.kchunks * kSfAtom;
-            if (lane == 0) {
+            if (p.fuse_x) {
+            } else if (lane == 0) {
                 const uint32_t bytes = (p.a_bits == 8 ? p.kchunks * kATileBytes : 0) + p.kchunks * kSfAtom;
                 if (bytes)
                     asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(dev::smem_addr(&a_full[as])),
@@ -465,13 +475,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dev::bulk_load(sfa, p.a_scales + tile * p.kchunks * kSfAtom, (uint32_t)(p.kchunks * kSfAtom),
                                &a_full[as]);
             }
-            if (p.a_bits != 8)
+            if (p.a_bits != 8 && !p.fuse_x)
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
-            if (lane == 0) sweep0[as] = ct0;  // published to the MMA thread by the a_full arrival
-            dev::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) dev::mbar_arrive(&a_full[as]);
+            if (!p.fuse_x) {
+                if (lane == 0) sweep0[as] = ct0;  // published to the MMA thread by the a_full arrival
+                dev::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) dev::mbar_arrive(&a_full[as]);
+            }
             // Centroid chunks: one thread walks the ring.  A slot is handed back by
             // the epilogue once the tile that read it has completed, or by the MMA
             // thread's per-chunk commit when the ring holds less than two tiles.
@@ -623,6 +635,127 @@ __global__ void __launch_bounds__(kThreads, 1)
             dev::mbar_wait(drain, 0, &no_abort, p.err);
         }
         __syncwarp();
+    } else if (p.fuse_x) {
+        // ------------------------------------------------------------ quantizers
+        // Warps 2 and 3 encode the gathered FP32 rows (rows 64 (w-2) .. +63) into
+        // the MXFP8 point tile and its scale atom, with the arithmetic of
+        // quantize_rows: per 32-feature block the UE8M0 scale of amax / 448 (1 for
+        // an all-zero block; computed from amax's bits, see ue8m0_mxfp8_scale),
+        // values times its exact reciprocal, E4M3 round-to-nearest-even saturating.
+        // One lane owns one (row, block) pair per pass of 8 rows: lane L takes
+        // row 8 g + (L & 7) and block L >> 3, so the block maximum needs no
+        // shuffle.  The staging rows are 512 B apart; lane L reads its eight
+        // 16-byte chunks starting at chunk (L & 7), so the 8 lanes of each
+        // shared-memory phase hit 8 different bank groups.
+        // The warp's 64 staging rows form 4 groups of 16 with one barrier each;
+        // as soon as a group is encoded, its rows of the next tile are gathered
+        // (lanes 0-3, four rows each), so the copies overlap the encoding.
+        constexpr int kRowsPerWarp = kBM / 2;  // 64
+        constexpr int kGroupRows = 16;
+        constexpr int kGroups = kRowsPerWarp / kGroupRows;  // 4
+        static_assert(2 * kRowsPerWarp == kBM && kChunk == 128 && kGroups * kGroupRows == kRowsPerWarp,
+                      "quantizer row split");
+        const int r0 = (warp - 2) * kRowsPerWarp;
+        uint64_t* xf = x_full + (warp - 2) * kGroups;
+        uint32_t outstanding = 0;  // bit G: a gather into group G is in flight
+        uint32_t xphase = 0;       // bit G: parity of group G's next completion
+        auto gather = [&](int64_t t, int grp) {
+            const int gr = r0 + grp * kGroupRows;  // first staging row of the group
+            if (lane == 0) dev::mbar_arrive_expect_tx(&xf[grp], (uint32_t)(kGroupRows * kChunk * 4));
+            __syncwarp();
+            if (lane < kGroupRows / 4) {
+                int32_t y[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t g = t * kBM + gr + 4 * lane + u;  // < t * kBM + kBM
+                    y[u] = g < mrows ? (p.pid ? p.pid[g] : (int32_t)g) : (int32_t)p.xrows;  // past the end: zeros
+                }
+                // staging rows gr + 4 lane .. + 3 <= 127: inside the 64 KB buffer
+                uint8_t* dst = smem + L.x_off + (uint32_t)(gr + 4 * lane) * kChunk * 4u;
+                dev::tma_gather4(dst, &tmap_x, 0, y[0], y[1], y[2], y[3], &xf[grp]);
+            }
+            outstanding |= 1u << grp;
+        };
+        // sweep starts (warp 2 publishes them), pipelined like the producer's
+        const int64_t step = gridDim.x;
+        auto lead_id = [&](int64_t t) -> int64_t {
+            if (!p.start_hint || t >= tiles_m || lane != 0 || warp != 2) return -1;
+            return p.pid ? (int64_t)p.pid[t * kBM] : t * kBM;
+        };
+        auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        int hint_cur = hint_of(lead_id(blockIdx.x));
+        int64_t lead_nxt = lead_id(blockIdx.x + step);
+        bool ok = true;
+        int it = 0;
+        if (blockIdx.x < tiles_m)
+            for (int grp = 0; grp < kGroups; ++grp) gather(blockIdx.x, grp);
+        const int blk = lane >> 3;      // 32-feature block of this lane
+        const uint32_t rot = lane & 7;  // first chunk read (row % 8 of this lane's rows)
+        const uint32_t xbase = dev::smem_addr(smem + L.x_off) + (uint32_t)(r0 + (lane & 7)) * (kChunk * 4) +
+                               (uint32_t)blk * 128u;
+        for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+            const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
+            hint_cur = hint_of(lead_nxt);
+            lead_nxt = lead_id(tile + 2 * step);
+            const int as = it % p.a_stages;
+            const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
+            if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+            const uint32_t a_tile = dev::smem_addr(smem + L.a_off + (uint32_t)as * kATileBytes);
+            const uint32_t sfa = dev::smem_addr(smem + L.sfa_off + (uint32_t)as * kSfAtom);
+            const bool refill = tile + gridDim.x < tiles_m;
+            for (int grp = 0; grp < kGroups && ok; ++grp) {
+                if (!dev::mbar_wait(&xf[grp], (xphase >> grp) & 1u, abort_flag, p.err)) { ok = false; break; }
+                xphase ^= 1u << grp;
+                outstanding &= ~(1u << grp);
+#pragma unroll 1
+                for (int pass = 0; pass < kGroupRows / 8; ++pass) {
+                    const int rbase = r0 + grp * kGroupRows + pass * 8;  // multiple of 8
+                    const int r = rbase + (lane & 7);
+                    const uint32_t src = xbase + (uint32_t)(grp * kGroupRows + pass * 8) * (kChunk * 4);
+                    float4 x[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) x[i] = dev::lds_f4(src + 16u * ((rot + i) & 7u));
+                    // fmaxf drops NaN in any order; starting from 0 the maximum is never NaN or -0
+                    float m[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        m[i] = fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w)));
+                    const float amax = fmaxf(fmaxf(fmaxf(fmaxf(0.0f, m[0]), fmaxf(m[1], m[2])),
+                                                   fmaxf(m[3], m[4])),
+                                             fmaxf(fmaxf(m[5], m[6]), m[7]));
+                    bool rare;
+                    uint32_t sc = dev::ue8m0_mxfp8_scale_common(amax, rare);
+                    if (__any_sync(0xffffffffu, rare)) {  // tiny or infinite maxima: warp-uniform detour
+                        if (rare) sc = dev::ue8m0_mxfp8_scale(amax);
+                    }
+                    const float rcp = dev::ue8m0_reciprocal(sc);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t c = (rot + i) & 7u;  // chunk held in x[i]: features 32 blk + 4 c ..
+                        dev::mul2(x[i].x, x[i].y, rcp);
+                        dev::mul2(x[i].z, x[i].w, rcp);
+                        const uint32_t lo = dev::e4m3x2_encode(x[i].x, x[i].y);
+                        const uint32_t hi = dev::e4m3x2_encode(x[i].z, x[i].w);
+                        dev::sts_u32(a_tile + sw128_offset(r, 32 * blk + 4 * (int)c), (lo & 0xffffu) | (hi << 16));
+                    }
+                    dev::sts_u8(sfa + ((r & 31) << 4) + ((r >> 5) << 2) + blk, sc);
+                }
+                // the group's staging rows are consumed: fetch the next tile's
+                __syncwarp();
+                if (refill) gather(tile + gridDim.x, grp);
+            }
+            if (!ok) break;
+            dev::fence_proxy_async();  // generic shared-memory writes -> visible to the tensor core
+            __syncwarp();
+            if (warp == 2 && lane == 0) sweep0[as] = ct0;  // published by the a_full arrival
+            if (lane == 0) dev::mbar_arrive(&a_full[as]);
+        }
+        // Unwinding after an abort: wait (bounded) for this warp's gathers in flight.
+        if (!ok && lane == 0) {
+            volatile int no_abort = 0;
+            for (int grp = 0; grp < kGroups; ++grp)
+                if ((outstanding >> grp) & 1u) dev::mbar_wait(&xf[grp], (xphase >> grp) & 1u, &no_abort, nullptr);
+        }
     }
     } else {
         // ------------------------------------------------------------ epilogue
@@ -788,15 +921,25 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 
 int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales, const uint8_t* b,
                    const uint8_t* b_scales, float* out, const MxArgmin* argmin, const int* rows_dev,
-                   cudaStream_t stream, bool scale_atoms) {
+                   cudaStream_t stream, bool scale_atoms, const float* points_f32, int64_t points_rows) {
     if (bits != 4 && bits != 6 && bits != 8) return fail(MXK_ERR_INVALID, "Precision must be 4, 6, or 8");
     if (m <= 0 || n <= 0) return MXK_OK;
     MXK_REQUIRE(k > 0 && k % kChunk == 0, "gemm_mx: k must be a positive multiple of 128");
     if (k / kChunk > kMaxChunks) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: k > 1024 is not supported");
-    MXK_REQUIRE(a && b && a_scales && b_scales, "gemm_mx: null operand");
-    MXK_REQUIRE(aligned(a, 16) && aligned(b, 16), "gemm_mx: operands must be 16-byte aligned");
-    MXK_REQUIRE(aligned(a_scales, scale_atoms ? 16 : 4) && aligned(b_scales, scale_atoms ? 16 : 4),
-                "gemm_mx: scales must be 4-byte aligned (16 for the atom layout)");
+    const bool fuse_x = points_f32 != nullptr;
+    if (fuse_x) {
+        MXK_REQUIRE(bits == 8 && k == kChunk && argmin, "fused quantize: MXFP8, d = 128 and the argmin epilogue only");
+        MXK_REQUIRE(aligned(points_f32, 16) && points_rows > 0 && points_rows < (1ll << 31),
+                    "fused quantize: points must be 16-byte aligned with 1..2^31-1 rows");
+        MXK_REQUIRE(argmin->pid || m <= points_rows, "fused quantize: more rows than points");
+    } else {
+        MXK_REQUIRE(a && a_scales, "gemm_mx: null operand");
+        MXK_REQUIRE(aligned(a, 16), "gemm_mx: operands must be 16-byte aligned");
+        MXK_REQUIRE(aligned(a_scales, scale_atoms ? 16 : 4), "gemm_mx: scales must be 4-byte aligned (16 for the atom layout)");
+    }
+    MXK_REQUIRE(b && b_scales, "gemm_mx: null operand");
+    MXK_REQUIRE(aligned(b, 16), "gemm_mx: operands must be 16-byte aligned");
+    MXK_REQUIRE(aligned(b_scales, scale_atoms ? 16 : 4), "gemm_mx: scales must be 4-byte aligned (16 for the atom layout)");
     MXK_REQUIRE(n < (1ll << 31) && m < (1ll << 31), "gemm_mx: m and n must be below 2^31 (TMA coordinates)");
     if (argmin) {
         MXK_REQUIRE(argmin->point_norms && argmin->centroid_norms && argmin->labels, "assign: null pointer");
@@ -805,11 +948,15 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         MXK_REQUIRE(out != nullptr, "gemm_mx: null output");
     }
 
-    CUtensorMap tmap_a, tmap_b;
+    CUtensorMap tmap_a, tmap_b, tmap_x;
     std::memset(&tmap_a, 0, sizeof(tmap_a));
-    if (bits == 8)
+    std::memset(&tmap_x, 0, sizeof(tmap_x));
+    if (bits == 8 && !fuse_x)
         MXK_CHECK(encode_tensor_map_2d(&tmap_a, a, (uint64_t)k, (uint64_t)m, (uint64_t)k, kChunk, kBM,
                                        CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
+    if (fuse_x)  // one-row box for tile::gather4; rows past points_rows read as zeros
+        MXK_CHECK(encode_tensor_map_2d(&tmap_x, points_f32, (uint64_t)k, (uint64_t)points_rows, (uint64_t)k * 4,
+                                       (uint32_t)k, 1, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_NONE));
     MXK_CHECK(encode_tensor_map_2d(&tmap_b, b, (uint64_t)k, (uint64_t)n, (uint64_t)k, kChunk, kBN,
                                    CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
 
@@ -825,6 +972,8 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     p.b_scales = b_scales;
     p.out = out;
     p.out_vec = out && aligned(out, 16) && (n % 4 == 0);
+    p.fuse_x = fuse_x;
+    p.xrows = points_rows;
     if (argmin) {
         p.pn = argmin->point_norms;
         p.cn = argmin->centroid_norms;
@@ -846,11 +995,13 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     p.sfb_resident = tiles_n * p.kchunks <= kMaxResidentSfb;
     auto sfb_atoms = [&](int bs) { return p.sfb_resident ? (int)(tiles_n * p.kchunks * kBAtoms) : bs * kBAtoms; };
     auto fits = [&](int as, int cn, int bs) {
-        return (int)smem_layout(p.kchunks, as, cn, bs, sfb_atoms(bs)).total + 1024 <= max_smem;
+        return (int)smem_layout(p.kchunks, as, cn, bs, sfb_atoms(bs), p.fuse_x).total + 1024 <= max_smem;
     };
     p.cn_smem = (argmin && n <= kMaxSmemNorms) ? (int)n : 0;
-    p.a_stages = fits(2, p.cn_smem, 4) ? 2 : 1;
-    if (!fits(p.a_stages, p.cn_smem, 4)) p.cn_smem = 0;
+    // (with the fused quantizer's 64 KB staging, two point stages leave room for
+    // three ring slots; a single point stage would serialize encoding and MMA)
+    p.a_stages = fits(2, p.cn_smem, 3) ? 2 : 1;
+    if (!fits(p.a_stages, p.cn_smem, 3)) p.cn_smem = 0;
     if (!fits(p.a_stages, p.cn_smem, 2)) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: shared memory budget exceeded");
     p.b_stages = 2;
     while (p.b_stages < kMaxBStages && fits(p.a_stages, p.cn_smem, p.b_stages + 1)) ++p.b_stages;
@@ -861,7 +1012,7 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     // At least 116 KB so that no second CTA shares the SM (each CTA holds all
     // 512 TMEM columns while it runs).
     const uint32_t smem_bytes =
-        std::max<uint32_t>(smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms).total + 1024,
+        std::max<uint32_t>(smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms, p.fuse_x).total + 1024,
                            116u * 1024u);
     if ((int)smem_bytes > max_smem) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: shared memory budget exceeded");
 
@@ -872,14 +1023,17 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     // atom layout the kernel bulk-copies; the temporaries are stream-ordered.
     uint8_t* tmp_atoms = nullptr;
     if (!scale_atoms) {
-        MXK_REQUIRE(!rows_dev, "gemm_mx: device-side row counts need atom-layout scales");
-        const int64_t a_bytes = scale_atom_bytes(m, k, kBM);
+        // (the fused quantizer writes the point scales itself; only B needs them)
+        MXK_REQUIRE(!rows_dev || fuse_x, "gemm_mx: device-side row counts need atom-layout scales");
+        const int64_t a_bytes = fuse_x ? 0 : scale_atom_bytes(m, k, kBM);
         const int64_t b_bytes = scale_atom_bytes(n, k, kBN);
         MXK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp_atoms), (size_t)(a_bytes + b_bytes), stream));
         const int sms = sm_count();
         {
             LaunchScope scope("scales_to_atoms", stream);
-            scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(m, p.kchunks, kBM, a_scales, tmp_atoms, a_bytes / 4);
+            if (a_bytes)
+                scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(m, p.kchunks, kBM, a_scales, tmp_atoms,
+                                                                    a_bytes / 4);
             scales_to_atoms_kernel<<<sms * 4, 256, 0, stream>>>(n, p.kchunks, kBN, b_scales, tmp_atoms + a_bytes,
                                                                 b_bytes / 4);
         }
@@ -888,7 +1042,7 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
             cudaFreeAsync(tmp_atoms, stream);
             return fail_cuda("scales_to_atoms_kernel", e);
         }
-        p.a_scales = tmp_atoms;
+        if (a_bytes) p.a_scales = tmp_atoms;
         p.b_scales = tmp_atoms + a_bytes;
     }
 
@@ -904,7 +1058,7 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
                                                      std::to_string(kLaunchRegs));
         }
         LaunchScope scope(name, stream);
-        kernel<<<grid, kThreads, smem_bytes, stream>>>(tmap_a, tmap_b, p);
+        kernel<<<grid, kThreads, smem_bytes, stream>>>(tmap_a, tmap_b, tmap_x, p);
         MXK_CUDA(cudaGetLastError());
         return MXK_OK;
     };
@@ -943,6 +1097,22 @@ int mxk_assign_mx_fused(int bits, int64_t rows, int k, int d, const void* a, con
     am.start_hint = start_hint;
     MXK_CHECK(mxk::launch_gemm_mx(bits, rows, k, d, a, a_scales, b, b_scales, nullptr, &am, nullptr,
                                   mxk::as_stream(stream)));
+    return mxk::check_device_error(mxk::as_stream(stream));
+}
+
+int mxk_assign_f32_fused(int64_t rows, int k, int d, const float* points, int64_t n_points, const uint8_t* b,
+                         const uint8_t* b_scales, const float* point_norms, const float* centroid_norms,
+                         const int* pid, int* labels, float* gaps, const int* start_hint, void* stream) {
+    mxk::MxArgmin am;
+    am.point_norms = point_norms;
+    am.centroid_norms = centroid_norms;
+    am.pid = pid;
+    am.labels = labels;
+    am.gaps = gaps;
+    am.start_hint = start_hint;
+    MXK_REQUIRE(points != nullptr, "assign_f32_fused: null points");
+    MXK_CHECK(mxk::launch_gemm_mx(8, rows, k, d, nullptr, nullptr, b, b_scales, nullptr, &am, nullptr,
+                                  mxk::as_stream(stream), false, points, n_points));
     return mxk::check_device_error(mxk::as_stream(stream));
 }
 

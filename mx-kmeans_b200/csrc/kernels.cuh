@@ -66,9 +66,13 @@ struct MxArgmin {
 // scale_atoms: the point scales are in the atom layout for kPointTileRows and the
 // centroid scales for kCentroidTileRows (see launch_quantize), which the kernel
 // fetches with bulk copies; otherwise both are row-major and converted per call.
+// points_f32 (argmin, bits 8, k 128 only): quantize the point tile in the kernel
+// from these FP32 rows (points_rows of them, gathered through argmin->pid), with
+// the bytes quantize_rows would write; a / a_scales are then unused.
 int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const uint8_t* a_scales,
                    const uint8_t* b, const uint8_t* b_scales, float* out, const MxArgmin* argmin,
-                   const int* rows_dev, cudaStream_t stream, bool scale_atoms = false);
+                   const int* rows_dev, cudaStream_t stream, bool scale_atoms = false,
+                   const float* points_f32 = nullptr, int64_t points_rows = 0);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

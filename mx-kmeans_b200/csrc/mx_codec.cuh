@@ -23,6 +23,45 @@ __device__ __forceinline__ uint32_t ue8m0_encode(float v) {
     return out & 0xffu;
 }
 
+// MXFP8 block scale: the UE8M0 code of amax / 448 rounded up to a power of two,
+// i.e. ue8m0_encode(amax > 0 ? amax / 448 : 1) with the IEEE division, without
+// dividing and without a call.  With amax = (1 + f 2^-23) 2^(E-127) and the
+// quotient normal (biased exponent E >= 10), the correctly rounded quotient
+// fl(amax / 448) is at most 2^(E-135) exactly when f <= 6291456 (the rounding
+// boundary lies at 1.75 (1 + 2^-24) 2^(E-127), strictly between two
+// representable mantissas), else at most 2^(E-134); so the code is
+// E - 8 + (f >= 6291457).  For E <= 9 the quotient is below 2^-125, where the
+// float grid is 2^-149, so its bit pattern is the integer
+// round-half-even(A 2^max(E-1,0) / 448) with A the integer significand of amax
+// (below 2^32); the hardware conversion then rounds that quotient.  Infinity
+// divided by 448 is infinity, converted directly.  Zero and NaN give code 127
+// (the scale 1.0 the reference uses when amax is not > 0).  Checked against the
+// division for every float32 bit pattern.
+//
+// ue8m0_mxfp8_scale_common is the branch-free common case: its code is exact
+// unless it sets `rare` (amax tiny or infinite), where ue8m0_mxfp8_scale must be
+// used instead.
+__device__ __forceinline__ uint32_t ue8m0_mxfp8_scale_common(float amax, bool& rare) {
+    const uint32_t bits = __float_as_uint(amax);
+    const uint32_t e = bits >> 23;
+    const bool pos = amax > 0.0f;
+    rare = pos && (e < 10u || e == 255u);
+    return pos ? e - 8u + ((bits & 0x7fffffu) >= 6291457u ? 1u : 0u) : 127u;
+}
+__device__ __forceinline__ uint32_t ue8m0_mxfp8_scale(float amax) {
+    bool rare;
+    const uint32_t common = ue8m0_mxfp8_scale_common(amax, rare);  // zero or NaN: 127 (scale 1.0)
+    if (!rare) return common;
+    const uint32_t bits = __float_as_uint(amax);
+    const uint32_t e = bits >> 23;
+    if (e == 255u) return ue8m0_encode(amax);  // +inf
+    const uint32_t sig = e ? (bits & 0x7fffffu) | 0x800000u : bits;
+    const uint32_t num = sig << (e ? e - 1u : 0u);
+    const uint32_t quo = num / 448u, rem = num - quo * 448u;
+    const uint32_t q = quo + ((rem > 224u || (rem == 224u && (quo & 1u))) ? 1u : 0u);
+    return ue8m0_encode(__uint_as_float(q));
+}
+
 // 2^(e-127) as a float (e in 0..254); e == 255 is the NaN code.
 __device__ __forceinline__ float ue8m0_value(uint32_t e) {
     if (e == 0) return __uint_as_float(0x00400000u);  // 2^-127 (subnormal)

@@ -451,6 +451,40 @@ int launch_group_compaction(int64_t n, const int* precision, const int* order, i
     return MXK_OK;
 }
 
+// Every float32 bit pattern through the division-free MXFP8 scale codec of the
+// fused assignment's in-kernel quantizer and through the IEEE division it
+// replaces (the rule quantize_rows applies); result[0] counts disagreements,
+// result[1] keeps the smallest disagreeing pattern (all ones when none).
+__global__ void __launch_bounds__(256) scale_codec_check_kernel(unsigned long long* __restrict__ result) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    unsigned long long bad = 0, first = ~0ull;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
+        const float a = __uint_as_float((uint32_t)i);
+        const uint32_t want = dev::ue8m0_encode(a > 0.0f ? a / 448.0f : 1.0f);
+        if (dev::ue8m0_mxfp8_scale(a) != want) {
+            ++bad;
+            first = first < i ? first : i;
+        }
+    }
+    if (bad) {
+        atomicAdd(result, bad);
+        atomicMin(result + 1, first);
+    }
+}
+
+int launch_scale_codec_check(unsigned long long* result, cudaStream_t stream) {
+    MXK_REQUIRE(result != nullptr, "check_mxfp8_scale_codec: result must not be null");
+    MXK_CUDA(cudaMemsetAsync(result, 0, sizeof(unsigned long long), stream));
+    MXK_CUDA(cudaMemsetAsync(result + 1, 0xff, sizeof(unsigned long long), stream));
+    int sms = 0, dev = 0;
+    MXK_CUDA(cudaGetDevice(&dev));
+    MXK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    LaunchScope scope("scale_codec_check", stream);
+    scale_codec_check_kernel<<<(unsigned)(sms * 8), 256, 0, stream>>>(result);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
 }  // namespace mxk
 
 extern "C" {
@@ -474,6 +508,10 @@ int mxk_assign_precisions(int64_t n, int d, const float* upper, const float* gap
                           int* precision, void* stream) {
     return mxk::launch_assign_precisions(n, d, upper, gaps, lc, ec, nullptr, precision, nullptr,
                                          mxk::as_stream(stream));
+}
+
+int mxk_check_mxfp8_scale_codec(unsigned long long* result, void* stream) {
+    return mxk::launch_scale_codec_check(result, mxk::as_stream(stream));
 }
 
 }  // extern "C"

@@ -51,6 +51,7 @@ SIGNATURES = {
     "mxk_quantize_rows": ([_I, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_precompute_point_bounds": ([_I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_precisions": ([_I64, _I, _P, _P, _F, _F, _P, _P], _I),
+    "mxk_check_mxfp8_scale_codec": ([_P, _P], _I),
     "mxk_gemm_mx": ([_I, _I64, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_gemm_fp32": ([_I64, _I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_clusters": ([_I64, _I, _P, _P, _P, _P, _P, _P, _P], _I),
@@ -58,6 +59,7 @@ SIGNATURES = {
     "mxk_centroid_shift": ([_I64, _P, _P, _P, _P, _P], _I),
     "mxk_centroid_shift_noalloc": ([_I64, _P, _P, _P, _P, _P], _I),
     "mxk_assign_mx_fused": ([_I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "mxk_assign_f32_fused": ([_I64, _I, _I, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_kmeans_mixed": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_comm_unique_id": ([ctypes.c_char_p], _I),
     "mxk_comm_init": ([ctypes.POINTER(_P), _I, _I, ctypes.c_char_p], _I),
@@ -131,6 +133,12 @@ def assign_precisions(n, d, upper, gaps, lc, ec, precision, stream=None):
     check(load().mxk_assign_precisions(n, d, _ptr(upper), _ptr(gaps), lc, ec, _ptr(precision), _stream(stream)))
 
 
+def check_mxfp8_scale_codec(result, stream=None):
+    """Exhaustive device check of the fused quantizer's MXFP8 scale rule against
+    ue8m0(amax / 448); result: 2 int64 device words (count, first pattern)."""
+    check(load().mxk_check_mxfp8_scale_codec(_ptr(result), _stream(stream)))
+
+
 def gemm_mx(bits, m, n, k, a, a_scales, b, b_scales, out, stream=None):
     check(load().mxk_gemm_mx(bits, m, n, k, _ptr(a), _ptr(a_scales), _ptr(b), _ptr(b_scales), _ptr(out),
                              _stream(stream)))
@@ -150,6 +158,13 @@ def assign_mx_fused(bits, rows, k, d, a, a_scales, b, b_scales, point_norms, cen
     check(load().mxk_assign_mx_fused(bits, rows, k, d, _ptr(a), _ptr(a_scales), _ptr(b), _ptr(b_scales),
                                      _ptr(point_norms), _ptr(centroid_norms), _ptr(pid), _ptr(labels), _ptr(gaps),
                                      _ptr(start_hint), _stream(stream)))
+
+
+def assign_f32_fused(rows, k, d, points, b, b_scales, point_norms, centroid_norms, labels, gaps=None, pid=None,
+                     start_hint=None, stream=None):
+    check(load().mxk_assign_f32_fused(rows, k, d, _ptr(points), points.shape[0], _ptr(b), _ptr(b_scales),
+                                      _ptr(point_norms), _ptr(centroid_norms), _ptr(pid), _ptr(labels), _ptr(gaps),
+                                      _ptr(start_hint), _stream(stream)))
 
 
 def update_centroids(points, labels, old_centroids, centroids, counts, stream=None):
