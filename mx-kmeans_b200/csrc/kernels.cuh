@@ -40,14 +40,18 @@ int launch_centroid_stats(int k, const float* errors, const float* norms, float*
 // scratch: compaction_scratch_ints(n) ints.  order (optional, n ints): the
 // sequence to compact (element i is point order[i]); null = 0..n-1.
 int64_t compaction_scratch_ints(int64_t n);
+// stop (optional, device word): when it is non-zero at run time the launches
+// do nothing except report empty groups (the Lloyd loop's converged state).
 int launch_group_compaction(int64_t n, const int* precision, const int* order, int* ids, int* group_counts,
-                            int* scratch, cudaStream_t stream);
+                            int* scratch, cudaStream_t stream, const int* stop = nullptr);
 
 // ---- order.cu -----------------------------------------------------------------
 // order = point indices 0..n-1 sorted by labels[] (counting sort over k keys;
 // order within a key is unspecified).  scratch: label_sort_scratch_ints(k) ints.
 int64_t label_sort_scratch_ints(int k);
-int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream);
+// stop (optional, device word): non-zero at run time = do nothing.
+int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream,
+                      const int* stop = nullptr);
 
 // ---- gemm_mx.cu ---------------------------------------------------------------
 struct MxArgmin {
@@ -85,14 +89,24 @@ int launch_assign_clusters(int64_t rows, int k, const float* point_norms, const 
 // ---- update.cu ---------------------------------------------------------------
 // sums (k x d) and counts (k) must be zeroed by the caller.  order (optional):
 // visit the points in this sequence (label-sorted orders make long label runs).
+// stop (optional, device word): non-zero at run time = do nothing.
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
-                      float* sums, int* counts, cudaStream_t stream);
+                      float* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
 // centroids = counts ? sums / counts : old.  If shift_scratch is not null
 // (shift_scratch_floats() floats), its last element receives sum((old - new)^2),
 // reduced in a fixed order (bit-reproducible).  sums and centroids may alias.
 int64_t shift_scratch_floats();
+//
+// loop (optional, device words, Lloyd driver): loop[0] = stopped, loop[1] =
+// completed iterations, loop[2] = stopped on a non-finite shift.  While
+// loop[0] is zero the launch updates the centroids, counts the iteration and
+// sets loop[0] when the shift is <= tolerance or not finite (the reference's
+// stopping rule, kmeans.cu:62-67); once it is set the launch does nothing, so a
+// driver may enqueue iterations before it has read whether the previous one
+// converged.  Requires shift_scratch.
 int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids,
-                    float* centroids, float* shift_scratch, cudaStream_t stream);
+                    float* centroids, float* shift_scratch, cudaStream_t stream, int* loop = nullptr,
+                    float tolerance = 0.0f);
 // sum((previous - current)^2) into shift_scratch[shift_scratch_floats() - 1].
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,
                  cudaStream_t stream);

@@ -14,8 +14,12 @@
 // counts from device memory, the product and assignment are one tcgen05 kernel
 // (no N x K buffer), workspaces come from the stream-ordered allocator, and the
 // shift is reduced in a fixed order so every rank of a sharded run sees the same
-// value.  The only host synchronization per iteration is the shift read-back the
-// stopping rule needs (as in the reference).
+// value.  The stopping rule runs on the device: the shift kernel sets a stop
+// word that turns every later launch of the call into a no-op, so the host
+// enqueues up to kLookahead iterations beyond the last one whose state it has
+// read and never waits on the GPU between iterations (the reference reads the
+// shift back and synchronizes every iteration).  Labels, centroids and the
+// returned iteration count are those of the iteration that met the rule.
 //
 // The reference's precision policy ignores the two-largest distance gap
 // (include/precision.hpp:20-26), so the driver's fused assignment does not track
@@ -109,6 +113,31 @@ struct Arena {
 };
 
 constexpr int64_t kFp32ChunkBytes = 512ll << 20;  // dense product chunk of the FP32 iterations
+// Iterations enqueued ahead of the last one whose loop state the host has read.
+// About 40 ms of GPU work at the benchmark shape, so a host thread descheduled or
+// held in the driver for that long does not leave the GPU idle.
+constexpr int kLookahead = 8;
+
+// Pinned host copies of the loop state words (one slot per iteration in flight)
+// and the events that say when each copy has landed.
+struct LoopMirror {
+    int* host = nullptr;
+    cudaEvent_t ev[kLookahead + 1] = {};
+    ~LoopMirror() {
+        // an error return can leave copies into `host` in flight
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventSynchronize(e);
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventDestroy(e);
+        if (host) cudaFreeHost(host);
+    }
+    int init() {
+        MXK_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int) * 4 * (kLookahead + 1),
+                               cudaHostAllocDefault));
+        for (cudaEvent_t& e : ev) MXK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        return MXK_OK;
+    }
+};
 
 int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
               const mxk_options* options, int* iterations, cudaStream_t stream) {
@@ -151,6 +180,11 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
+    int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] unused
+    MXK_CHECK(ws.alloc(&loop, 4));
+    MXK_CUDA(cudaMemsetAsync(loop, 0, sizeof(int) * 4, stream));
+    LoopMirror mirror;
+    MXK_CHECK(mirror.init());
     float* dots = nullptr;
     int64_t chunk_rows = 0;
     if (options->fp32_iterations > 0 && n > 0) {
@@ -166,13 +200,12 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
 
     const bool sharded = comm && comm->nranks > 1;
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
-    int result = options->max_iterations;
     for (int it = 0; it < options->max_iterations; ++it) {
         // From the second iteration on, visit points grouped by their previous
         // label (order.cu); the first iteration keeps ascending point order.
         const int* ord = nullptr;
         if (it > 0 && n > 0) {
-            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream));
+            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
             ord = order;
         }
         MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
@@ -193,7 +226,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                                       kCentroidTileRows));
             MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
             MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream));
-            MXK_CHECK(launch_group_compaction(n, precision, ord, ids, gcount, cscratch, stream));
+            MXK_CHECK(launch_group_compaction(n, precision, ord, ids, gcount, cscratch, stream, loop));
             static const int group_bits[3] = {4, 6, 8};
             for (int g = 0; g < 3; ++g) {
                 // MXFP8 at d = 128: the GEMM quantizes the point tiles itself from the
@@ -222,7 +255,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         // kmeans.cu:62-65
         MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
         MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
-        MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream));
+        MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream, loop));
         if (sharded) {
             NcclApi& api = nccl();
             ncclResult_t r = api.GroupStart();
@@ -232,20 +265,26 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             if (r != ncclSuccess) return fail_nccl("ncclAllReduce", r);
             if (r2 != ncclSuccess) return fail_nccl("ncclGroupEnd", r2);
         }
-        MXK_CHECK(launch_finalize(d, k, sums, counts, prev, centroids, shift, stream));
-        float host_shift = 0.0f;
-        MXK_CUDA(cudaMemcpyAsync(&host_shift, shift + shift_scratch_floats() - 1, sizeof(float), cudaMemcpyDeviceToHost,
-                                 stream));
-        MXK_CUDA(cudaStreamSynchronize(stream));
-        MXK_CHECK(check_device_error(stream));
-        if (!std::isfinite(host_shift))
-            return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");
-        if (host_shift <= options->tolerance) {
-            result = it + 1;
-            break;
+        MXK_CHECK(launch_finalize(d, k, sums, counts, prev, centroids, shift, stream, loop, options->tolerance));
+        const int slot = it % (kLookahead + 1);
+        MXK_CUDA(cudaMemcpyAsync(mirror.host + 4 * slot, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+        MXK_CUDA(cudaEventRecord(mirror.ev[slot], stream));
+        // Read the state of iteration it - lookahead.  FP32 iterations (whose
+        // kernels do not consult the stop word) and verbose runs are read at once,
+        // so no FP32 iteration is ever enqueued after the loop has stopped.
+        const int lookahead = (options->verbose || it + 1 < options->fp32_iterations) ? 0 : kLookahead;
+        const int seen = it - lookahead;
+        if (seen >= 0) {
+            const int sslot = seen % (kLookahead + 1);
+            MXK_CUDA(cudaEventSynchronize(mirror.ev[sslot]));
+            if (mirror.host[4 * sslot]) break;  // stopped at or before iteration `seen`
         }
     }
-    *iterations = result;
+    MXK_CUDA(cudaMemcpyAsync(mirror.host, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+    MXK_CUDA(cudaStreamSynchronize(stream));
+    MXK_CHECK(check_device_error(stream));
+    if (mirror.host[2]) return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");
+    *iterations = mirror.host[1];
     return MXK_OK;
 }
 

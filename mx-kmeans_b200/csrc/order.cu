@@ -22,7 +22,8 @@ constexpr int kSmemBins = 16384;  // keys counted in shared memory up to this k
 __device__ __forceinline__ int clamp_key(int v, int k) { return (unsigned)v < (unsigned)k ? v : k - 1; }
 
 __global__ void __launch_bounds__(512) label_histogram_kernel(int64_t n, int k, const int* __restrict__ labels,
-                                                              int* __restrict__ hist) {
+                                                              int* __restrict__ hist, const int* __restrict__ stop) {
+    if (stop && *stop) return;  // the Lloyd loop has already converged
     extern __shared__ int local[];
     const bool use_smem = k <= kSmemBins;
     if (use_smem) {
@@ -47,7 +48,9 @@ __global__ void __launch_bounds__(512) label_histogram_kernel(int64_t n, int k, 
 }
 
 // Exclusive scan of the k counts (one block of 1024 threads).
-__global__ void __launch_bounds__(1024) label_scan_kernel(int k, int* __restrict__ hist) {
+__global__ void __launch_bounds__(1024) label_scan_kernel(int k, int* __restrict__ hist,
+                                                          const int* __restrict__ stop) {
+    if (stop && *stop) return;
     __shared__ int warp_tot[32];
     __shared__ int carry;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -85,7 +88,8 @@ __global__ void __launch_bounds__(1024) label_scan_kernel(int k, int* __restrict
 // single global atomic, and places its points through shared-memory cursors.
 __global__ void __launch_bounds__(512) label_scatter_block_kernel(int64_t n, int k, const int* __restrict__ labels,
                                                                   int* __restrict__ offsets, int* __restrict__ order,
-                                                                  int64_t per_block) {
+                                                                  int64_t per_block, const int* __restrict__ stop) {
+    if (stop && *stop) return;
     extern __shared__ int cursor[];
     const int64_t begin = (int64_t)blockIdx.x * per_block;
     const int64_t end = begin + per_block < n ? begin + per_block : n;
@@ -119,7 +123,9 @@ __global__ void __launch_bounds__(512) label_scatter_block_kernel(int64_t n, int
 // order[offset[key]++] = p, one atomic per group of equal keys within a warp
 // (used when k is too large for the shared-memory cursors).
 __global__ void __launch_bounds__(512) label_scatter_kernel(int64_t n, int k, const int* __restrict__ labels,
-                                                            int* __restrict__ offsets, int* __restrict__ order) {
+                                                            int* __restrict__ offsets, int* __restrict__ order,
+                                                            const int* __restrict__ stop) {
+    if (stop && *stop) return;
     for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < n; base += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = base + threadIdx.x;
         const bool valid = p < n;
@@ -138,7 +144,8 @@ __global__ void __launch_bounds__(512) label_scatter_kernel(int64_t n, int k, co
 
 int64_t label_sort_scratch_ints(int k) { return k; }
 
-int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream) {
+int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream,
+                      const int* stop) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(k > 0 && labels && order && scratch, "label_sort: bad arguments");
     MXK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int) * (size_t)k, stream));
@@ -148,12 +155,12 @@ int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scra
         MXK_CUDA(cudaFuncSetAttribute(label_histogram_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     {
         LaunchScope scope("label_histogram", stream);
-        label_histogram_kernel<<<sms * 2, 512, smem, stream>>>(n, k, labels, scratch);
+        label_histogram_kernel<<<sms * 2, 512, smem, stream>>>(n, k, labels, scratch, stop);
         MXK_CUDA(cudaGetLastError());
     }
     {
         LaunchScope scope("label_scan", stream);
-        label_scan_kernel<<<1, 1024, 0, stream>>>(k, scratch);
+        label_scan_kernel<<<1, 1024, 0, stream>>>(k, scratch, stop);
         MXK_CUDA(cudaGetLastError());
     }
     if (k <= kSmemBins) {
@@ -163,11 +170,12 @@ int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scra
             MXK_CUDA(cudaFuncSetAttribute(label_scatter_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
         LaunchScope scope("label_scatter", stream);
-        label_scatter_block_kernel<<<(unsigned)blocks, 512, smem, stream>>>(n, k, labels, scratch, order, per_block);
+        label_scatter_block_kernel<<<(unsigned)blocks, 512, smem, stream>>>(n, k, labels, scratch, order, per_block,
+                                                                                stop);
         MXK_CUDA(cudaGetLastError());
     } else {
         LaunchScope scope("label_scatter", stream);
-        label_scatter_kernel<<<sms * 4, 512, 0, stream>>>(n, k, labels, scratch, order);
+        label_scatter_kernel<<<sms * 4, 512, 0, stream>>>(n, k, labels, scratch, order, stop);
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;

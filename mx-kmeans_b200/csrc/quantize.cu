@@ -276,7 +276,9 @@ constexpr int kCompactBlock = 1024;  // elements per block (256 threads x 4)
 // reference's copy_if, or label-sorted when the driver passes that order.
 __global__ void __launch_bounds__(256) group_block_count_kernel(int64_t n, const int* __restrict__ precision,
                                                                 const int* __restrict__ order,
-                                                                int* __restrict__ block_counts, int nblocks) {
+                                                                int* __restrict__ block_counts, int nblocks,
+                                                                const int* __restrict__ stop) {
+    if (stop && *stop) return;  // the Lloyd loop has already converged
     __shared__ int cnt[3];
     if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
     __syncthreads();
@@ -299,9 +301,14 @@ __global__ void __launch_bounds__(256) group_block_count_kernel(int64_t n, const
 }
 
 // Exclusive scan of per-block counts for each group (one block, three warps).
-__global__ void group_scan_kernel(int* __restrict__ block_counts, int nblocks, int* __restrict__ group_counts) {
+__global__ void group_scan_kernel(int* __restrict__ block_counts, int nblocks, int* __restrict__ group_counts,
+                                  const int* __restrict__ stop) {
     const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (g >= 3) return;
+    if (stop && *stop) {  // converged: empty groups, so the quantize and GEMM launches that read them do nothing
+        if (lane == 0) group_counts[g] = 0;
+        return;
+    }
     int* c = block_counts + (size_t)g * nblocks;
     int carry = 0;
     for (int b0 = 0; b0 < nblocks; b0 += 32) {
@@ -321,7 +328,8 @@ __global__ void group_scan_kernel(int* __restrict__ block_counts, int nblocks, i
 __global__ void __launch_bounds__(256) group_scatter_kernel(int64_t n, const int* __restrict__ precision,
                                                             const int* __restrict__ order,
                                                             const int* __restrict__ block_offsets, int nblocks,
-                                                            int* __restrict__ ids) {
+                                                            int* __restrict__ ids, const int* __restrict__ stop) {
+    if (stop && *stop) return;
     __shared__ int warp_tot[3][8];
     __shared__ int running[3];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -429,23 +437,23 @@ int launch_centroid_stats(int k, const float* errors, const float* norms, float*
 int64_t compaction_scratch_ints(int64_t n) { return 3 * ((n + kCompactBlock - 1) / kCompactBlock) + 3; }
 
 int launch_group_compaction(int64_t n, const int* precision, const int* order, int* ids, int* group_counts,
-                            int* scratch, cudaStream_t stream) {
+                            int* scratch, cudaStream_t stream, const int* stop) {
     if (n <= 0) return MXK_OK;
     const int64_t nb = (n + kCompactBlock - 1) / kCompactBlock;
     MXK_REQUIRE(nb < (1ll << 31), "compaction: too many points");
     {
         LaunchScope scope("group_count", stream);
-        group_block_count_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb);
+        group_block_count_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb, stop);
         MXK_CUDA(cudaGetLastError());
     }
     {
         LaunchScope scope("group_scan", stream);
-        group_scan_kernel<<<1, 96, 0, stream>>>(scratch, (int)nb, group_counts);
+        group_scan_kernel<<<1, 96, 0, stream>>>(scratch, (int)nb, group_counts, stop);
         MXK_CUDA(cudaGetLastError());
     }
     {
         LaunchScope scope("group_scatter", stream);
-        group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb, ids);
+        group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb, ids, stop);
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;

@@ -48,7 +48,8 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
                                                               const int* __restrict__ labels,
                                                               const int* __restrict__ order, float* __restrict__ sums,
                                                               int* __restrict__ counts, int64_t per_warp,
-                                                              unsigned* __restrict__ err) {
+                                                              unsigned* __restrict__ err, const int* __restrict__ stop) {
+    if (stop && *stop) return;  // the Lloyd loop has already converged
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t begin = warp * per_warp;
@@ -95,7 +96,9 @@ __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int 
                                                                  const float* __restrict__ points,
                                                                  const int* __restrict__ labels,
                                                                  const int* __restrict__ order, float* __restrict__ sums,
-                                                                 int* __restrict__ counts, unsigned* __restrict__ err) {
+                                                                 int* __restrict__ counts, unsigned* __restrict__ err,
+                                                                 const int* __restrict__ stop) {
+    if (stop && *stop) return;
     extern __shared__ float priv[];  // k*d sums, then k counts
     int* pcount = reinterpret_cast<int*>(priv + (int64_t)k * d);
     const int kd = k * d;
@@ -131,7 +134,9 @@ __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int 
 // Generic fallback for d % 128 != 0 (API use with unpadded d).
 __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* __restrict__ points,
                                          const int* __restrict__ labels, float* __restrict__ sums,
-                                         int* __restrict__ counts, unsigned* __restrict__ err) {
+                                         int* __restrict__ counts, unsigned* __restrict__ err,
+                                         const int* __restrict__ stop) {
+    if (stop && *stop) return;
     const int64_t total = n * d;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t row = i / d;
@@ -150,7 +155,9 @@ __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* _
 // the same iteration without exchanging it.
 __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float* __restrict__ sums,
                                                        const int* __restrict__ counts, const float* __restrict__ old,
-                                                       float* __restrict__ centroids, float* __restrict__ partials) {
+                                                       float* __restrict__ centroids, float* __restrict__ partials,
+                                                       const int* __restrict__ stop) {
+    if (stop && *stop) return;  // converged: the centroids stay as they are
     __shared__ float warp_sum[8];
     const int64_t total = (int64_t)k * d;
     float local = 0.0f;
@@ -173,8 +180,12 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float
     }
 }
 
-// Sums the per-CTA partials in a fixed order into out[0].
-__global__ void sum_partials_kernel(const float* __restrict__ partials, int count, float* __restrict__ out) {
+// Sums the per-CTA partials in a fixed order into out[0].  With `loop` (the
+// Lloyd driver's state words, see launch_finalize) it also applies the stopping
+// rule, and does nothing once the loop has stopped.
+__global__ void sum_partials_kernel(const float* __restrict__ partials, int count, float* __restrict__ out,
+                                    int* __restrict__ loop, float tolerance) {
+    if (loop && *(volatile int*)loop) return;  // read by every thread before thread 0 can write it
     __shared__ float warp_sum[32];
     float local = 0.0f;
     for (int i = threadIdx.x; i < count; i += blockDim.x) local += partials[i];
@@ -185,6 +196,15 @@ __global__ void sum_partials_kernel(const float* __restrict__ partials, int coun
         float s = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
         out[0] = s;
+        if (loop) {
+            loop[1] += 1;
+            if (!isfinite(s)) {
+                loop[2] = 1;
+                loop[0] = 1;
+            } else if (s <= tolerance) {
+                loop[0] = 1;
+            }
+        }
     }
 }
 
@@ -211,7 +231,7 @@ constexpr int kShiftBlocks = 256;  // fixed grid of the shift reduction (<= part
 }  // namespace
 
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, float* sums,
-                      int* counts, cudaStream_t stream) {
+                      int* counts, cudaStream_t stream, const int* stop) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && k > 0 && points && labels && sums && counts, "update_centroids: bad arguments");
     const int sms = sm_count();
@@ -230,7 +250,7 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
                                       (int)priv_bytes));
         LaunchScope scope("accumulate_private", stream);
         accumulate_private_kernel<<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, order, sums, counts,
-                                                                             err);
+                                                                             err, stop);
         MXK_CUDA(cudaGetLastError());
         return MXK_OK;
     }
@@ -244,7 +264,7 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
         switch (d / 128) {
 #define MXK_ACC_CASE(J) \
     case J: accumulate_runs_kernel<J><<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, order, sums, counts, \
-                                                                       per_warp, err);                              \
+                                                                       per_warp, err, stop);                        \
         break;
             MXK_ACC_CASE(1) MXK_ACC_CASE(2) MXK_ACC_CASE(3) MXK_ACC_CASE(4) MXK_ACC_CASE(5) MXK_ACC_CASE(6)
             MXK_ACC_CASE(7) MXK_ACC_CASE(8)
@@ -254,7 +274,7 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
         return MXK_OK;
     }
     LaunchScope scope("accumulate_scalar", stream);
-    accumulate_scalar_kernel<<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err);
+    accumulate_scalar_kernel<<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
@@ -262,19 +282,21 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
 int64_t shift_scratch_floats() { return kShiftBlocks + 1; }
 
 int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids, float* centroids,
-                    float* shift_scratch, cudaStream_t stream) {
+                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance) {
+    MXK_REQUIRE(!loop || shift_scratch, "finalize: the loop state needs the shift scratch");
     const int64_t total = (int64_t)k * d;
     int64_t blocks = (total + 255) / 256;
     if (blocks > kShiftBlocks) blocks = kShiftBlocks;
     {
         LaunchScope scope("finalize", stream);
         finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(d, k, sums, counts, old_centroids, centroids,
-                                                              shift_scratch);
+                                                              shift_scratch, loop);
         MXK_CUDA(cudaGetLastError());
     }
     if (shift_scratch) {
         LaunchScope scope("shift_total", stream);
-        sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks);
+        sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks, loop,
+                                                    tolerance);
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;
@@ -291,7 +313,8 @@ int launch_shift(int64_t elements, const float* previous, const float* current, 
         MXK_CUDA(cudaGetLastError());
     }
     LaunchScope scope("shift_total", stream);
-    sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks);
+    sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks, nullptr,
+                                                0.0f);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }

@@ -119,3 +119,38 @@ def test_duplicate_centroids_keep_lowest_index(torch_cuda, mxk, orc):
     assert not np.any(lg == 137)
     it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=3, tolerance=0.0)
     assert np.array_equal(lg, lo)
+
+
+def test_stop_rule_on_device_matches_exact_iteration_count(torch_cuda, mxk):
+    """The stopping rule runs on the device and the driver enqueues iterations
+    ahead of reading it: iterations enqueued after the stop must change nothing.
+    Integer-valued points make every sum exact, so runs are deterministic: the
+    per-iteration shifts are recovered from runs capped at 1, 2, ... iterations,
+    a tolerance is placed between them, and the early-stopping run must equal
+    the run capped at the expected iteration bit for bit."""
+    torch = torch_cuda
+    n, d, k = 12000, 128, 24
+    x = np.rint(blobs(n, 64, k, seed=21, spread=12.0, sigma=2.0)).astype(np.float32)
+    c0 = x[np.random.default_rng(5).choice(n, k, replace=False)].copy()
+    cents = [c0.astype(np.float64)]
+    for cap in range(1, 9):
+        it, c, _ = _run(torch, mxk, x, c0, max_iterations=cap, tolerance=0.0)
+        assert it == cap
+        cents.append(c.astype(np.float64))
+    shifts = [float(((cents[i] - cents[i - 1]) ** 2).sum()) for i in range(1, 9)]
+    # first iteration j >= 2 whose shift is clearly below every earlier one
+    j = next(i + 1 for i in range(1, 8) if shifts[i] < 0.9 * min(shifts[:i]))
+    tol = 0.5 * (shifts[j - 1] + min(shifts[:j - 1]))
+    it_ref, c_ref, l_ref = _run(torch, mxk, x, c0, max_iterations=j, tolerance=0.0)
+    for cap in (j, j + 1, j + 30):
+        it2, c2, l2 = _run(torch, mxk, x, c0, max_iterations=cap, tolerance=tol)
+        assert it2 == j
+        assert np.array_equal(l2, l_ref) and np.array_equal(c2, c_ref)
+    # a tolerance no shift meets: the count is the cap
+    cap = min(j + 2, 8)
+    if min(shifts[:cap]) > 0.0:
+        it3, _, _ = _run(torch, mxk, x, c0, max_iterations=cap, tolerance=0.0)
+        assert it3 == cap
+    # a loose tolerance stops on the first iteration
+    it4, _, _ = _run(torch, mxk, x, c0, max_iterations=60, tolerance=1e30)
+    assert it4 == 1
