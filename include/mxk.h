@@ -44,6 +44,12 @@ const char* mxk_last_error(void);
 int mxk_version(void);
 /* Number of kernels this library launched since load (all devices). */
 uint64_t mxk_launch_count(void);
+/* No reference counterpart (the reference allocates and frees its workspace in
+ * every kmeans_mixed call, src/kmeans.cu:17-27).  kmeans_mixed takes its
+ * workspace from a per-device pool that keeps the memory mapped between calls;
+ * this returns the current device's pooled memory to the driver (synchronizes
+ * the device). */
+int mxk_release_workspace(void);
 
 /* ---- ops (include/kmeans.cuh:23-47) ------------------------------------ */
 

@@ -61,6 +61,11 @@ int encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uin
 
 int sm_count();
 
+// The library's stream-ordered memory pool on the current device (created on
+// first use; freed blocks stay mapped until mxk_release_workspace).  Null if it
+// cannot be created.
+cudaMemPool_t workspace_pool();
+
 }  // namespace mxk
 
 // ---------------------------------------------------------------------------

@@ -89,7 +89,10 @@ struct Comm {
 };
 
 // ---------------------------------------------------------------------------
-// Workspace (stream-ordered allocations, released at the end of the call).
+// Workspace: stream-ordered allocations from the library's per-device pool,
+// returned to it at the end of the call.  The pool keeps the memory mapped, so a
+// repeated call does not map its ~1.4 GB of workspace again;
+// mxk_release_workspace gives it back to the driver.
 
 namespace {
 
@@ -104,7 +107,9 @@ struct Arena {
     int alloc(T** out, int64_t count) {
         void* p = nullptr;
         const size_t bytes = sizeof(T) * (size_t)(count > 0 ? count : 1);
-        cudaError_t e = cudaMallocAsync(&p, bytes, stream);
+        cudaMemPool_t pool = workspace_pool();
+        if (!pool) return fail(MXK_ERR_CUDA, "kmeans workspace: cannot create the memory pool");
+        cudaError_t e = cudaMallocFromPoolAsync(&p, bytes, pool, stream);
         if (e != cudaSuccess) return fail_cuda("cudaMallocAsync (kmeans workspace)", e);
         ptrs.push_back(p);
         *out = static_cast<T*>(p);

@@ -118,6 +118,29 @@ int check_device_error(cudaStream_t stream) {
     return MXK_OK;
 }
 
+cudaMemPool_t workspace_pool() {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+        uint64_t keep = ~0ull;  // keep freed blocks mapped for the next call
+        if (cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess) {
+            cudaMemPoolDestroy(pool);
+            return nullptr;
+        }
+        pools[dev] = pool;
+    }
+    return pools[dev];
+}
+
 int sm_count() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -162,6 +185,14 @@ const char* mxk_last_error(void) { return mxk::g_last_error.c_str(); }
 int mxk_version(void) { return 100; }
 
 uint64_t mxk_launch_count(void) { return mxk::g_launches.load(); }
+
+int mxk_release_workspace(void) {
+    cudaMemPool_t pool = mxk::workspace_pool();
+    if (!pool) return mxk::fail(MXK_ERR_CUDA, "release_workspace: no workspace pool on the current device");
+    MXK_CUDA(cudaDeviceSynchronize());
+    MXK_CUDA(cudaMemPoolTrimTo(pool, 0));
+    return MXK_OK;
+}
 
 int mxk_profile_enable(int on) {
     std::lock_guard<std::mutex> lock(mxk::g_mutex);

@@ -52,6 +52,7 @@ SIGNATURES = {
     "mxk_precompute_point_bounds": ([_I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_precisions": ([_I64, _I, _P, _P, _F, _F, _P, _P], _I),
     "mxk_check_mxfp8_scale_codec": ([_P, _P], _I),
+    "mxk_release_workspace": ([], _I),
     "mxk_gemm_mx": ([_I, _I64, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_gemm_fp32": ([_I64, _I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_clusters": ([_I64, _I, _P, _P, _P, _P, _P, _P, _P], _I),
@@ -131,6 +132,12 @@ def precompute_point_bounds(points, norms, upper, stream=None):
 
 def assign_precisions(n, d, upper, gaps, lc, ec, precision, stream=None):
     check(load().mxk_assign_precisions(n, d, _ptr(upper), _ptr(gaps), lc, ec, _ptr(precision), _stream(stream)))
+
+
+def release_workspace():
+    """Return the kmeans workspace kept by the library's pool on the current
+    device to the driver."""
+    check(load().mxk_release_workspace())
 
 
 def check_mxfp8_scale_codec(result, stream=None):
