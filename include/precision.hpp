@@ -29,6 +29,12 @@ MXK_HD inline int select_precision(float p4, float p6, float lc, float ec, int d
     return 8;
 }
 
+// select_precision above is MXFP8 whatever its inputs.  While this holds, the
+// Lloyd driver puts every point in the MXFP8 group without computing the
+// policy's inputs (point bounds, centroid errors, gaps) or compacting by
+// precision -- the same groups, labels and centroids as evaluating it.
+constexpr bool kSelectPrecisionIsForcedMxfp8 = true;
+
 // Two largest distances seen so far (include/precision.hpp:29-36).
 MXK_HD inline void insert_largest_distance(float value, float& first, float& second) {
     if (value > first) {

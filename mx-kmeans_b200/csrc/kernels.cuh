@@ -98,7 +98,8 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
 int64_t shift_scratch_floats();
 //
 // loop (optional, device words, Lloyd driver): loop[0] = stopped, loop[1] =
-// completed iterations, loop[2] = stopped on a non-finite shift.  While
+// completed iterations, loop[2] = stopped on a non-finite shift, loop[3] = the
+// row count later launches read (set to 0 when the loop stops).  While
 // loop[0] is zero the launch updates the centroids, counts the iteration and
 // sets loop[0] when the shift is <= tolerance or not finite (the reference's
 // stopping rule, kmeans.cu:62-67); once it is set the launch does nothing, so a

@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "precision.hpp"
 
 namespace mxk {
 
@@ -161,35 +162,50 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
           *prev = nullptr, *sums = nullptr, *shift = nullptr;
     int *precision = nullptr, *ids = nullptr, *gcount = nullptr, *cscratch = nullptr, *counts = nullptr;
     uint8_t *qpoints = nullptr, *pscales = nullptr, *qcent = nullptr, *cscales = nullptr;
+    // With the forced-MXFP8 policy the precision inputs and groups are not
+    // needed (see kSelectPrecisionIsForcedMxfp8); the general path keeps them.
+    constexpr bool kForced8 = kSelectPrecisionIsForcedMxfp8;
+    MXK_REQUIRE(n < (1ll << 31), "kmeans_mixed: n must be below 2^31");
     MXK_CHECK(ws.alloc(&pnorm, n));
-    MXK_CHECK(ws.alloc(&upper, ((n + 31) / 32) * 96));
     MXK_CHECK(ws.alloc(&gaps, n));
-    MXK_CHECK(ws.alloc(&precision, n));
-    MXK_CHECK(ws.alloc(&ids, 3 * n));
-    MXK_CHECK(ws.alloc(&gcount, 4));
-    MXK_CHECK(ws.alloc(&cscratch, compaction_scratch_ints(n)));
+    if (!kForced8) {
+        MXK_CHECK(ws.alloc(&upper, ((n + 31) / 32) * 96));
+        MXK_CHECK(ws.alloc(&precision, n));
+        MXK_CHECK(ws.alloc(&ids, 3 * n));
+        MXK_CHECK(ws.alloc(&gcount, 4));
+        MXK_CHECK(ws.alloc(&cscratch, compaction_scratch_ints(n)));
+    }
     int *order = nullptr, *sort_scratch = nullptr;
     MXK_CHECK(ws.alloc(&order, n));
     MXK_CHECK(ws.alloc(&sort_scratch, label_sort_scratch_ints(k)));
-    MXK_CHECK(ws.alloc(&qpoints, n * d));
-    MXK_CHECK(ws.alloc(&pscales, scale_atom_bytes(n, d)));
+    // (the fused quantize at d = 128 never materializes the MXFP8 point rows)
+    const bool need_qpoints = !kForced8 || d != 128;
+    if (need_qpoints) {
+        MXK_CHECK(ws.alloc(&qpoints, n * d));
+        MXK_CHECK(ws.alloc(&pscales, scale_atom_bytes(n, d)));
+    }
     MXK_CHECK(ws.alloc(&cnorm, k));
-    MXK_CHECK(ws.alloc(&cerr, k));
-    MXK_CHECK(ws.alloc(&stats, 2));
+    if (!kForced8) {
+        MXK_CHECK(ws.alloc(&cerr, k));
+        MXK_CHECK(ws.alloc(&stats, 2));
+    }
     MXK_CHECK(ws.alloc(&qcent, kd));
     MXK_CHECK(ws.alloc(&cscales, scale_atom_bytes(k, d, kCentroidTileRows)));
     // scale atoms of padding rows are never written; keep them finite
-    MXK_CUDA(cudaMemsetAsync(pscales, 0, (size_t)scale_atom_bytes(n, d), stream));
+    if (need_qpoints) MXK_CUDA(cudaMemsetAsync(pscales, 0, (size_t)scale_atom_bytes(n, d), stream));
     MXK_CUDA(cudaMemsetAsync(cscales, 0, (size_t)scale_atom_bytes(k, d, kCentroidTileRows), stream));
     MXK_CHECK(ws.alloc(&prev, kd));
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
-    int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] unused
+    int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)
     MXK_CHECK(ws.alloc(&loop, 4));
-    MXK_CUDA(cudaMemsetAsync(loop, 0, sizeof(int) * 4, stream));
     LoopMirror mirror;
     MXK_CHECK(mirror.init());
+    mirror.host[0] = mirror.host[1] = mirror.host[2] = 0;
+    mirror.host[3] = (int)n;
+    // (slot 0 is next written by iteration 0's state copy, after this one in stream order)
+    MXK_CUDA(cudaMemcpyAsync(loop, mirror.host, sizeof(int) * 4, cudaMemcpyHostToDevice, stream));
     float* dots = nullptr;
     int64_t chunk_rows = 0;
     if (options->fp32_iterations > 0 && n > 0) {
@@ -200,7 +216,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
 
     // Once per run (kmeans.cu:24-27).
     MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
-    MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
+    if (!kForced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
 
     const bool sharded = comm && comm->nranks > 1;
@@ -225,6 +241,28 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             }
             if (options->verbose && (!comm || comm->rank == 0))
                 std::fprintf(stderr, "iteration=%d precision=FP32\n", it + 1);
+        } else if (kForced8) {
+            // Every point is in the MXFP8 group, in the visiting sequence `ord`;
+            // the group's row count is loop[3] (n, or 0 once the loop stopped).
+            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
+                                      kCentroidTileRows));
+            // MXFP8 at d = 128: the GEMM quantizes the point tiles itself from the
+            // FP32 rows (same bytes as quantize_rows), so this pass disappears.
+            const bool fused_q = d == 128;
+            if (!fused_q)
+                MXK_CHECK(launch_quantize(8, n, d, points, ord, qpoints, pscales, nullptr, loop + 3, stream,
+                                          kPointTileRows));
+            MxArgmin am;
+            am.point_norms = pnorm;
+            am.centroid_norms = cnorm;
+            am.pid = ord;
+            am.labels = labels;
+            am.gaps = nullptr;
+            am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
+            MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, loop + 3, stream,
+                                     true, fused_q ? points : nullptr, n));
+            if (options->verbose && (!comm || comm->rank == 0))
+                std::fprintf(stderr, "iteration=%d fp4=0 fp6=0 fp8=%lld\n", it + 1, (long long)n);
         } else {
             MXK_CUDA(cudaMemsetAsync(cerr, 0, sizeof(float) * k, stream));
             MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream,

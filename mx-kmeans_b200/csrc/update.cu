@@ -201,8 +201,10 @@ __global__ void sum_partials_kernel(const float* __restrict__ partials, int coun
             if (!isfinite(s)) {
                 loop[2] = 1;
                 loop[0] = 1;
+                loop[3] = 0;
             } else if (s <= tolerance) {
                 loop[0] = 1;
+                loop[3] = 0;
             }
         }
     }

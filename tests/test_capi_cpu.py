@@ -64,3 +64,34 @@ def test_errors_are_reported_without_a_gpu(mxk):
 def test_build_flags_target_sm100a():
     mk = open(os.path.join(ROOT, "mx-kmeans_b200", "Makefile")).read()
     assert "ARCH    := -gencode arch=compute_100a,code=sm_100a" in mk
+
+
+def test_forced_mxfp8_flag_matches_select_precision(tmp_path):
+    """The Lloyd driver skips the precision policy's inputs while
+    kSelectPrecisionIsForcedMxfp8 holds; the header's select_precision must then
+    return MXFP8 for every input, including NaN and infinite ones."""
+    import subprocess
+    src = tmp_path / "p.cpp"
+    src.write_text(r'''
+#include <cmath>
+#include <cstdio>
+#include <initializer_list>
+#include <limits>
+#include "precision.hpp"
+int main() {
+    static_assert(kSelectPrecisionIsForcedMxfp8, "flag");
+    const float inf = std::numeric_limits<float>::infinity(), nan = std::nanf("");
+    const float v[] = {0.0f, -0.0f, 1e-30f, 0.5f, 1.0f, 64.0f, 1e6f, 3e38f, inf, -inf, nan, -1.0f};
+    int bad = 0;
+    for (float p4 : v) for (float p6 : v) for (float lc : v) for (float ec : v) for (float gap : v)
+        for (int d : {1, 96, 128, 4096}) bad += select_precision(p4, p6, lc, ec, d, gap) != 8;
+    std::printf("%d\n", bad);
+    return bad != 0;
+}
+''')
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = tmp_path / "p"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(root, "include"), str(src), "-o", str(exe)],
+                   check=True, timeout=120)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "0"
