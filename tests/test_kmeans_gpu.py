@@ -154,3 +154,27 @@ def test_stop_rule_on_device_matches_exact_iteration_count(torch_cuda, mxk):
     # a loose tolerance stops on the first iteration
     it4, _, _ = _run(torch, mxk, x, c0, max_iterations=60, tolerance=1e30)
     assert it4 == 1
+
+
+def test_large_k_two_iterations_match_oracle(torch_cuda, mxk, orc):
+    """The benchmark's K = 2048 at D = 128 (fused quantize, 11 centroid tiles,
+    label-sorted second iteration).  n gives each CTA about three row tiles and a
+    partial last tile.  Integer-valued points make every sum exact, so every
+    cluster whose members agree with the oracle's must have the identical
+    centroid."""
+    torch = torch_cuda
+    n, d, k = 56909, 128, 2048
+    x = np.rint(blobs(n, 96, 256, seed=17, spread=20.0, sigma=3.0)).astype(np.float32)
+    c0 = x[np.random.default_rng(3).choice(n, k, replace=False)].copy()
+    for iters in (1, 2):
+        it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=iters, tolerance=0.0)
+        it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=iters, tolerance=0.0)
+        assert it_g == it_o == iters
+        same = lg == lo
+        assert same.mean() > 0.999
+        counts_g = np.bincount(lg, minlength=k)
+        counts_o = np.bincount(lo, minlength=k)
+        keep = (counts_g == counts_o) & (counts_g > 0)
+        keep[np.unique(np.concatenate([lg[~same], lo[~same]]))] = False
+        assert keep.sum() > 0.9 * k
+        assert np.array_equal(cg[keep], co[keep])
