@@ -125,7 +125,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -134,9 +134,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
-    def stop(self):
+    def stop(self, window=None):
+        """Summary of the samples that arrived within `window` = (t0, t1) of
+        time.monotonic() (all samples when None)."""
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -146,7 +148,9 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for t, line in self.lines:
+            if window and not window[0] <= t <= window[1] + 0.05:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -318,15 +322,18 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    # The clock sampler starts before the warm-up (nvidia-smi takes a while to
+    # come up); only the samples that arrive during the timed region are kept.
+    sampler = ClockSampler(physical_index(local_rank))
+    sampler.start()
     for _ in range(max(args.warmup, 0)):
         step()
 
     # ---- timed region (device time, CUDA events on the launching stream)
-    sampler = ClockSampler(physical_index(local_rank))
-    sampler.start()
     mxk.profile_enable(True)
     launches0 = mxk.launch_count()
     barrier()
+    t_wall0 = time.monotonic()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     iters = 0
@@ -334,10 +341,11 @@ def main():
         iters += step()
     ev1.record(stream)
     barrier()
+    t_wall1 = time.monotonic()
     launches = mxk.launch_count() - launches0
     stats = mxk.profile_read()
     mxk.profile_enable(False)
-    clocks = sampler.stop()
+    clocks = sampler.stop(window=(t_wall0, t_wall1))
     ms = ev0.elapsed_time(ev1)
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
