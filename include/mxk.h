@@ -144,6 +144,23 @@ int mxk_assign_f32_fused(int64_t rows, int k, int d, const float* points, int64_
                          const uint8_t* b_scales, const float* point_norms, const float* centroid_norms,
                          const int* pid, int* labels, float* gaps, const int* start_hint, void* stream);
 
+/* ---- centroid initialisation on the GPU ----------------------------------- */
+
+/* init_centroids_farthest, include/host_utils.hpp:121-141, on device data:
+ * centroids (k x d) receive the same rows the reference's host function picks
+ * (float squared distances feature by feature, the first maximum; first center
+ * row 0).  points: n x d device rows, 16-byte aligned, d % 4 == 0, 1 <= k <= n.
+ * Synchronous on `stream`. */
+int mxk_init_farthest(int64_t n, int d, int k, const float* points, float* centroids, void* stream);
+
+/* init_centroids, include/host_utils.hpp:80-119 (D^2-sampling K-Means++ with
+ * std::mt19937(seed)), on device data: the same rows as the reference's host
+ * function for the same seed (same random draws, double distances, and the
+ * choice its sequential running sum makes).  Same requirements as
+ * mxk_init_farthest; n < 2^31.  Synchronous on `stream`. */
+int mxk_init_kmeanspp(int64_t n, int d, int k, const float* points, float* centroids, uint32_t seed,
+                      void* stream);
+
 /* ---- Lloyd driver --------------------------------------------------------- */
 
 /* kmeans_mixed, include/kmeans.cuh:20-21 / src/kmeans.cu:12-68.  Points n x d

@@ -152,9 +152,28 @@ int main(int argc, char** argv) {
                 throw std::runtime_error("This build requires an sm_100 Blackwell data-center GPU, such as B200");
         }
         const auto points = mxk_cli::read_points(args.input, args.n, args.d, d);
-        const auto initial = args.initialization == "farthest"
-                                 ? mxk_cli::init_farthest(points, args.n, d, args.k)
-                                 : mxk_cli::init_kmeanspp(points, args.n, d, args.k, uint32_t(args.seed));
+        // Initial centroids on GPU 0 (mxk_init_*: the same rows as the reference's
+        // host_utils.hpp functions pick, at GPU speed).
+        std::vector<float> initial(size_t(args.k) * d);
+        {
+            check_cuda(cudaSetDevice(0), "cudaSetDevice");
+            float *dev_points = nullptr, *dev_centroids = nullptr;
+            check_cuda(cudaMalloc(&dev_points, sizeof(float) * points.size()), "cudaMalloc");
+            check_cuda(cudaMalloc(&dev_centroids, sizeof(float) * initial.size()), "cudaMalloc");
+            check_cuda(cudaMemcpy(dev_points, points.data(), sizeof(float) * points.size(), cudaMemcpyHostToDevice),
+                       "cudaMemcpy");
+            const int st = args.initialization == "farthest"
+                               ? mxk_init_farthest(args.n, d, args.k, dev_points, dev_centroids, nullptr)
+                               : mxk_init_kmeanspp(args.n, d, args.k, dev_points, dev_centroids,
+                                                   uint32_t(args.seed), nullptr);
+            if (st == MXK_OK)
+                check_cuda(cudaMemcpy(initial.data(), dev_centroids, sizeof(float) * initial.size(),
+                                      cudaMemcpyDeviceToHost),
+                           "cudaMemcpy");
+            cudaFree(dev_points);
+            cudaFree(dev_centroids);
+            check(st);
+        }
         const int G = args.gpus;
         std::vector<Shard> shards(G);
         unsigned char uid[128] = {};

@@ -53,6 +53,8 @@ SIGNATURES = {
     "mxk_assign_precisions": ([_I64, _I, _P, _P, _F, _F, _P, _P], _I),
     "mxk_check_mxfp8_scale_codec": ([_P, _P], _I),
     "mxk_release_workspace": ([], _I),
+    "mxk_init_farthest": ([_I64, _I, _I, _P, _P, _P], _I),
+    "mxk_init_kmeanspp": ([_I64, _I, _I, _P, _P, ctypes.c_uint32, _P], _I),
     "mxk_gemm_mx": ([_I, _I64, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
     "mxk_gemm_fp32": ([_I64, _I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_clusters": ([_I64, _I, _P, _P, _P, _P, _P, _P, _P], _I),
@@ -132,6 +134,21 @@ def precompute_point_bounds(points, norms, upper, stream=None):
 
 def assign_precisions(n, d, upper, gaps, lc, ec, precision, stream=None):
     check(load().mxk_assign_precisions(n, d, _ptr(upper), _ptr(gaps), lc, ec, _ptr(precision), _stream(stream)))
+
+
+def init_farthest(points, centroids, stream=None):
+    """Farthest-first initial centroids (the reference's init_centroids_farthest)
+    from device points [n, d] into device centroids [k, d]."""
+    n, d = points.shape
+    check(load().mxk_init_farthest(n, d, centroids.shape[0], _ptr(points), _ptr(centroids), _stream(stream)))
+
+
+def init_kmeanspp(points, centroids, seed, stream=None):
+    """K-Means++ initial centroids (the reference's init_centroids with
+    std::mt19937(seed)) from device points [n, d] into device centroids [k, d]."""
+    n, d = points.shape
+    check(load().mxk_init_kmeanspp(n, d, centroids.shape[0], _ptr(points), _ptr(centroids), seed & 0xffffffff,
+                                   _stream(stream)))
 
 
 def release_workspace():
