@@ -85,28 +85,6 @@ def make_dataset(torch, n, device):
     return x
 
 
-def kmeanspp_init(torch, x, k, seed):
-    """D^2-sampling K-Means++ on the device (same draw structure as the reference:
-    first index uniform, each next index with probability proportional to the
-    squared distance to the nearest chosen center).  Untimed set-up."""
-    g = torch.Generator(device=x.device).manual_seed(seed)
-    n = x.shape[0]
-    pn = (x * x).sum(1)
-    centers = torch.empty((k, x.shape[1]), device=x.device)
-    idx = int(torch.randint(0, n, (1,), generator=g, device=x.device).item())
-    dist = torch.full((n,), float("inf"), device=x.device)
-    for c in range(k):
-        centers[c] = x[idx]
-        cvec = x[idx]
-        d = (pn - 2.0 * (x @ cvec) + (cvec * cvec).sum()).clamp_min_(0.0)
-        dist = torch.minimum(dist, d)
-        dist[idx] = 0.0
-        if c + 1 == k:
-            break
-        idx = int(torch.multinomial(dist, 1, generator=g).item())
-    return centers
-
-
 # ----------------------------------------------------------------------------- clocks
 
 class ClockSampler:
@@ -177,9 +155,10 @@ def physical_index(local_rank):
 
 # ----------------------------------------------------------------------------- CPU legs
 
-def cpu_sample_rate(fn_name, n_total):
-    """Time an oracle Lloyd iteration on the host cores over a bounded sample of
-    the workload (about 10-20 s of CPU work); -> (point-iters/s, sample text, cores)."""
+def cpu_sampler(fn_name, n_total, target_s=12.0):
+    """A bounded sample of the workload for an oracle Lloyd iteration on the host
+    cores, sized to about target_s seconds of CPU work.  -> (run, rows, sample
+    text, cores): run() times one iteration over a fresh sample of `rows` points."""
     import numpy as np
     import oracle
     threads = oracle.hardware_threads()
@@ -193,7 +172,7 @@ def cpu_sample_rate(fn_name, n_total):
 
     c0 = sample(K_CLUSTERS)
 
-    def run(x):
+    def run_on(x):
         t = time.perf_counter()
         if fn_name == "lloyd_fp32":
             oracle.lloyd_fp32(x, c0, 1, 0.0, threads)
@@ -202,31 +181,41 @@ def cpu_sample_rate(fn_name, n_total):
         return time.perf_counter() - t
 
     n = 4096
-    t = run(sample(n))
-    target = 12.0
-    n2 = int(min(n_total, max(n, n * target / max(t, 1e-3))))
-    n2 = max(4096, n2 // 4096 * 4096)
-    t2 = run(sample(n2))
+    t = run_on(sample(n))
+    rows = int(min(n_total, max(n, n * target_s / max(t, 1e-3))))
+    rows = max(4096, rows // 4096 * 4096)
     kind = "FP32 Lloyd (oracle port of the reference's host-visible algorithm)" if fn_name == "lloyd_fp32" else \
         "MX Lloyd step (oracle port of kmeans_mixed: MXFP8 quantize, product, assign, update)"
-    return n2 / t2, f"1 iteration of {kind} over {n2} of the {n_total} points, K={K_CLUSTERS}, D={D_PAD}", threads
+    text = f"1 iteration of {kind} over {rows} of the {n_total} points, K={K_CLUSTERS}, D={D_PAD}"
+    return (lambda: run_on(sample(rows))), rows, text, threads
+
+
+def cpu_sample_rate(fn_name, n_total):
+    """Point-iterations per second of one bounded sample; -> (rate, sample text, cores)."""
+    run, rows, text, cores = cpu_sampler(fn_name, n_total)
+    return rows / run(), text, cores
 
 
 def reference_arm(args, rank):
+    """The reference's Lloyd step on the host cores (its GPU path is sm_120a-only):
+    W untimed and K timed steps, each one iteration over a bounded sample."""
     if rank != 0:
         return
-    value, sample, cores = cpu_sample_rate("lloyd_step", args.n)
-    steps = []
-    for _ in range(args.steps):
-        steps.append(value)
+    steps = max(args.steps, 1)
+    run, rows, sample, cores = cpu_sampler("lloyd_step", args.n, target_s=min(12.0, 60.0 / steps))
+    for _ in range(max(args.warmup, 0)):
+        run()
+    seconds = sum(run() for _ in range(steps))
+    value = rows * steps / seconds
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3 / steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "mxfp8+f32", "data": "synthetic",
             "config": {"workload": WORKLOAD},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": ("the reference's Lloyd path is sm_120a-only CUDA (no CPU implementation); this arm times the "
-                     "oracle's C restatement of kmeans_mixed on the host cores")}
+                     "oracle's C restatement of kmeans_mixed on the host cores, each step one iteration over a "
+                     "bounded sample of the workload")}
     print(json.dumps(line), flush=True)
 
 
@@ -295,7 +284,10 @@ def main():
     n = args.n
     x_full = make_dataset(torch, n, dev)
     if args.init == "kmeans++":
-        c_init = kmeanspp_init(torch, x_full, K_CLUSTERS, SEED)
+        # the library's GPU K-Means++: the rows the reference's init_centroids
+        # (include/host_utils.hpp:80-119) picks for this seed; untimed set-up
+        c_init = torch.empty((K_CLUSTERS, x_full.shape[1]), device=dev)
+        mxk.init_kmeanspp(x_full, c_init, SEED)
     else:
         g = torch.Generator(device=dev).manual_seed(SEED)
         c_init = x_full[torch.randperm(n, generator=g, device=dev)[:K_CLUSTERS]].clone()
