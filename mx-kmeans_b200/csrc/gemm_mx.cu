@@ -53,19 +53,24 @@ constexpr int kSfAtom = 512;             // 128 rows x 4 scale bytes
 constexpr int kBAtoms = (kBN + 127) / 128;  // scale atoms per centroid-tile chunk
 constexpr int kMaxBStages = 12;          // centroid-chunk ring depth: as many as shared memory holds
 constexpr int kAccStages = 2;            // 2 x 192 accumulator columns
-constexpr int kEpiPerQuad = 3;           // epilogue warps per TMEM lane quadrant
-constexpr int kSliceCols = kBN / kEpiPerQuad;  // 64 accumulator columns per epilogue warp
+constexpr int kEpiPerQuad = 3;  // epilogue warps per TMEM lane quadrant
+constexpr int kSliceCols = kBN / kEpiPerQuad;  // accumulator columns per epilogue warp
+constexpr int kSubChunks = kSliceCols / 32;    // 32-column TMEM loads per warp and tile
 constexpr int kEpiWarps = 4 * kEpiPerQuad;
-constexpr int kEpiWarp0 = 4;             // warpgroup 0: producer, MMA issuer, two idle warps
+constexpr int kEpiWarp0 = 4;             // warpgroup 0: producer, MMA issuer, two quantizer warps
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
-// Register split (setmaxnreg, argmin kernels): launched at 128 per thread, the
-// first warpgroup drops to kLowRegs and the three epilogue warpgroups rise to
-// kHighRegs.  Per SM sub-partition (one warp of each warpgroup) that is
-// 80 + 3 * 144 = 512 = 4 * 128 registers per lane, exactly the launch budget.
-constexpr int kLaunchRegs = 128;
+// Registers: one CTA per SM owns the whole register file.  With three epilogue
+// warpgroups the kernel launches at 128 per thread and rebalances with
+// setmaxnreg: warpgroup 0 drops to kLowRegs and the epilogue warpgroups rise to
+// kHighRegs (per SM sub-partition 80 + 3 * 144 = 512 = 4 * 128 registers per
+// lane, exactly the launch budget).  (Six epilogue warps per quadrant at 72
+// registers each, for more latency hiding, spilled heavily.)
+constexpr bool kRegSplit = kEpiPerQuad == 3;
+constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
 constexpr int kLowRegs = 80;
 constexpr int kHighRegs = 144;
-static_assert(kLowRegs + 3 * kHighRegs == 4 * kLaunchRegs, "register split must equal the launch budget");
+static_assert(!kRegSplit || kLowRegs + 3 * kHighRegs == 4 * kLaunchRegs,
+              "register split must equal the launch budget");
 constexpr int kMaxSmemNorms = 8192;      // centroid norms staged in shared memory up to this k
 constexpr int kMaxChunks = 8;            // K <= 1024
 constexpr uint32_t kTmemCols = 512;
@@ -74,7 +79,7 @@ constexpr uint32_t kSfbCol = kSfaCol + 32;       // 416: centroid scales, 4 colu
 constexpr int kSfbChunkCols = 4 * kBAtoms;       // TMEM columns per (centroid tile, K chunk)
 constexpr int kMaxResidentSfb = (512 - (int)kSfbCol) / kSfbChunkCols;  // 12 (tile, chunk) pairs
 constexpr int kNumBars = 64;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
-static_assert(kSliceCols == 64 && kBN % 32 == 0, "each epilogue warp drains two 32-column chunks");
+static_assert(kSliceCols % 32 == 0 && kBN % kEpiPerQuad == 0, "each epilogue warp drains whole 32-column chunks");
 static_assert(kSfbCol + kSfbChunkCols <= kTmemCols, "TMEM budget");
 
 struct GemmParams {
@@ -135,8 +140,8 @@ __host__ __device__ inline SmemLayout smem_layout(int kchunks, int a_stages, int
     s.x_off = s.b_off + b_stages * kBTileBytes;   // FP32 staging of one point tile (fused quantize)
     s.sfa_off = s.x_off + (fuse_x ? kBM * kChunk * 4 : 0);
     s.sfb_off = s.sfa_off + a_stages * kchunks * kSfAtom;
-    s.merge_off = s.sfb_off + sfb_atoms * kSfAtom;           // [2 buffers][2 depositors][128 rows] x 16 B
-    s.seed_off = s.merge_off + 2 * 2 * kBM * 16;              // [2 buffers][3 warps][128 rows] x 8 B
+    s.merge_off = s.sfb_off + sfb_atoms * kSfAtom;  // [2 buffers][kEpiPerQuad - 1 depositors][128 rows] x 16 B
+    s.seed_off = s.merge_off + 2 * (kEpiPerQuad - 1) * kBM * 16;  // [2 buffers][kEpiPerQuad warps][128 rows] x 8 B
     s.cn_off = s.seed_off + 2 * kEpiPerQuad * kBM * 8;
     s.bar_off = s.cn_off + (uint32_t)((cn_floats * 4 + 15) / 16 * 16);
     s.total = s.bar_off + kNumBars * 8 + 128;  // barriers, then TMEM slot, abort flag, sweep starts, norm maxima
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp < kEpiWarp0) {
-    if constexpr (kArgmin) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
+    if constexpr (kArgmin && kRegSplit) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         RingPos bring{0, 0u, kBStages};
@@ -759,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     } else {
         // ------------------------------------------------------------ epilogue
-        if constexpr (kArgmin) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
+        if constexpr (kArgmin && kRegSplit) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
         // Warp (q, j): TMEM lane quadrant q = warp % 4 (the only lanes it may
         // read), columns [64 j, 64 j + 64) of every accumulator tile.  All three
         // warps of a quadrant drain each tile together, so a stage is held only
@@ -832,9 +837,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         rel.advance(1);
                     }
                 }
-                uint32_t v[2][32];
-                dev::tmem_ld_32x32b_x32(lane_base + (uint32_t)s * kBN, v[0]);
-                dev::tmem_ld_32x32b_x32(lane_base + (uint32_t)s * kBN + 32, v[1]);
+                uint32_t v[kSubChunks][32];
+#pragma unroll
+                for (int sub = 0; sub < kSubChunks; ++sub)
+                    dev::tmem_ld_32x32b_x32(lane_base + (uint32_t)s * kBN + 32u * sub, v[sub]);
                 dev::tmem_wait_ld();
                 dev::tc_fence_before();
                 __syncwarp();
@@ -842,7 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (++s == kAccStages) s = 0, sph ^= 1u;
                 const int slice0 = ct * kBN + j * kSliceCols;
 #pragma unroll
-                for (int sub = 0; sub < 2; ++sub) {
+                for (int sub = 0; sub < kSubChunks; ++sub) {
                     const int cc = slice0 + sub * 32;
                     if constexpr (!kArgmin) {
                         if (valid) {
@@ -885,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // mbarriers with bounded waits (never bar.sync).
                 const int hb = q * 2 + buf;
                 const uint32_t hph = (uint32_t)(it >> 1) & 1u;
-                float4* slots = merge + (size_t)buf * 2 * kBM;
+                float4* slots = merge + (size_t)buf * (kEpiPerQuad - 1) * kBM;
                 if (j != 0) {
                     if (!dev::mbar_wait(&merge_empty[hb], hph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     slots[(j - 1) * kBM + r] = make_float4(m.first, __int_as_float(m.best), m.largest, m.next);
@@ -893,12 +899,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) dev::mbar_arrive(&merge_full[hb]);
                 } else {
                     if (!dev::mbar_wait(&merge_full[hb], hph, abort_flag, p.err)) { ok = false; break; }
-                    const float4 o0 = slots[r], o1 = slots[kBM + r];
+                    float4 o[kEpiPerQuad - 1];
+#pragma unroll
+                    for (int w = 0; w < kEpiPerQuad - 1; ++w) o[w] = slots[w * kBM + r];
                     __syncwarp();
                     if (lane == 0) dev::mbar_arrive(&merge_empty[hb]);
                     if (valid) {
-                        merge_rowmin<kGaps>(m, o0.x, __float_as_int(o0.y), o0.z, o0.w);
-                        merge_rowmin<kGaps>(m, o1.x, __float_as_int(o1.y), o1.z, o1.w);
+#pragma unroll
+                        for (int w = 0; w < kEpiPerQuad - 1; ++w)
+                            merge_rowmin<kGaps>(m, o[w].x, __float_as_int(o[w].y), o[w].z, o[w].w);
                         p.labels[point] = m.best;
                         if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
