@@ -178,3 +178,32 @@ def test_large_k_two_iterations_match_oracle(torch_cuda, mxk, orc):
         keep[np.unique(np.concatenate([lg[~same], lo[~same]]))] = False
         assert keep.sum() > 0.9 * k
         assert np.array_equal(cg[keep], co[keep])
+
+
+@pytest.mark.parametrize("n,d,k,init", [(30000, 256, 1024, "farthest"), (20000, 768, 2048, "kmeans++")])
+def test_config_shapes_one_iteration_vs_oracle(torch_cuda, mxk, orc, n, d, k, init):
+    """configs[2] / configs[4] shapes at a small N (D = 256 and 768: several K
+    chunks; K = 2048 at D = 768: centroid scales streamed with the ring), from
+    the library's own initialisation, one Lloyd iteration against the oracle."""
+    torch = torch_cuda
+    x = blobs(n, d, 64, seed=d + k, spread=10.0, sigma=1.0)
+    xt = torch.from_numpy(x).cuda()
+    ct = torch.empty((k, d), device="cuda")
+    if init == "farthest":
+        mxk.init_farthest(xt, ct)
+    else:
+        mxk.init_kmeanspp(xt, ct, 19)
+    c0 = ct.cpu().numpy()
+    lab = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    it = mxk.kmeans_mixed(xt, ct, lab, mxk.Options(max_iterations=1, tolerance=0.0))
+    assert it == 1
+    lg, cg = lab.cpu().numpy(), ct.cpu().numpy()
+    shift, co, lo, dots = orc.lloyd_step(x, orc.l2_norm(x), c0, want_dots=True)
+    near, first, second = orc.top2(orc.l2_norm(x), orc.l2_norm(c0), dots)
+    diff = lg != lo
+    scale = orc.l2_norm(x) + orc.l2_norm(c0).max()
+    assert np.all((second - first)[diff] <= 1e-5 * scale[diff])
+    moved = np.unique(np.concatenate([lg[diff], lo[diff]]))
+    keep = np.ones(k, bool)
+    keep[moved] = False
+    assert np.allclose(cg[keep], co[keep], rtol=1e-4, atol=1e-5)
