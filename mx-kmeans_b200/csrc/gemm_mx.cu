@@ -111,6 +111,12 @@ struct GemmParams {
     int* labels;
     float* gaps;
     const int* start_hint;  // optional: a label per point; each tile's sweep starts at its first row's tile
+    // optional (argmin): per point tile, the centroid tiles that can hold one of
+    // its rows' nearest centroids (bit t = tile t; the others are neither loaded,
+    // multiplied nor scanned).  Every bit set when null.  Needs tiles_n <= 64.
+    const uint64_t* tile_mask;
+    float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
+    int best_dist_stride;  // best_dist[point * best_dist_stride]
     unsigned* err;
 };
 
@@ -383,8 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
     volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [2] per A stage
     float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 4;             // [kThreads / 32]
+    // [2] per A stage: the point tile's centroid-tile mask, published with sweep0
+    volatile unsigned long long* sweep_mask =
+        reinterpret_cast<volatile unsigned long long*>(bars + kNumBars) + (4 + kThreads / 32 + 1) / 2;
     static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 8 <= kNumBars, "barrier slots");
-    static_assert(4 + kThreads / 32 <= 32, "words after the barriers");
+    static_assert(4 + kThreads / 32 + 1 + 4 <= 32, "words after the barriers");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mrows = p.m_dev ? (int64_t)*p.m_dev : p.m;
@@ -455,12 +464,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             return p.pid ? (int64_t)p.pid[t * kBM] : t * kBM;
         };
         auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        auto mask_of = [&](int64_t t) -> uint64_t {  // (lane 0 only) centroid tiles of point tile t
+            return p.tile_mask && t < tiles_m && lane == 0 ? p.tile_mask[t] : ~0ull;
+        };
         int hint_cur = hint_of(lead_id(blockIdx.x));
         int64_t lead_nxt = lead_id(blockIdx.x + step);
+        uint64_t mask_nxt = mask_of(blockIdx.x);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
+            const uint64_t tmask = mask_nxt;
             hint_cur = hint_of(lead_nxt);
             lead_nxt = lead_id(tile + 2 * step);
+            mask_nxt = mask_of(tile + step);
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
             // (fused quantize: the quantizer warps own the point tile and its sweep start)
@@ -484,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
             if (!p.fuse_x) {
-                if (lane == 0) sweep0[as] = ct0;  // published to the MMA thread by the a_full arrival
+                if (lane == 0) sweep0[as] = ct0, sweep_mask[as] = tmask;  // published by the a_full arrival
                 dev::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) dev::mbar_arrive(&a_full[as]);
@@ -495,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
                 for (int i = 0; i < tiles_n && ok; ++i) {
                     const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
+                    if (!((tmask >> ct) & 1ull)) continue;
                     for (int kc = 0; kc < p.kchunks; ++kc) {
                         if (!dev::mbar_wait(&b_empty[bring.slot], bring.phase ^ 1u, abort_flag, p.err)) {
                             ok = false;
@@ -568,8 +584,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                 16, 128, dev::kLayoutNone));
                     const uint64_t adesc = dev::smem_desc(dev::smem_addr(smem + a_off), 16, 1024, dev::kLayoutSwizzle128);
                     int ct = sweep0[as];
+                    const uint64_t tmask = sweep_mask[as];
                     uint32_t sfb = tmem + kSfbCol + (uint32_t)(ct * kSfbChunkCols);
                     for (int i = 0; i < tiles_n; ++i) {
+                        if (!((tmask >> ct) & 1ull)) {  // pruned centroid tile
+                            if (++ct == tiles_n) ct = 0, sfb = tmem + kSfbCol;
+                            else sfb += kSfbChunkCols;
+                            continue;
+                        }
                         if (!dev::mbar_wait_lean(&acc_empty[s], sph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                         dev::tc_fence_after();
                         if (!dev::mbar_wait_lean(&b_full[slot], bph, abort_flag, p.err)) { ok = false; break; }
@@ -601,7 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                             dev::smem_desc(sfa_base + kc * kSfAtom, 16, 128, dev::kLayoutNone));
                 const uint64_t adesc0 = dev::smem_desc(a_base, 16, 1024, dev::kLayoutSwizzle128);
                 int ct = sweep0[as];
+                const uint64_t tmask = sweep_mask[as];
                 for (int i = 0; i < tiles_n && ok; ++i, ct = ct + 1 == tiles_n ? 0 : ct + 1) {
+                    if (!((tmask >> ct) & 1ull)) continue;  // pruned centroid tile
                     if (!dev::mbar_wait_lean(&acc_empty[s], sph ^ 1u, abort_flag, p.err)) { ok = false; break; }
                     dev::tc_fence_after();
                     const uint32_t d_tmem = tmem + (uint32_t)s * kBN;
@@ -752,7 +776,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             dev::fence_proxy_async();  // generic shared-memory writes -> visible to the tensor core
             __syncwarp();
-            if (warp == 2 && lane == 0) sweep0[as] = ct0;  // published by the a_full arrival
+            if (warp == 2 && lane == 0) {  // published to the MMA thread by the a_full arrival
+                sweep0[as] = ct0;
+                sweep_mask[as] = p.tile_mask ? p.tile_mask[tile] : ~0ull;
+            }
             if (lane == 0) dev::mbar_arrive(&a_full[as]);
         }
         // Unwinding after an abort: wait (bounded) for this warp's gathers in flight.
@@ -789,6 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             cmax = c > cmax || c != c ? c : cmax;
         }
         RingPos rel{0, 0u, kBStages};
+        uint32_t seed_ph = 0;  // phase of this quadrant's seed exchanges
         int s = 0;           // accumulator stage of the next tile
         uint32_t sph = 0;
         bool ok = true;
@@ -809,9 +837,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         auto norm_of = [&](int64_t id) -> float { return id >= 0 ? p.pn[id] : 0.0f; };
         auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        auto mask_of = [&](int64_t t) -> uint64_t {  // centroid tiles of point tile t
+            return p.tile_mask && t < tiles_m ? p.tile_mask[t] : ~0ull;
+        };
         int64_t id_cur = row_id(blockIdx.x), lead_cur = lead_id(blockIdx.x);
         float pn_cur = norm_of(id_cur);
         int hint_cur = hint_of(lead_cur);
+        uint64_t mask_cur = mask_of(blockIdx.x);
         int64_t id_nxt = row_id(blockIdx.x + step), lead_nxt = lead_id(blockIdx.x + step);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -823,12 +855,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             // issue the next row tiles' loads now; they are consumed an iteration later
             const float pn_nxt = norm_of(id_nxt);
             const int hint_nxt = hint_of(lead_nxt);
+            const uint64_t tmask = mask_cur;
+            const uint64_t mask_nxt = mask_of(tile + step);
             const int64_t id_nn = row_id(tile + 2 * step), lead_nn = lead_id(tile + 2 * step);
             const uint64_t pn2 = dev::pack2(pn, pn);
             const float pc = pn + cmax;
             RowMin m{__int_as_float(0x7f800000), -1e38f, -1e38f, 0x7fffffff};
             for (int i = 0; i < tiles_n; ++i) {
                 const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
+                if (!((tmask >> ct) & 1ull)) continue;  // pruned centroid tile (the first, ct0, never is)
                 if (!dev::mbar_wait(&acc_full[s], sph, abort_flag, p.err)) { ok = false; break; }
                 dev::tc_fence_after();
                 if (releaser) {
@@ -871,12 +906,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         fold_chunk<kGaps>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m);
                     }
                 }
-                if (seeding && i == 0) {
-                    float2* mine = seed + (size_t)(buf * kEpiPerQuad) * kBM;
+                if (seeding && i == 0 && (tmask & (tmask - 1ull)) != 0) {  // (more tiles follow in this row tile)
+                    // The exchange is skipped for row tiles with a single centroid tile,
+                    // so its barrier phase and buffer follow their own count (the same
+                    // in the quadrant's three warps, which see the same masks).
+                    float2* mine = seed + (size_t)(seed_ph * kEpiPerQuad) * kBM;
                     mine[j * kBM + r] = make_float2(m.first, __int_as_float(m.best));
                     __syncwarp();
                     if (lane == 0) dev::mbar_arrive(&seed_bar[q]);
-                    if (!dev::mbar_wait(&seed_bar[q], (uint32_t)buf, abort_flag, p.err)) { ok = false; break; }
+                    if (!dev::mbar_wait(&seed_bar[q], seed_ph, abort_flag, p.err)) { ok = false; break; }
+                    seed_ph ^= 1u;
 #pragma unroll
                     for (int o = 0; o < kEpiPerQuad; ++o) {
                         if (o == j) continue;
@@ -909,11 +948,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int w = 0; w < kEpiPerQuad - 1; ++w)
                             merge_rowmin<kGaps>(m, o[w].x, __float_as_int(o[w].y), o[w].z, o[w].w);
                         p.labels[point] = m.best;
+                        if (p.best_dist) p.best_dist[point * p.best_dist_stride] = m.first;
                         if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
                 }
             }
-            id_cur = id_nxt, lead_cur = lead_nxt, pn_cur = pn_nxt, hint_cur = hint_nxt;
+            id_cur = id_nxt, lead_cur = lead_nxt, pn_cur = pn_nxt, hint_cur = hint_nxt, mask_cur = mask_nxt;
             id_nxt = id_nn, lead_nxt = lead_nn;
         }
     }
@@ -990,6 +1030,10 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         p.labels = argmin->labels;
         p.gaps = argmin->gaps;
         p.start_hint = argmin->start_hint;
+        p.tile_mask = argmin->tile_mask;
+        p.best_dist = argmin->best_dist;
+        p.best_dist_stride = argmin->best_dist_stride;
+        MXK_REQUIRE(!p.tile_mask || (n + kBN - 1) / kBN <= 64, "gemm_mx: a tile mask covers at most 64 centroid tiles");
     }
     p.err = device_error_word();
     if (!p.err) return fail(MXK_ERR_CUDA, "gemm_mx: cannot allocate the device error word");

@@ -64,6 +64,14 @@ struct MxArgmin {
     // overwritten): each 128-row tile sweeps the centroids starting at the tile
     // of its first row's hint; results do not depend on it
     const int* start_hint = nullptr;
+    // optional: per 128-row point tile, a mask of the 192-centroid tiles that may
+    // hold a row's nearest centroid (bit t = centroid tile t; the tile of the
+    // first row's start_hint must be set); the others are skipped.  n <= 64 tiles.
+    const uint64_t* tile_mask = nullptr;
+    // optional: each point's distance to its nearest centroid, at
+    // best_dist[point * best_dist_stride]
+    float* best_dist = nullptr;
+    int best_dist_stride = 1;
 };
 // Dense: out[m x n] = A . B^T.  Argmin: labels of the m rows against n centroids.
 // rows_dev (optional) = device-resident m (m is then an upper bound).
@@ -77,6 +85,32 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
                    const uint8_t* b, const uint8_t* b_scales, float* out, const MxArgmin* argmin,
                    const int* rows_dev, cudaStream_t stream, bool scale_atoms = false,
                    const float* points_f32 = nullptr, int64_t points_rows = 0);
+
+// ---- prune.cu ----------------------------------------------------------------
+// Exact pruning of centroid tiles (see prune.cu for the bounds).  Supported for
+// at most 64 centroid tiles and d % 128 == 0, d <= 1024.
+bool prune_supported(int64_t k, int d);
+// Per point, once per run: pinfo = (+inf: the slot the GEMM writes the point's
+// distance into, |x|^2 - |x^|^2, |x^|^2, |x|^2) for its MXFP8 round trip x^
+// (pn: the norms the GEMM uses).
+int launch_point_quant_stats(int64_t n, int d, const float* points, const float* pn, float4* pinfo,
+                             cudaStream_t stream);
+// Centroid geometry: chat (k x d dequantized centroids), cst (k x (|c|^2 -
+// |c^|^2, |c^|^2, |c|^2 as cn, 0)), tst (per tile: min beta, max |c^|^2, max
+// |c|^2, non-finite flag) and, with prev: delta (k upper bounds of |c^ -
+// c^_prev|) and dmin (k x tiles lower bounds of quantized centroid-to-tile
+// distances).  stop: the Lloyd loop's stop word (optional).
+// gram: gram_scratch_floats(k) floats of scratch.
+int64_t gram_scratch_floats(int k);
+int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
+                             float* gram, float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
+                             cudaStream_t stream);
+// Per 128-row point tile (rows in pid order), the mask of centroid tiles that
+// may hold a row's nearest centroid, from the previous labels and distances
+// and the current (cst) and previous (cst_old) centroid stats.
+int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
+                     const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
+                     const float* dmin, uint64_t* mask, const int* stop, cudaStream_t stream);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

@@ -205,6 +205,24 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
+    // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
+    // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
+    const bool prune = kForced8 && n > 0 && prune_supported(k, d);
+    const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
+    float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *gram = nullptr;
+    float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
+    float4 *cstats = nullptr, *tstats = nullptr;  // [2][k] per-centroid stats by iteration parity; [ctiles]
+    uint64_t* tmask = nullptr;
+    if (prune) {
+        MXK_CHECK(ws.alloc(&pinfo, n));
+        MXK_CHECK(ws.alloc(&chat, kd));
+        MXK_CHECK(ws.alloc(&gram, gram_scratch_floats(k)));
+        MXK_CHECK(ws.alloc(&dmin, (int64_t)k * ctiles));
+        MXK_CHECK(ws.alloc(&cdelta, k));
+        MXK_CHECK(ws.alloc(&cstats, 2 * (int64_t)k));
+        MXK_CHECK(ws.alloc(&tstats, ctiles));
+        MXK_CHECK(ws.alloc(&tmask, (n + kPointTileRows - 1) / kPointTileRows));
+    }
     int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)
     MXK_CHECK(ws.alloc(&loop, 4));
     LoopMirror mirror;
@@ -223,6 +241,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
 
     // Once per run (kmeans.cu:24-27).
     MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
+    if (prune) MXK_CHECK(launch_point_quant_stats(n, d, points, pnorm, pinfo, stream));
     if (!kForced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
 
@@ -238,8 +257,19 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
             ord = order;
         }
-        MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
+        // Pruning needs the previous iteration's labels and distances from the
+        // MX GEMM (not an FP32 iteration) and, in prev, the centroids it used.
+        const bool prune_it = prune && it >= 1 && it - 1 >= options->fp32_iterations;
+        float4* cst = cstats + (int64_t)(it & 1) * k;
+        const float4* cst_old = cstats + (int64_t)((it + 1) & 1) * k;
+        if (prune && it >= options->fp32_iterations)  // this iteration's centroid stats (the next one's old ones)
+            MXK_CHECK(launch_centroid_geometry(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, gram, dmin,
+                                               cdelta, cst, tstats, loop, stream));
+        if (prune_it)
+            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, loop,
+                                       stream));
+        MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         if (it < options->fp32_iterations) {
             // kmeans.cu:31-34: FP32 product, assignment without pid (gap init -1).
             for (int64_t r0 = 0; r0 < n; r0 += chunk_rows) {
@@ -268,6 +298,9 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.labels = labels;
             am.gaps = nullptr;
             am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
+            am.tile_mask = prune_it ? tmask : nullptr;
+            am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
+            am.best_dist_stride = 4;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, loop + 3, stream,
                                      true, fused_q ? points : nullptr, n));
             if (options->verbose && (!comm || comm->rank == 0))

@@ -1,0 +1,281 @@
+// Exact pruning of centroid tiles for the fused assignment GEMM.
+//
+// A Lloyd iteration assigns each point x to argmin_c d(x, c), where d is the
+// MX distance fmaf(-2, D(x, c), |x|^2 + |c|^2) and D the tensor-core product of
+// the MXFP8-quantized rows x^ and c^.  The GEMM need not multiply a
+// 192-centroid tile against a 128-point tile when no point of the point tile can
+// have its minimum there.  The test proves that from the previous iteration,
+// working in the quantized space where the tensor core works:
+//
+// * d(x, c) = |x^ - c^|^2 + alpha_x + beta_c + rho, with the per-row constants
+//   alpha_x = |x|^2 - |x^|^2 and beta_c = |c|^2 - |c^|^2 (the norms the GEMM
+//   adds are those of the unquantized rows) and a rounding term
+//   |rho| <= kappa (|x|^2 + |c|^2 + |x^|^2 + |c^|^2 + 2 |x^| |c^|) covering the
+//   tensor core's FP32 accumulation (taken as <= 1.5e-5 of sum |x^_i c^_i|), the
+//   fmaf, and the FP32 evaluation of alpha and beta.
+// * Upper bound.  x's previous label a and previous distance d_prev (written by
+//   the previous GEMM against c_a_old) give |x^ - c^_a_old| <= sqrt(d_prev -
+//   alpha_x - beta_a_old + rho_old); with the quantized centroid's move
+//   delta_a = |c^_a - c^_a_old|, r = that + delta_a >= |x^ - c^_a| and
+//   U = r^2 + alpha_x + beta_a + rho >= d(x, c_a) >= the new minimum.
+// * Lower bound.  For c in tile T, |x^ - c^| >= |c^ - c^_a| - r >= dmin(a, T) -
+//   r (dmin: the smallest quantized distance from c^_a into T), so d(x, c) >=
+//   max(0, dmin(a, T) - r)^2 + alpha_x + min_T beta - rho_T.  When that exceeds
+//   U, no centroid of T can be x's nearest (nor tie with it): T is skipped.
+//
+// A point tile computes the union of its rows' tiles (each row's own tile
+// always among them).  Every bound is evaluated with outward margins well above
+// the FP32 rounding of its own arithmetic, and any non-finite input keeps every
+// tile.  The labels are those of the unpruned computation, bit for bit (tested
+// by replaying iterations without a mask).
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "mx_codec.cuh"
+
+namespace mxk {
+namespace {
+
+constexpr int kGeoThreads = 256;
+constexpr int kGramRows = 1024;  // centroid rows per Gram product
+constexpr int kMaxPruneTiles = 64;
+
+// MXFP8 round trip of 4 consecutive features held by one lane; the 8 lanes of
+// each 32-feature block share its scale (quantize_rows' arithmetic, the values
+// the tensor core multiplies).
+__device__ __forceinline__ float4 mxfp8_round_trip4(float4 x, int lane) {
+    float amax = fmaxf(fmaxf(fmaxf(0.0f, fabsf(x.x)), fmaxf(fabsf(x.y), fabsf(x.z))), fabsf(x.w));
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    (void)lane;
+    const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
+    const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
+    auto rt = [&](float v) { return dev::e4m3_decode(dev::e4m3x2_encode(v * rcp, 0.0f) & 0xffu) * scale; };
+    return make_float4(rt(x.x), rt(x.y), rt(x.z), rt(x.w));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Per point, once per run (one warp per row): pinfo = (distance slot, alpha =
+// |x|^2 - |x^|^2, |x^|^2, |x|^2), |x|^2 being the norm the GEMM uses; the GEMM
+// writes each point's distance into the first slot.
+__global__ void __launch_bounds__(256) point_quant_stats_kernel(int64_t n, int d, const float* __restrict__ points,
+                                                                const float* __restrict__ pn,
+                                                                float4* __restrict__ pinfo) {
+    const int lane = threadIdx.x & 31;
+    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (p >= n) return;
+    const float* row = points + p * d;
+    float h = 0.0f;
+    for (int j = 4 * lane; j < d; j += 128) {
+        const float4 xh = mxfp8_round_trip4(__ldg(reinterpret_cast<const float4*>(row + j)), lane);
+        h = fmaf(xh.x, xh.x, fmaf(xh.y, xh.y, fmaf(xh.z, xh.z, fmaf(xh.w, xh.w, h))));
+    }
+    h = warp_sum(h);
+    if (lane == 0) pinfo[p] = make_float4(__int_as_float(0x7f800000), pn[p] - h, h, pn[p]);
+}
+
+// Per centroid (one warp per row): the dequantized row c^ into chat, stats
+// cst[a] = (beta = |c|^2 - |c^|^2, |c^|^2, |c|^2, 0), and delta[a] >= |c^_a -
+// c^_a_old| (the previous centroids' round trip; +inf without prev).
+__global__ void __launch_bounds__(256) centroid_quant_kernel(int k, int d, const float* __restrict__ c,
+                                                             const float* __restrict__ prev,
+                                                             const float* __restrict__ cn, float* __restrict__ chat,
+                                                             float4* __restrict__ cst, float* __restrict__ delta,
+                                                             const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    const int lane = threadIdx.x & 31;
+    const int a = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (a >= k) return;
+    float h = 0.0f, mv = 0.0f;
+    for (int j = 4 * lane; j < d; j += 128) {
+        const float4 ch = mxfp8_round_trip4(__ldg(reinterpret_cast<const float4*>(c + (int64_t)a * d + j)), lane);
+        *reinterpret_cast<float4*>(chat + (int64_t)a * d + j) = ch;
+        h = fmaf(ch.x, ch.x, fmaf(ch.y, ch.y, fmaf(ch.z, ch.z, fmaf(ch.w, ch.w, h))));
+        if (prev) {
+            const float4 oh =
+                mxfp8_round_trip4(__ldg(reinterpret_cast<const float4*>(prev + (int64_t)a * d + j)), lane);
+            const float t0 = ch.x - oh.x, t1 = ch.y - oh.y, t2 = ch.z - oh.z, t3 = ch.w - oh.w;
+            mv = fmaf(t0, t0, fmaf(t1, t1, fmaf(t2, t2, fmaf(t3, t3, mv))));
+        }
+    }
+    h = warp_sum(h);
+    mv = warp_sum(mv);
+    if (lane == 0) {
+        const float rel = 1.0f + (float)(d + 8) * 1.2e-7f;  // rounding of an FP32 sum of d squares
+        delta[a] = prev ? sqrtf(mv * rel) * (1.0f + 1e-6f) : __int_as_float(0x7f800000);
+        cst[a] = make_float4(cn[a] - h, h, cn[a], 0.0f);
+    }
+}
+
+// dmin[(a0 + i) * tiles + T], i < rows: a lower bound of min over c in T of
+// |c^ - c^_a|, from the Gram rows gram[i][b] = <c^_{a0+i}, c^_b> (FP32 SGEMM)
+// and the quantized squared norms cst[].y: |c^_a - c^_b|^2 = h_a + h_b - 2 G_ab,
+// less a bound on the rounding of the product, the norms and this sum.
+__global__ void __launch_bounds__(kGeoThreads) gram_pairs_kernel(int a0, int k, int d, int tiles, int tile_cols,
+                                                                 const float* __restrict__ gram,
+                                                                 const float4* __restrict__ cst,
+                                                                 float* __restrict__ dmin,
+                                                                 const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    __shared__ unsigned best[kMaxPruneTiles];
+    const int a = a0 + blockIdx.x;
+    for (int t = threadIdx.x; t < kMaxPruneTiles; t += blockDim.x) best[t] = 0x7f800000u;
+    __syncthreads();
+    const float ha = cst[a].y;
+    const float rel = (float)(d + 16) * 1.2e-7f;
+    const float* g = gram + (int64_t)blockIdx.x * k;
+    for (int b = threadIdx.x; b < k; b += blockDim.x) {
+        const float hb = cst[b].y;
+        float lo = 0.0f;
+        if (b != a) {
+            const float d2 = ha + hb - 2.0f * g[b];
+            lo = d2 - rel * (ha + hb + 2.0f * sqrtf(ha) * sqrtf(hb));
+        }
+        if (lo == lo) atomicMin(&best[b / tile_cols], __float_as_uint(fmaxf(lo, 0.0f)));
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+        const float lo = __uint_as_float(best[t]);  // +inf if every entry was NaN: then no bound
+        dmin[(int64_t)a * tiles + t] = lo < __int_as_float(0x7f800000) ? sqrtf(lo) * (1.0f - 1e-6f) : 0.0f;
+    }
+}
+
+// Per centroid tile: (min beta, max |c^|^2, max |c|^2, non-finite flag).
+__global__ void tile_stats_kernel(int k, int tiles, int tile_cols, const float4* __restrict__ cst,
+                                  float4* __restrict__ tst, const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+        float4 m = make_float4(__int_as_float(0x7f800000), 0.0f, 0.0f, 0.0f);
+        const int e = min(k, (t + 1) * tile_cols);
+        for (int b = t * tile_cols; b < e; ++b) {
+            const float4 v = cst[b];
+            m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
+            if (!(fabsf(v.x) < __int_as_float(0x7f800000) && v.y < __int_as_float(0x7f800000) &&
+                  v.z < __int_as_float(0x7f800000)))
+                m.w = 1.0f;  // a non-finite centroid: no pruning against this tile
+        }
+        tst[t] = m;
+    }
+}
+
+// The rounding term rho of the header comment for squared norms px, pc (of x and
+// c) and hx2, hc2 (of x^ and c^).
+__device__ __forceinline__ float rho_bound(float px, float hx2, float pc, float hc2, float kappa) {
+    return kappa * (px + pc + hx2 + hc2 + 2.0f * sqrtf(hx2) * sqrtf(hc2));
+}
+
+// One block per 128-row point tile: the union over its rows of the centroid
+// tiles the bounds cannot exclude.
+__global__ void __launch_bounds__(128) tile_mask_kernel(
+    int64_t rows, int k, int d, int tiles, int tile_cols, const int* __restrict__ pid,
+    const int* __restrict__ prev_label, const float4* __restrict__ pinfo, const float4* __restrict__ cst,
+    const float4* __restrict__ cst_old,
+    const float4* __restrict__ tst, const float* __restrict__ delta, const float* __restrict__ dmin,
+    uint64_t* __restrict__ mask, const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
+    const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
+    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
+    const float inf = __int_as_float(0x7f800000);
+    uint64_t m = 0;
+    if (row < rows) {
+        const int64_t x = pid ? pid[row] : row;
+        const int a = prev_label[x];
+        m = all;
+        if ((unsigned)a < (unsigned)k) {
+            const float4 pi = pinfo[x];  // (previous distance, alpha_x, |x^|^2, |x|^2)
+            const float dp = pi.x, px = pi.w;
+            const float2 ps = make_float2(pi.y, pi.z);
+            const float4 now = cst[a], old = cst_old[a];
+            const float r0 = dp - ps.x - old.x + rho_bound(px, ps.y, old.z, old.y, kappa);
+            const float r = (sqrtf(fmaxf(r0, 0.0f)) * (1.0f + 1e-6f) + delta[a]) * (1.0f + 1e-6f);
+            const float u = r * r * (1.0f + 1e-6f) + ps.x + now.x + rho_bound(px, ps.y, now.z, now.y, kappa);
+            const float um = u + 1e-4f * (fabsf(u) + fabsf(ps.x) + fabsf(now.x)) + 1e-30f;
+            if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(ps.x) < inf) {  // false for NaN too: keep every tile
+                m = 1ull << (a / tile_cols);  // its own tile
+                const float* dm = dmin + (int64_t)a * tiles;
+                for (int t = 0; t < tiles; ++t) {
+                    const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
+                    const float g = fmaxf(dm[t] - r, 0.0f);
+                    const float lb = g * g * (1.0f - 1e-6f) + ps.x + ts.x - rho_bound(px, ps.y, ts.z, ts.y, kappa);
+                    const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(ps.x) + fabsf(ts.x));
+                    if (!(lbm > um) || ts.w != 0.0f) m |= 1ull << t;
+                }
+            }
+        }
+    }
+    // union over the 128 rows
+    m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
+        ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
+    __shared__ uint64_t part[4];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) mask[blockIdx.x] = part[0] | part[1] | part[2] | part[3];
+}
+
+}  // namespace
+
+bool prune_supported(int64_t k, int d) {
+    return (k + kCentroidTileRows - 1) / kCentroidTileRows <= kMaxPruneTiles && d % 128 == 0 && d <= 1024;
+}
+
+int launch_point_quant_stats(int64_t n, int d, const float* points, const float* pn, float4* pinfo,
+                             cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    MXK_REQUIRE(d % 128 == 0, "point stats: d must be a multiple of 128");
+    LaunchScope scope("point_quant_stats", stream);
+    point_quant_stats_kernel<<<(unsigned)((n * 32 + 255) / 256), 256, 0, stream>>>(n, d, points, pn, pinfo);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int64_t gram_scratch_floats(int k) { return (int64_t)std::min(k, kGramRows) * k; }
+
+int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
+                             float* gram, float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
+                             cudaStream_t stream) {
+    MXK_REQUIRE(prune_supported(k, d), "centroid geometry: unsupported shape");
+    const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
+    {
+        LaunchScope scope("centroid_quant_stats", stream);
+        centroid_quant_kernel<<<(unsigned)(((int64_t)k * 32 + 255) / 256), 256, 0, stream>>>(k, d, centroids, prev,
+                                                                                            cn, chat, cst, delta,
+                                                                                            stop);
+        MXK_CUDA(cudaGetLastError());
+    }
+    if (prev) {  // the pairwise bounds are only used with a previous iteration
+        for (int a0 = 0; a0 < k; a0 += kGramRows) {
+            const int rows = std::min(kGramRows, k - a0);
+            MXK_CHECK(launch_gemm_fp32(rows, k, d, chat + (int64_t)a0 * d, chat, gram, stream));
+            LaunchScope scope("centroid_pairs", stream);
+            gram_pairs_kernel<<<(unsigned)rows, kGeoThreads, 0, stream>>>(a0, k, d, tiles, kCentroidTileRows, gram, cst,
+                                                                         dmin, stop);
+            MXK_CUDA(cudaGetLastError());
+        }
+    }
+    LaunchScope scope("tile_stats", stream);
+    tile_stats_kernel<<<1, 64, 0, stream>>>(k, tiles, kCentroidTileRows, cst, tst, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
+                     const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
+                     const float* dmin, uint64_t* mask, const int* stop, cudaStream_t stream) {
+    if (rows <= 0) return MXK_OK;
+    const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
+    MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
+    const int64_t blocks = (rows + kPointTileRows - 1) / kPointTileRows;
+    LaunchScope scope("tile_mask", stream);
+    tile_mask_kernel<<<(unsigned)blocks, 128, 0, stream>>>(rows, k, d, tiles, kCentroidTileRows, pid, prev_label,
+                                                           pinfo, cst, cst_old, tst, delta, dmin, mask, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+}  // namespace mxk

@@ -207,3 +207,43 @@ def test_config_shapes_one_iteration_vs_oracle(torch_cuda, mxk, orc, n, d, k, in
     keep = np.ones(k, bool)
     keep[moved] = False
     assert np.allclose(cg[keep], co[keep], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,blobs_k,spread,sigma,iters", [(56909, 300, 12.0, 2.0, (2, 3, 5)),
+                                                         (300000, 2048, 8.0, 0.6, (4, 8))])
+def test_pruned_assignment_equals_unpruned(torch_cuda, mxk, n, blobs_k, spread, sigma, iters):
+    """From the second iteration on, the driver skips centroid tiles that the
+    previous iteration's labels and distances prove cannot hold a point's nearest
+    centroid.  Replay: the labels of iteration t (from a run capped at t) must
+    equal an unpruned assignment (mxk_assign_f32_fused, no tile mask) against the
+    centroids a run capped at t - 1 ends with.  Integer-valued points make every
+    update exact, so both runs see the same centroids."""
+    # (the second case: many row tiles per CTA, most of them needing a single
+    # centroid tile, mixed with multi-tile ones)
+    torch = torch_cuda
+    d, k = 128, 2048
+    x = np.rint(blobs(n, 96, blobs_k, seed=31, spread=spread, sigma=sigma) * 4).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    c0 = torch.empty((k, d), device="cuda")
+    mxk.init_kmeanspp(xt, c0, 5)
+    pn = torch.empty(n, device="cuda")
+    mxk.compute_l2_norm(xt, pn)
+
+    def run(iters):
+        ct = c0.clone()
+        lab = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        assert mxk.kmeans_mixed(xt, ct, lab, mxk.Options(max_iterations=iters, tolerance=0.0)) == iters
+        return ct, lab
+
+    for t in iters:
+        c_prev, _ = run(t - 1)
+        _, lab_t = run(t)
+        qc = torch.empty(k * d, dtype=torch.uint8, device="cuda")
+        sc = torch.empty(k * d // 32, dtype=torch.uint8, device="cuda")
+        mxk.quantize_rows(8, c_prev, qc, sc)
+        cn = torch.empty(k, device="cuda")
+        mxk.compute_l2_norm(c_prev, cn)
+        lab_u = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        mxk.assign_f32_fused(n, k, d, xt, qc, sc, pn, cn, lab_u)
+        torch.cuda.synchronize()
+        assert torch.equal(lab_t, lab_u), f"iteration {t}: {(lab_t != lab_u).sum().item()} labels differ"
