@@ -169,6 +169,15 @@ int mxk_init_kmeanspp(int64_t n, int d, int k, const float* points, float* centr
 int mxk_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
                      const mxk_options* options, int* iterations, void* stream);
 
+/* Opt-in variant, no reference counterpart: the same Lloyd loop with the points'
+ * MXFP8 encoding computed once per call and kept (n * d + n * d / 32 bytes
+ * more device memory) instead of re-quantizing every iteration as the
+ * reference does (src/kmeans.cu:45-57).  Under the forced-MXFP8 policy the
+ * bytes are the same every iteration, so labels and centroids are those of
+ * mxk_kmeans_mixed. */
+int mxk_kmeans_mixed_cached(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                            const mxk_options* options, int* iterations, void* stream);
+
 /* ---- multi-GPU (no counterpart in the reference, which is single-GPU) ------ */
 
 /* Row-sharded Lloyd: each rank holds n_local rows; centroids are replicated; per

@@ -52,6 +52,7 @@ constexpr int kBTileBytes = kBN * kChunk;   // 24 KB
 constexpr int kSfAtom = 512;             // 128 rows x 4 scale bytes
 constexpr int kBAtoms = (kBN + 127) / 128;  // scale atoms per centroid-tile chunk
 constexpr int kMaxBStages = 12;          // centroid-chunk ring depth: as many as shared memory holds
+constexpr int kMaxAStages = 4;           // point-tile stages (4 when no FP32 staging takes the room)
 constexpr int kAccStages = 2;            // 2 x 192 accumulator columns
 constexpr int kEpiPerQuad = 3;  // epilogue warps per TMEM lane quadrant
 constexpr int kSliceCols = kBN / kEpiPerQuad;  // accumulator columns per epilogue warp
@@ -78,7 +79,7 @@ constexpr uint32_t kSfaCol = kAccStages * kBN;  // 384: 4 columns per K chunk (<
 constexpr uint32_t kSfbCol = kSfaCol + 32;       // 416: centroid scales, 4 columns per atom
 constexpr int kSfbChunkCols = 4 * kBAtoms;       // TMEM columns per (centroid tile, K chunk)
 constexpr int kMaxResidentSfb = (512 - (int)kSfbCol) / kSfbChunkCols;  // 12 (tile, chunk) pairs
-constexpr int kNumBars = 64;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
+constexpr int kNumBars = 72;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
 static_assert(kSliceCols % 32 == 0 && kBN % kEpiPerQuad == 0, "each epilogue warp drains whole 32-column chunks");
 static_assert(kSfbCol + kSfbChunkCols <= kTmemCols, "TMEM budget");
 
@@ -373,11 +374,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms, p.fuse_x);
     const int kBStages = p.b_stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-    uint64_t* a_full = bars;                 // [2]
-    uint64_t* a_empty = bars + 2;            // [2]
-    uint64_t* b_full = bars + 4;             // [kMaxBStages]
-    uint64_t* b_empty = bars + 4 + kMaxBStages;
-    uint64_t* acc_full = bars + 4 + 2 * kMaxBStages;  // [kAccStages]
+    uint64_t* a_full = bars;                 // [kMaxAStages]
+    uint64_t* a_empty = bars + kMaxAStages;  // [kMaxAStages]
+    uint64_t* b_full = bars + 2 * kMaxAStages;  // [kMaxBStages]
+    uint64_t* b_empty = b_full + kMaxBStages;
+    uint64_t* acc_full = b_empty + kMaxBStages;  // [kAccStages]
     uint64_t* acc_empty = acc_full + kAccStages;
     uint64_t* drain = acc_empty + kAccStages;
     uint64_t* merge_full = drain + 1;        // [q * 2 + row-tile parity] two depositing warps -> merging warp
@@ -387,13 +388,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* x_full = sfb_full + 1;         // [8] 16 FP32 rows of a quantizer warp gathered (fused quantize)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
-    volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [2] per A stage
-    float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 4;             // [kThreads / 32]
-    // [2] per A stage: the point tile's centroid-tile mask, published with sweep0
-    volatile unsigned long long* sweep_mask =
-        reinterpret_cast<volatile unsigned long long*>(bars + kNumBars) + (4 + kThreads / 32 + 1) / 2;
-    static_assert(4 + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 8 <= kNumBars, "barrier slots");
-    static_assert(4 + kThreads / 32 + 1 + 4 <= 32, "words after the barriers");
+    // after the barriers (32 words): [0] TMEM slot, [1] abort flag, [2, 6) sweep
+    // starts per A stage, [6, 6 + 16) per-warp centroid-norm maxima, [24, 32) the
+    // point tile's centroid-tile mask per A stage (64-bit, published with sweep0)
+    volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [kMaxAStages]
+    float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 2 + kMaxAStages;  // [kThreads / 32]
+    volatile unsigned long long* sweep_mask = reinterpret_cast<volatile unsigned long long*>(bars + kNumBars) + 12;
+    static_assert(2 * kMaxAStages + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 8 <= kNumBars,
+                  "barrier slots");
+    static_assert(2 + kMaxAStages + kThreads / 32 <= 24 && 24 + 2 * kMaxAStages <= 32, "words after the barriers");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mrows = p.m_dev ? (int64_t)*p.m_dev : p.m;
@@ -402,7 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         // fused quantize: the two quantizer warps arrive
-        for (int i = 0; i < 2; ++i) dev::mbar_init(&a_full[i], p.fuse_x ? 2 : 1), dev::mbar_init(&a_empty[i], 1);
+        for (int i = 0; i < kMaxAStages; ++i)
+            dev::mbar_init(&a_full[i], p.fuse_x ? 2 : 1), dev::mbar_init(&a_empty[i], 1);
         for (int i = 0; i < kBStages; ++i) dev::mbar_init(&b_full[i], 1), dev::mbar_init(&b_empty[i], 1);
         for (int i = 0; i < kAccStages; ++i)
             dev::mbar_init(&acc_full[i], 1), dev::mbar_init(&acc_empty[i], kEpiWarps);
@@ -575,8 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int slot = 0;
                 uint32_t bph = 0;
                 for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
-                    const int as = p.a_stages == 2 ? (it & 1) : 0;
-                    const uint32_t aph = (uint32_t)(p.a_stages == 2 ? (it >> 1) : it) & 1u;
+                    const int as = it % p.a_stages;
+                    const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
                     if (!dev::mbar_wait_lean(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
                     dev::tc_fence_after();
                     const uint32_t a_off = L.a_off + (uint32_t)as * kATileBytes;
@@ -612,8 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             for (int64_t tile = blockIdx.x; tile < tiles_m && ok && !fast; tile += gridDim.x, ++it) {
-                const int as = p.a_stages == 2 ? (it & 1) : 0;
-                const uint32_t aph = (uint32_t)(p.a_stages == 2 ? (it >> 1) : it) & 1u;
+                const int as = it % p.a_stages;
+                const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
                 if (!dev::mbar_wait_lean(&a_full[as], aph, abort_flag, p.err)) { ok = false; break; }
                 dev::tc_fence_after();
                 const uint32_t a_base = dev::smem_addr(smem + L.a_off + (uint32_t)as * p.kchunks * kATileBytes);
@@ -1053,7 +1057,14 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     p.cn_smem = (argmin && n <= kMaxSmemNorms) ? (int)n : 0;
     // (with the fused quantizer's 64 KB staging, two point stages leave room for
     // three ring slots; a single point stage would serialize encoding and MMA)
-    p.a_stages = fits(2, p.cn_smem, 3) ? 2 : 1;
+    // Point-tile stages: up to four when they fit beside four ring slots (the
+    // gathered-A path, whose tiles are short when centroid tiles are pruned),
+    // else two beside three (with the fused quantizer's 64 KB FP32 staging a
+    // single stage would serialize encoding and MMA), else one.
+    p.a_stages = 1;
+    for (int as = kMaxAStages; as >= 2; --as)
+        if (!p.fuse_x && fits(as, p.cn_smem, 4)) { p.a_stages = as; break; }
+    if (p.a_stages == 1 && fits(2, p.cn_smem, 3)) p.a_stages = 2;
     if (!fits(p.a_stages, p.cn_smem, 3)) p.cn_smem = 0;
     if (!fits(p.a_stages, p.cn_smem, 2)) return fail(MXK_ERR_UNSUPPORTED, "gemm_mx: shared memory budget exceeded");
     p.b_stages = 2;

@@ -28,6 +28,11 @@ inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileR
     return (rows + tile_rows - 1) / tile_rows * (d / 128) * ((tile_rows + 127) / 128) * 512;
 }
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
+// Rows of an MXFP8 matrix (d bytes per row, d / 32 row-major scale bytes)
+// gathered in the order pid (null: identity) into contiguous rows, scales in the
+// kPointTileRows atom layout.  stop: the Lloyd loop's stop word (optional).
+int launch_gather_mxfp8_rows(int64_t rows, int d, const uint8_t* src, const uint8_t* src_scales, const int* pid,
+                             uint8_t* dst, uint8_t* dst_scales, const int* stop, cudaStream_t stream);
 int launch_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
                         cudaStream_t stream);
 // lc/ec either as host values (lc_dev == nullptr) or read from device memory.

@@ -153,7 +153,7 @@ struct LoopMirror {
 };
 
 int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
-              const mxk_options* options, int* iterations, cudaStream_t stream) {
+              const mxk_options* options, int* iterations, cudaStream_t stream, bool cache_points = false) {
     MXK_REQUIRE(options && iterations, "kmeans_mixed: null options or iterations");
     MXK_REQUIRE(k > 0 && d > 0 && n >= 0, "kmeans_mixed: require n >= 0, d > 0, k > 0");
     MXK_REQUIRE(d % 128 == 0, "kmeans_mixed: d must be padded to a multiple of 128");
@@ -185,8 +185,18 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     int *order = nullptr, *sort_scratch = nullptr;
     MXK_CHECK(ws.alloc(&order, n));
     MXK_CHECK(ws.alloc(&sort_scratch, label_sort_scratch_ints(k)));
+    // Opt-in point cache: under the forced-MXFP8 policy the points' MXFP8 bytes
+    // never change, so they are quantized once per call and only regathered
+    // when the visiting order changes (the reference re-quantizes every
+    // iteration; the results are the same).
+    const bool cache = cache_points && kForced8;
+    uint8_t *qnat = nullptr, *snat = nullptr;
+    if (cache) {
+        MXK_CHECK(ws.alloc(&qnat, n * d));
+        MXK_CHECK(ws.alloc(&snat, n * d / 32));
+    }
     // (the fused quantize at d = 128 never materializes the MXFP8 point rows)
-    const bool need_qpoints = !kForced8 || d != 128;
+    const bool need_qpoints = !kForced8 || d != 128 || cache;
     if (need_qpoints) {
         MXK_CHECK(ws.alloc(&qpoints, n * d));
         MXK_CHECK(ws.alloc(&pscales, scale_atom_bytes(n, d)));
@@ -242,19 +252,23 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     // Once per run (kmeans.cu:24-27).
     MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
     if (prune) MXK_CHECK(launch_point_quant_stats(n, d, points, pnorm, pinfo, stream));
+    if (cache) MXK_CHECK(launch_quantize(8, n, d, points, nullptr, qnat, snat, nullptr, nullptr, stream, 0));
     if (!kForced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
 
     const bool sharded = comm && comm->nranks > 1;
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+    bool cached_stale = true;  // the gathered copy of the cached rows does not follow the current order
     for (int it = 0; it < options->max_iterations; ++it) {
         // From the second iteration on, visit points grouped by their label of
         // the previous (or, every other iteration, the one before) iteration
         // (order.cu); the first iteration keeps ascending point order.
         const int* ord = nullptr;
         if (it > 0 && n > 0) {
-            if ((it - 1) % kResortEvery == 0)
+            if ((it - 1) % kResortEvery == 0) {
                 MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
+                cached_stale = true;
+            }
             ord = order;
         }
         MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
@@ -287,10 +301,16 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                                       kCentroidTileRows));
             // MXFP8 at d = 128: the GEMM quantizes the point tiles itself from the
             // FP32 rows (same bytes as quantize_rows), so this pass disappears.
-            const bool fused_q = d == 128;
-            if (!fused_q)
+            const bool fused_q = d == 128 && !cache;
+            if (cache) {
+                // regather the cached rows when the visiting order has changed
+                if (cached_stale)
+                    MXK_CHECK(launch_gather_mxfp8_rows(n, d, qnat, snat, ord, qpoints, pscales, loop, stream));
+                cached_stale = false;
+            } else if (!fused_q) {
                 MXK_CHECK(launch_quantize(8, n, d, points, ord, qpoints, pscales, nullptr, loop + 3, stream,
                                           kPointTileRows));
+            }
             MxArgmin am;
             am.point_norms = pnorm;
             am.centroid_norms = cnorm;
@@ -381,6 +401,12 @@ extern "C" {
 int mxk_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
                      const mxk_options* options, int* iterations, void* stream) {
     return mxk::run_lloyd(nullptr, n, d, k, points, centroids, labels, options, iterations, mxk::as_stream(stream));
+}
+
+int mxk_kmeans_mixed_cached(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                            const mxk_options* options, int* iterations, void* stream) {
+    return mxk::run_lloyd(nullptr, n, d, k, points, centroids, labels, options, iterations, mxk::as_stream(stream),
+                          true);
 }
 
 int mxk_comm_unique_id(unsigned char id[128]) {

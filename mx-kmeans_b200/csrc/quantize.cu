@@ -5,6 +5,8 @@
 // point_bounds_kernel :74-98, precision_kernel :100-108, launchers :111-134),
 // src/kernels/assignment.cu:7-16 (norms) and src/kmeans.cu:36-52 (centroid
 // statistics and group compaction).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mx_codec.cuh"
@@ -456,6 +458,44 @@ int launch_group_compaction(int64_t n, const int* precision, const int* order, i
         group_scatter_kernel<<<(unsigned)nb, 256, 0, stream>>>(n, precision, order, scratch, (int)nb, ids, stop);
         MXK_CUDA(cudaGetLastError());
     }
+    return MXK_OK;
+}
+
+// Rows of an MXFP8 matrix (packed values, row-major scales) copied in the order
+// pid into contiguous rows, with the scales rewritten in the atom layout of
+// kPointTileRows-row tiles (what the GEMM bulk-copies).  One thread per 16
+// bytes of values; the first d / 128 threads of a row also move its scale words.
+__global__ void __launch_bounds__(256) gather_mxfp8_rows_kernel(int64_t rows, int d, const uint8_t* __restrict__ src,
+                                                                const uint8_t* __restrict__ src_scales,
+                                                                const int* __restrict__ pid,
+                                                                uint8_t* __restrict__ dst,
+                                                                uint8_t* __restrict__ dst_scales,
+                                                                const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    const int pieces = d >> 4;
+    const int64_t total = rows * pieces;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = g / pieces;
+        const int piece = (int)(g - row * pieces);
+        const int64_t from = pid ? (int64_t)pid[row] : row;
+        reinterpret_cast<uint4*>(dst + row * d)[piece] = reinterpret_cast<const uint4*>(src + from * d)[piece];
+        if (piece < (d >> 7)) {  // the four block scales of 128-feature chunk `piece`
+            const uint32_t w = reinterpret_cast<const uint32_t*>(src_scales + from * (d >> 5))[piece];
+            *reinterpret_cast<uint32_t*>(dst_scales + scale_atom_offset(row, 4 * piece, d >> 7, kPointTileRows)) = w;
+        }
+    }
+}
+
+int launch_gather_mxfp8_rows(int64_t rows, int d, const uint8_t* src, const uint8_t* src_scales, const int* pid,
+                             uint8_t* dst, uint8_t* dst_scales, const int* stop, cudaStream_t stream) {
+    if (rows <= 0) return MXK_OK;
+    MXK_REQUIRE(d % 128 == 0, "gather_mxfp8_rows: d must be a multiple of 128");
+    const int64_t total = rows * (d >> 4);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 32);
+    LaunchScope scope("gather_mxfp8_rows", stream);
+    gather_mxfp8_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, d, src, src_scales, pid, dst, dst_scales,
+                                                                   stop);
+    MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
 

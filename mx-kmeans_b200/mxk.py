@@ -64,6 +64,7 @@ SIGNATURES = {
     "mxk_assign_mx_fused": ([_I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_assign_f32_fused": ([_I64, _I, _I, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_kmeans_mixed": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
+    "mxk_kmeans_mixed_cached": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_comm_unique_id": ([ctypes.c_char_p], _I),
     "mxk_comm_init": ([ctypes.POINTER(_P), _I, _I, ctypes.c_char_p], _I),
     "mxk_comm_destroy": ([_P], _I),
@@ -204,13 +205,15 @@ def centroid_shift(previous, current, device_sum, stream=None):
     return out.value
 
 
-def kmeans_mixed(points, centroids, labels, options=None, stream=None):
-    """Run the Lloyd loop in place on device tensors; returns the iteration count."""
+def kmeans_mixed(points, centroids, labels, options=None, stream=None, cache_points=False):
+    """Run the Lloyd loop in place on device tensors; returns the iteration count.
+    cache_points: quantize the points once per call instead of every iteration
+    (mxk_kmeans_mixed_cached; same results, reported separately)."""
     opts = options or Options()
     iters = ctypes.c_int(0)
-    check(load().mxk_kmeans_mixed(points.shape[0], points.shape[1], centroids.shape[0], _ptr(points),
-                                  _ptr(centroids), _ptr(labels), ctypes.byref(opts), ctypes.byref(iters),
-                                  _stream(stream)))
+    fn = load().mxk_kmeans_mixed_cached if cache_points else load().mxk_kmeans_mixed
+    check(fn(points.shape[0], points.shape[1], centroids.shape[0], _ptr(points), _ptr(centroids), _ptr(labels),
+             ctypes.byref(opts), ctypes.byref(iters), _stream(stream)))
     return iters.value
 
 

@@ -247,3 +247,25 @@ def test_pruned_assignment_equals_unpruned(torch_cuda, mxk, n, blobs_k, spread, 
         mxk.assign_f32_fused(n, k, d, xt, qc, sc, pn, cn, lab_u)
         torch.cuda.synchronize()
         assert torch.equal(lab_t, lab_u), f"iteration {t}: {(lab_t != lab_u).sum().item()} labels differ"
+
+
+@pytest.mark.parametrize("n,d,k", [(56909, 128, 2048), (20000, 256, 300)])
+def test_cached_points_equal_default(torch_cuda, mxk, n, d, k):
+    """mxk_kmeans_mixed_cached (points quantized once, regathered when the
+    visiting order changes) gives the default path's labels, centroids and
+    iteration count; integer data keeps both runs deterministic."""
+    torch = torch_cuda
+    x = np.rint(blobs(n, d - 32, 200, seed=41, spread=10.0, sigma=1.5, pad_to=d) * 2).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    c0 = torch.empty((k, d), device="cuda")
+    mxk.init_kmeanspp(xt, c0, 11)
+    out = []
+    for cached in (False, True):
+        ct = c0.clone()
+        lab = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        it = mxk.kmeans_mixed(xt, ct, lab, mxk.Options(max_iterations=7, tolerance=0.0), cache_points=cached)
+        torch.cuda.synchronize()
+        out.append((it, ct.cpu().numpy(), lab.cpu().numpy()))
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][2], out[1][2])
+    assert np.array_equal(out[0][1], out[1][1])
