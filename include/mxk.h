@@ -50,6 +50,10 @@ uint64_t mxk_launch_count(void);
  * this returns the current device's pooled memory to the driver (synchronizes
  * the device). */
 int mxk_release_workspace(void);
+/* Measurement aid, no reference counterpart: the number of 128 x 192 tiles the
+ * current device's MX GEMM launches have multiplied since the last reset
+ * (synchronizes the device); pruned tiles are not counted. */
+int mxk_gemm_tiles_multiplied(unsigned long long* count, int reset);
 
 /* ---- ops (include/kmeans.cuh:23-47) ------------------------------------ */
 

@@ -52,6 +52,9 @@ struct LaunchScope {
 // Device-wide error word: kernels with bounded waits set it on timeout.
 int check_device_error(cudaStream_t stream);
 unsigned* device_error_word();
+// Per-device count of 128 x 192 tiles the MX GEMM has multiplied (all K chunks),
+// for reporting the tensor work actually executed when tiles are pruned.
+unsigned long long* device_tile_counter();
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved through the runtime,
 // so the library has no link-time dependency on libcuda).

@@ -116,6 +116,7 @@ struct GemmParams {
     // its rows' nearest centroids (bit t = tile t; the others are neither loaded,
     // multiplied nor scanned).  Every bit set when null.  Needs tiles_n <= 64.
     const uint64_t* tile_mask;
+    unsigned long long* tiles_done;  // count of multiplied 128 x 192 tiles (all K chunks)
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
     int best_dist_stride;  // best_dist[point * best_dist_stride]
     unsigned* err;
@@ -555,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // detected with a non-suspending test first.
         if (lane == 0) {
             RingPos brd{0, 0u, kBStages};
+            uint32_t tiles_issued = 0;
             int s = 0;           // accumulator stage of tile a = a % 2
             uint32_t sph = 0;    // (a / 2) & 1
             int it = 0;
@@ -606,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             dev::tc_mma_mx(d, adesc + 2u * kb, bdesc + 2u * kb, idesc0 | dev::mx_idesc_sf((uint32_t)kb),
                                            sfa | ((uint32_t)kb << 30), sfb | ((uint32_t)kb << 30), kb != 0);
                         dev::tc_commit(&acc_full[s]);
+                        ++tiles_issued;
                         s ^= 1;
                         sph ^= (uint32_t)(s == 0);
                         if (++slot == kBStages) slot = 0, bph ^= 1u;
@@ -658,11 +661,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (!ok) break;
                     dev::tc_commit(&acc_full[s]);
+                    ++tiles_issued;
                     if (++s == kAccStages) s = 0, sph ^= 1u;
                 }
                 if (ok) dev::tc_commit(&a_empty[as]);
             }
             // Make sure every issued MMA/copy has finished before TMEM is freed.
+            if (p.tiles_done && ok) atomicAdd(p.tiles_done, (unsigned long long)tiles_issued);
             dev::tc_commit(drain);
             volatile int no_abort = 0;
             dev::mbar_wait(drain, 0, &no_abort, p.err);
@@ -1040,6 +1045,7 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         MXK_REQUIRE(!p.tile_mask || (n + kBN - 1) / kBN <= 64, "gemm_mx: a tile mask covers at most 64 centroid tiles");
     }
     p.err = device_error_word();
+    p.tiles_done = device_tile_counter();
     if (!p.err) return fail(MXK_ERR_CUDA, "gemm_mx: cannot allocate the device error word");
 
     int max_smem = 0, dev = 0;

@@ -100,6 +100,20 @@ unsigned* device_error_word() {
     return g_error_words[dev];
 }
 
+unsigned long long* device_tile_counter() {
+    static unsigned long long* counters[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!counters[dev]) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+        counters[dev] = static_cast<unsigned long long*>(p);
+    }
+    return counters[dev];
+}
+
 int check_device_error(cudaStream_t stream) {
     unsigned* w = device_error_word();
     if (!w) return fail(MXK_ERR_CUDA, "cannot allocate the device error word");
@@ -185,6 +199,15 @@ const char* mxk_last_error(void) { return mxk::g_last_error.c_str(); }
 int mxk_version(void) { return 100; }
 
 uint64_t mxk_launch_count(void) { return mxk::g_launches.load(); }
+
+int mxk_gemm_tiles_multiplied(unsigned long long* count, int reset) {
+    unsigned long long* c = mxk::device_tile_counter();
+    if (!c) return mxk::fail(MXK_ERR_CUDA, "gemm_tiles_multiplied: no counter on the current device");
+    MXK_CUDA(cudaDeviceSynchronize());
+    MXK_CUDA(cudaMemcpy(count, c, sizeof(*count), cudaMemcpyDeviceToHost));
+    if (reset) MXK_CUDA(cudaMemset(c, 0, sizeof(*c)));
+    return MXK_OK;
+}
 
 int mxk_release_workspace(void) {
     cudaMemPool_t pool = mxk::workspace_pool();

@@ -53,6 +53,7 @@ SIGNATURES = {
     "mxk_assign_precisions": ([_I64, _I, _P, _P, _F, _F, _P, _P], _I),
     "mxk_check_mxfp8_scale_codec": ([_P, _P], _I),
     "mxk_release_workspace": ([], _I),
+    "mxk_gemm_tiles_multiplied": ([ctypes.POINTER(ctypes.c_ulonglong), _I], _I),
     "mxk_init_farthest": ([_I64, _I, _I, _P, _P, _P], _I),
     "mxk_init_kmeanspp": ([_I64, _I, _I, _P, _P, ctypes.c_uint32, _P], _I),
     "mxk_gemm_mx": ([_I, _I64, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
@@ -150,6 +151,14 @@ def init_kmeanspp(points, centroids, seed, stream=None):
     n, d = points.shape
     check(load().mxk_init_kmeanspp(n, d, centroids.shape[0], _ptr(points), _ptr(centroids), seed & 0xffffffff,
                                    _stream(stream)))
+
+
+def gemm_tiles_multiplied(reset=False):
+    """128 x 192 tiles multiplied by the MX GEMM on the current device since the
+    last reset (pruned tiles excluded)."""
+    v = ctypes.c_ulonglong(0)
+    check(load().mxk_gemm_tiles_multiplied(ctypes.byref(v), 1 if reset else 0))
+    return v.value
 
 
 def release_workspace():
