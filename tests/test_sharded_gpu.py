@@ -45,11 +45,13 @@ def _run(rank, world, port, n, d, k, seed, iters):
     return out
 
 
-def test_two_gpu_sharded_matches_single_gpu():
+# the second case has four centroid tiles, so from the second iteration on each
+# rank prunes tiles from its own rows' bounds
+@pytest.mark.parametrize("n,d,k,seed,iters", [(20011, 128, 40, 9, 8), (60013, 128, 700, 3, 10)])
+def test_two_gpu_sharded_matches_single_gpu(n, d, k, seed, iters):
     import torch
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    n, d, k, seed, iters = 20011, 128, 40, 9, 8
     out = _spawn(_run, 2, n, d, k, seed, iters)
     labels = np.concatenate([out[r]["labels"] for r in sorted(out, key=lambda r: out[r]["first"])])
     single_labels, single_cent, single_iters = out[0]["single"]
