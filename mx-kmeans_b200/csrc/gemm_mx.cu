@@ -79,7 +79,7 @@ constexpr uint32_t kSfaCol = kAccStages * kBN;  // 384: 4 columns per K chunk (<
 constexpr uint32_t kSfbCol = kSfaCol + 32;       // 416: centroid scales, 4 columns per atom
 constexpr int kSfbChunkCols = 4 * kBAtoms;       // TMEM columns per (centroid tile, K chunk)
 constexpr int kMaxResidentSfb = (512 - (int)kSfbCol) / kSfbChunkCols;  // 12 (tile, chunk) pairs
-constexpr int kNumBars = 72;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
+constexpr int kNumBars = 80;             // mbarrier slots (see the kernel's carve-up); TMEM slot after them
 static_assert(kSliceCols % 32 == 0 && kBN % kEpiPerQuad == 0, "each epilogue warp drains whole 32-column chunks");
 static_assert(kSfbCol + kSfbChunkCols <= kTmemCols, "TMEM budget");
 
@@ -387,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* seed_bar = merge_empty + 8;    // [q] the quadrant's three first-tile minima are published
     uint64_t* sfb_full = seed_bar + 4;       // resident centroid scales have landed in shared memory
     uint64_t* x_full = sfb_full + 1;         // [8] 16 FP32 rows of a quantizer warp gathered (fused quantize)
+    uint64_t* x_empty = x_full + 8;          // [8] the quantizer warp has encoded those rows
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars) + 1;
     // after the barriers (32 words): [0] TMEM slot, [1] abort flag, [2, 6) sweep
@@ -395,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* sweep0 = reinterpret_cast<volatile int*>(bars + kNumBars) + 2;  // [kMaxAStages]
     float* warp_cmax = reinterpret_cast<float*>(bars + kNumBars) + 2 + kMaxAStages;  // [kThreads / 32]
     volatile unsigned long long* sweep_mask = reinterpret_cast<volatile unsigned long long*>(bars + kNumBars) + 12;
-    static_assert(2 * kMaxAStages + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 8 <= kNumBars,
+    static_assert(2 * kMaxAStages + 2 * kMaxBStages + 2 * kAccStages + 1 + 16 + 4 + 1 + 16 <= kNumBars,
                   "barrier slots");
     static_assert(2 + kMaxAStages + kThreads / 32 <= 24 && 24 + 2 * kMaxAStages <= 32, "words after the barriers");
 
@@ -418,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int q = 0; q < 4; ++q) dev::mbar_init(&seed_bar[q], kEpiPerQuad);
         dev::mbar_init(sfb_full, 1);
-        for (int i = 0; i < 8; ++i) dev::mbar_init(&x_full[i], 1);
+        for (int i = 0; i < 8; ++i) dev::mbar_init(&x_full[i], 1), dev::mbar_init(&x_empty[i], 1);
         *abort_flag = 0;
         dev::fence_barrier_init();
     }
@@ -472,10 +473,132 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto mask_of = [&](int64_t t) -> uint64_t {  // (lane 0 only) centroid tiles of point tile t
             return p.tile_mask && t < tiles_m && lane == 0 ? p.tile_mask[t] : ~0ull;
         };
+        uint32_t xf_issued = 0;  // (fused quantize) bit G: staging group G has been gathered
+        uint32_t xf_par = 0;     // bit G: number of gathers into group G, mod 2
+        if (p.fuse_x) {
+            // Fused quantize: this warp also refills the quantizers' FP32 staging.
+            // Two streams are served as their barriers allow: centroid tiles into
+            // the B ring, and the next row tile's point rows into each 16-row
+            // staging group a quantizer warp has released (x_empty), in the order
+            // the two warps consume them (0, 4, 1, 5, ...).  The rows' point ids
+            // are loaded one group ahead, the centroid-tile masks and sweep starts
+            // one and two row tiles ahead, so neither stream waits on a global load.
+            constexpr uint32_t kGroupBytes = 16u * kChunk * 4u;
+            auto group_of = [](int k) { return (k & 1) * 4 + (k >> 1); };
+            int64_t gt = blockIdx.x;  // row tile being gathered
+            int gk = 0;               // position of the next group in the consumption order
+            uint32_t xe_par = 0xffu;  // bit G: parity awaited on x_empty[G] (a fresh barrier passes 1)
+            int32_t y[4] = {0, 0, 0, 0};
+            auto load_ids = [&](int64_t t, int G) {
+                if (lane < 4) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int64_t g = t * kBM + 16 * G + 4 * lane + u;
+                        y[u] = g < mrows ? (p.pid ? p.pid[g] : (int32_t)g) : (int32_t)p.xrows;  // past the end: zeros
+                    }
+                }
+            };
+            bool g_more = gt < tiles_m;
+            if (g_more) load_ids(gt, group_of(0));
+            // centroid stream (lane 0): row tile bt, sweep position bi
+            int64_t bt = blockIdx.x;
+            int bi = 0;
+            auto ct0_of = [&](int h) { return h >= 0 && (int64_t)h < p.n ? h / kBN : 0; };
+            int ct0 = ct0_of(hint_of(lead_id(bt)));
+            uint64_t bmask = mask_of(bt);
+            int hint_nxt = hint_of(lead_id(bt + step));
+            uint64_t mask_nxt = mask_of(bt + step);
+            int64_t lead_nn = lead_id(bt + 2 * step);
+            auto next_b = [&]() -> bool {  // (lane 0) advance to the next centroid tile to load
+                while (bt < tiles_m) {
+                    for (; bi < tiles_n; ++bi) {
+                        const int ct = ct0 + bi < tiles_n ? ct0 + bi : ct0 + bi - tiles_n;
+                        if ((bmask >> ct) & 1ull) return true;
+                    }
+                    bt += step;
+                    bi = 0;
+                    ct0 = ct0_of(hint_nxt);
+                    bmask = mask_nxt;
+                    hint_nxt = hint_of(lead_nn);
+                    mask_nxt = mask_of(bt + step);
+                    lead_nn = lead_id(bt + 2 * step);
+                }
+                return false;
+            };
+            bool b_more = __shfl_sync(0xffffffffu, lane == 0 ? (int)next_b() : 0, 0) != 0;
+            long long idle_since = clock64();
+            while (g_more || b_more) {
+                bool progressed = false;
+                if (g_more) {
+                    const int G = group_of(gk);
+                    const int ready = __shfl_sync(
+                        0xffffffffu, lane == 0 ? (int)dev::mbar_test(&x_empty[G], (xe_par >> G) & 1u) : 0, 0);
+                    if (ready) {
+                        xe_par ^= 1u << G;
+                        if (lane == 0) dev::mbar_arrive_expect_tx(&x_full[G], kGroupBytes);
+                        __syncwarp();
+                        if (lane < 4)  // staging rows 16 G + 4 lane .. + 3: inside the 64 KB buffer
+                            dev::tma_gather4(smem + L.x_off + (uint32_t)(16 * G + 4 * lane) * kChunk * 4u, &tmap_x, 0,
+                                             y[0], y[1], y[2], y[3], &x_full[G]);
+                        xf_issued |= 1u << G;
+                        xf_par ^= 1u << G;
+                        if (++gk == 8) gk = 0, gt += step;
+                        g_more = gt < tiles_m;
+                        if (g_more) load_ids(gt, group_of(gk));
+                        progressed = true;
+                    }
+                }
+                if (b_more) {
+                    const int ready = __shfl_sync(
+                        0xffffffffu, lane == 0 ? (int)dev::mbar_test(&b_empty[bring.slot], bring.phase ^ 1u) : 0, 0);
+                    if (ready) {
+                        int more = 0;
+                        if (lane == 0) {
+                            const int ct = ct0 + bi < tiles_n ? ct0 + bi : ct0 + bi - tiles_n;
+                            uint64_t* full = &b_full[bring.slot];
+                            dev::mbar_arrive_expect_tx(
+                                full, (uint32_t)(kBTileBytes + (p.sfb_resident ? 0 : kBAtoms * kSfAtom)));
+                            dev::tma_load_2d(smem + L.b_off + bring.slot * kBTileBytes, &tmap_b, 0, ct * kBN, full);
+                            if (!p.sfb_resident)
+                                dev::bulk_load(smem + L.sfb_off + bring.slot * kBAtoms * kSfAtom,
+                                               p.b_scales + (int64_t)ct * kBAtoms * kSfAtom, kBAtoms * kSfAtom, full);
+                            ++issued;
+                            bring.advance(1);
+                            ++bi;
+                            more = next_b();
+                        }
+                        b_more = __shfl_sync(0xffffffffu, more, 0) != 0;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    idle_since = clock64();
+                } else {
+                    // nothing to issue: back off briefly (this warp shares its
+                    // scheduler with epilogue warps), give up on an abort or a
+                    // wait past the limit
+                    int quit = 0;
+                    if (lane == 0) {
+                        if (*abort_flag) {
+                            quit = 1;
+                        } else if (clock64() - idle_since > dev::kWaitLimitCycles) {
+                            *abort_flag = 1;
+                            if (p.err) atomicOr(p.err, 1u << MXK_ERR_TIMEOUT);
+                            quit = 1;
+                        }
+                    }
+                    if (__shfl_sync(0xffffffffu, quit, 0)) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(20);
+                }
+            }
+        }
         int hint_cur = hint_of(lead_id(blockIdx.x));
         int64_t lead_nxt = lead_id(blockIdx.x + step);
         uint64_t mask_nxt = mask_of(blockIdx.x);
-        for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
+        for (int64_t tile = blockIdx.x; tile < tiles_m && ok && !p.fuse_x; tile += gridDim.x, ++it) {
             const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
             const uint64_t tmask = mask_nxt;
             hint_cur = hint_of(lead_nxt);
@@ -483,12 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mask_nxt = mask_of(tile + step);
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
-            // (fused quantize: the quantizer warps own the point tile and its sweep start)
-            if (!p.fuse_x && !dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+            if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             uint8_t* a_smem = smem + L.a_off + (uint32_t)as * p.kchunks * kATileBytes;
             uint8_t* sfa = smem + L.sfa_off + (uint32_t)as * p.kchunks * kSfAtom;
-            if (p.fuse_x) {
-            } else if (lane == 0) {
+            if (lane == 0) {
                 const uint32_t bytes = (p.a_bits == 8 ? p.kchunks * kATileBytes : 0) + p.kchunks * kSfAtom;
                 if (bytes)
                     asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(dev::smem_addr(&a_full[as])),
@@ -500,15 +621,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dev::bulk_load(sfa, p.a_scales + tile * p.kchunks * kSfAtom, (uint32_t)(p.kchunks * kSfAtom),
                                &a_full[as]);
             }
-            if (p.a_bits != 8 && !p.fuse_x)
+            if (p.a_bits != 8)
                 for (int kc = 0; kc < p.kchunks; ++kc)
                     fill_a_subbyte(a_smem + kc * kATileBytes, p, tile * kBM, kc, mrows, lane);
-            if (!p.fuse_x) {
-                if (lane == 0) sweep0[as] = ct0, sweep_mask[as] = tmask;  // published by the a_full arrival
-                dev::fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) dev::mbar_arrive(&a_full[as]);
-            }
+            if (lane == 0) sweep0[as] = ct0, sweep_mask[as] = tmask;  // published by the a_full arrival
+            dev::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) dev::mbar_arrive(&a_full[as]);
             // Centroid chunks: one thread walks the ring.  A slot is handed back by
             // the epilogue once the tile that read it has completed, or by the MMA
             // thread's per-chunk commit when the ring holds less than two tiles.
@@ -543,8 +662,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             volatile int no_abort = 0;
             for (uint32_t c = issued > (uint32_t)kBStages ? issued - kBStages : 0; c < issued; ++c)
                 dev::mbar_wait(&b_full[c % kBStages], (c / kBStages) & 1u, &no_abort, nullptr);
-            for (int j = it > p.a_stages ? it - p.a_stages : 0; j <= it; ++j)
-                dev::mbar_wait(&a_full[j % p.a_stages], (uint32_t)(j / p.a_stages) & 1u, &no_abort, nullptr);
+            if (p.fuse_x) {
+                for (int G = 0; G < 8; ++G)
+                    if ((xf_issued >> G) & 1u)
+                        dev::mbar_wait(&x_full[G], ((xf_par >> G) & 1u) ^ 1u, &no_abort, nullptr);
+            } else {
+                for (int j = it > p.a_stages ? it - p.a_stages : 0; j <= it; ++j)
+                    dev::mbar_wait(&a_full[j % p.a_stages], (uint32_t)(j / p.a_stages) & 1u, &no_abort, nullptr);
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -685,9 +810,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // shuffle.  The staging rows are 512 B apart; lane L reads its eight
         // 16-byte chunks starting at chunk (L & 7), so the 8 lanes of each
         // shared-memory phase hit 8 different bank groups.
-        // The warp's 64 staging rows form 4 groups of 16 with one barrier each;
-        // as soon as a group is encoded, its rows of the next tile are gathered
-        // (lanes 0-3, four rows each), so the copies overlap the encoding.
+        // The warp's 64 staging rows form 4 groups of 16 with two barriers each:
+        // the producer warp gathers a group's rows (x_full) and refills it with
+        // the next row tile's as soon as this warp has encoded it (x_empty), so
+        // the copies overlap the encoding.
         constexpr int kRowsPerWarp = kBM / 2;  // 64
         constexpr int kGroupRows = 16;
         constexpr int kGroups = kRowsPerWarp / kGroupRows;  // 4
@@ -695,56 +821,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                       "quantizer row split");
         const int r0 = (warp - 2) * kRowsPerWarp;
         uint64_t* xf = x_full + (warp - 2) * kGroups;
-        uint32_t outstanding = 0;  // bit G: a gather into group G is in flight
-        uint32_t xphase = 0;       // bit G: parity of group G's next completion
-        auto gather = [&](int64_t t, int grp) {
-            const int gr = r0 + grp * kGroupRows;  // first staging row of the group
-            if (lane == 0) dev::mbar_arrive_expect_tx(&xf[grp], (uint32_t)(kGroupRows * kChunk * 4));
-            __syncwarp();
-            if (lane < kGroupRows / 4) {
-                int32_t y[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int64_t g = t * kBM + gr + 4 * lane + u;  // < t * kBM + kBM
-                    y[u] = g < mrows ? (p.pid ? p.pid[g] : (int32_t)g) : (int32_t)p.xrows;  // past the end: zeros
-                }
-                // staging rows gr + 4 lane .. + 3 <= 127: inside the 64 KB buffer
-                uint8_t* dst = smem + L.x_off + (uint32_t)(gr + 4 * lane) * kChunk * 4u;
-                dev::tma_gather4(dst, &tmap_x, 0, y[0], y[1], y[2], y[3], &xf[grp]);
-            }
-            outstanding |= 1u << grp;
-        };
-        // sweep starts (warp 2 publishes them), pipelined like the producer's
+        uint64_t* xe = x_empty + (warp - 2) * kGroups;
+        uint32_t xphase = 0;  // bit G: parity of group G's next completion
+        // sweep starts and centroid-tile masks (warp 2 publishes them), pipelined
+        // like the producer's
         const int64_t step = gridDim.x;
+        const bool lead_lane = lane == 0 && warp == 2;
         auto lead_id = [&](int64_t t) -> int64_t {
-            if (!p.start_hint || t >= tiles_m || lane != 0 || warp != 2) return -1;
+            if (!p.start_hint || t >= tiles_m || !lead_lane) return -1;
             return p.pid ? (int64_t)p.pid[t * kBM] : t * kBM;
         };
         auto hint_of = [&](int64_t id) -> int { return id >= 0 ? p.start_hint[id] : -1; };
+        auto mask_of = [&](int64_t t) -> uint64_t {
+            return p.tile_mask && t < tiles_m && lead_lane ? p.tile_mask[t] : ~0ull;
+        };
         int hint_cur = hint_of(lead_id(blockIdx.x));
         int64_t lead_nxt = lead_id(blockIdx.x + step);
+        uint64_t mask_cur = mask_of(blockIdx.x);
         bool ok = true;
         int it = 0;
-        if (blockIdx.x < tiles_m)
-            for (int grp = 0; grp < kGroups; ++grp) gather(blockIdx.x, grp);
         const int blk = lane >> 3;      // 32-feature block of this lane
         const uint32_t rot = lane & 7;  // first chunk read (row % 8 of this lane's rows)
         const uint32_t xbase = dev::smem_addr(smem + L.x_off) + (uint32_t)(r0 + (lane & 7)) * (kChunk * 4) +
                                (uint32_t)blk * 128u;
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int ct0 = hint_cur >= 0 && (int64_t)hint_cur < p.n ? hint_cur / kBN : 0;
+            const uint64_t tmask = mask_cur;
             hint_cur = hint_of(lead_nxt);
             lead_nxt = lead_id(tile + 2 * step);
+            mask_cur = mask_of(tile + step);
             const int as = it % p.a_stages;
             const uint32_t aph = (uint32_t)(it / p.a_stages) & 1u;
             if (!dev::mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             const uint32_t a_tile = dev::smem_addr(smem + L.a_off + (uint32_t)as * kATileBytes);
             const uint32_t sfa = dev::smem_addr(smem + L.sfa_off + (uint32_t)as * kSfAtom);
-            const bool refill = tile + gridDim.x < tiles_m;
             for (int grp = 0; grp < kGroups && ok; ++grp) {
                 if (!dev::mbar_wait(&xf[grp], (xphase >> grp) & 1u, abort_flag, p.err)) { ok = false; break; }
                 xphase ^= 1u << grp;
-                outstanding &= ~(1u << grp);
 #pragma unroll 1
                 for (int pass = 0; pass < kGroupRows / 8; ++pass) {
                     const int rbase = r0 + grp * kGroupRows + pass * 8;  // multiple of 8
@@ -778,24 +891,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     dev::sts_u8(sfa + ((r & 31) << 4) + ((r >> 5) << 2) + blk, sc);
                 }
-                // the group's staging rows are consumed: fetch the next tile's
+                // the group's staging rows are consumed: the producer refills them
                 __syncwarp();
-                if (refill) gather(tile + gridDim.x, grp);
+                if (lane == 0) dev::mbar_arrive(&xe[grp]);
             }
             if (!ok) break;
             dev::fence_proxy_async();  // generic shared-memory writes -> visible to the tensor core
             __syncwarp();
-            if (warp == 2 && lane == 0) {  // published to the MMA thread by the a_full arrival
+            if (lead_lane) {  // published to the MMA thread by the a_full arrival
                 sweep0[as] = ct0;
-                sweep_mask[as] = p.tile_mask ? p.tile_mask[tile] : ~0ull;
+                sweep_mask[as] = tmask;
             }
             if (lane == 0) dev::mbar_arrive(&a_full[as]);
-        }
-        // Unwinding after an abort: wait (bounded) for this warp's gathers in flight.
-        if (!ok && lane == 0) {
-            volatile int no_abort = 0;
-            for (int grp = 0; grp < kGroups; ++grp)
-                if ((outstanding >> grp) & 1u) dev::mbar_wait(&xf[grp], (xphase >> grp) & 1u, &no_abort, nullptr);
         }
     }
     } else {
