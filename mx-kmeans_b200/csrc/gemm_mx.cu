@@ -119,6 +119,7 @@ struct GemmParams {
     unsigned long long* tiles_done;  // count of multiplied 128 x 192 tiles (all K chunks)
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
     int best_dist_stride;  // best_dist[point * best_dist_stride]
+    const float2* row_bound;  // optional (argmin): MxArgmin::row_bound
     unsigned* err;
 };
 
@@ -242,6 +243,10 @@ struct NormSrc {
     }
 };
 
+// Label of a row minimum that holds no centroid yet (its distance may be a
+// bound rather than a candidate's).
+constexpr int kNoLabel = 0x7fffffff;
+
 // Running (distance, index) minimum and two largest distances of one row.
 struct RowMin {
     float first, largest, next;
@@ -254,9 +259,11 @@ struct RowMin {
 // search only when the chunk minimum can change the running minimum (smaller,
 // or equal, resolved by the lower index as insert_distance does).  NaN
 // distances never compare, as in the reference.
+// force: evaluate the chunk even when its minimum exceeds m.first, taking it if
+// m holds no centroid yet (m.first is then only a bound).
 template <bool kGaps, class Norms>
 __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, int c0,
-                                               RowMin& m) {
+                                               RowMin& m, bool force = false) {
     float dist[32];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -279,12 +286,12 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const No
     const float mb = dev::min3f(m3[3], m3[4], m3[5]);
     const float mc = dev::min3f(m3[6], m3[7], m3[8]);
     const float cm = fminf(dev::min3f(ma, mb, mc), fminf(m3[9], m3[10]));
-    if (cm <= m.first) {
+    if (cm <= m.first || (force && cm == cm)) {
         int idx = 31;
 #pragma unroll
         for (int j = 30; j >= 0; --j) idx = dist[j] == cm ? j : idx;
         const int cand = c0 + idx;
-        if (cm < m.first || cand < m.best) {
+        if (cm < m.first || (cm == m.first && cand < m.best) || m.best == kNoLabel) {
             m.first = cm;
             m.best = cand;
         }
@@ -302,7 +309,7 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const No
 // and take the exact path.  pc = pn + max(cn).
 template <class Norms>
 __device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2,
-                                                        float pn, float pc, int c0, RowMin& m) {
+                                                        float pn, float pc, int c0, RowMin& m, bool force) {
     // keys folded into two running 3-input minima as they are formed (few live registers)
     float ka = __int_as_float(0x7f800000), kb = ka;
 #pragma unroll
@@ -316,19 +323,21 @@ __device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32],
     }
     const float kmin = fminf(ka, kb);
     const float scale = pc + fabsf(kmin) + fabsf(m.first);
-    if (fmaf(-0x1p-20f, scale, pn + kmin) > m.first) return;
-    argmin_chunk32<false>(v, cn, pn2, c0, m);
+    if (!force && fmaf(-0x1p-20f, scale, pn + kmin) > m.first) return;
+    argmin_chunk32<false>(v, cn, pn2, c0, m, force);
 }
 
-// Columns c0.. of a 32-column chunk that runs past n: one column at a time.
+// Columns c0.. of a 32-column chunk that runs past n: one column at a time
+// (column `forced` is taken while m holds no centroid, as in argmin_chunk32).
 template <bool kGaps, class Norms>
 __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms& cn, float pn, int c0, int64_t n,
-                                            RowMin& m) {
+                                            RowMin& m, int forced) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         if (c0 + j < n) {
             const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cn.load1(c0 + j));
-            if (dist < m.first || (dist == m.first && c0 + j < m.best)) {
+            if (dist < m.first || (dist == m.first && c0 + j < m.best) ||
+                (c0 + j == forced && m.best == kNoLabel && dist == dist)) {
                 m.first = dist;
                 m.best = c0 + j;
             }
@@ -341,25 +350,27 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms
 }
 
 // One 32-column chunk of a row starting at column cc: screened fast path, the
-// exact path when gaps are needed, one column at a time past n.
+// exact path when gaps are needed, one column at a time past n.  The chunk
+// holding column `forced` (the row's previous label, or -1) is always
+// evaluated exactly, so a row whose minimum starts at a bound finds a centroid.
 template <bool kGaps, class Norms>
 __device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, float pn, float pc,
-                                           int cc, int64_t n, RowMin& m) {
+                                           int cc, int64_t n, RowMin& m, int forced) {
     if (cc + 32 <= n) {
         if constexpr (kGaps)
             argmin_chunk32<true>(v, cn, pn2, cc, m);
         else
-            argmin_chunk32_screened(v, cn, pn2, pn, pc, cc, m);
+            argmin_chunk32_screened(v, cn, pn2, pn, pc, cc, m, (unsigned)(forced - cc) < 32u);
     } else if (cc < n) {
-        argmin_tail<kGaps>(v, cn, pn, cc, n, m);
+        argmin_tail<kGaps>(v, cn, pn, cc, n, m, forced);
     }
 }
 
 // Lexicographic (distance, index) minimum and two-largest merge of a partial
-// result (d, b, l, nx) into m.
+// result (d, b, l, nx) into m; a partial without a centroid never displaces one.
 template <bool kGaps>
 __device__ __forceinline__ void merge_rowmin(RowMin& m, float d, int b, float l, float nx) {
-    if (d < m.first || (d == m.first && b < m.best)) m.first = d, m.best = b;
+    if (b != kNoLabel && (d < m.first || (d == m.first && b < m.best) || m.best == kNoLabel)) m.first = d, m.best = b;
     if constexpr (kGaps) {
         m.next = fmaxf(fminf(m.largest, l), fmaxf(m.next, nx));
         m.largest = fmaxf(m.largest, l);
@@ -921,8 +932,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * kSliceCols);
         // After each row tile's first (hinted) centroid tile the quadrant's three
         // warps swap their running minima, so each then starts from the likely
-        // winner and rarely needs an index search.
-        const bool seeding = kArgmin && tiles_n >= 2;
+        // winner and rarely needs an index search.  With row bounds each row's
+        // minimum starts at its bound instead, which needs no exchange.
+        const bool seeding = kArgmin && tiles_n >= 2 && !p.row_bound;
         // One warp hands the tile's centroid-ring slots back to the producer:
         // acc_full means every MMA that read them has completed.
         const bool releaser = p.epi_release && q == 0 && j == 0 && lane == 0;
@@ -956,10 +968,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto mask_of = [&](int64_t t) -> uint64_t {  // centroid tiles of point tile t
             return p.tile_mask && t < tiles_m ? p.tile_mask[t] : ~0ull;
         };
+        auto bound_of = [&](int64_t t) -> float2 {  // (bound, previous label) of this lane's row of tile t
+            const int64_t g = t * kBM + r;
+            return kArgmin && p.row_bound && t < tiles_m && g < mrows ? p.row_bound[g]
+                                                                      : make_float2(__int_as_float(0x7f800000),
+                                                                                    __int_as_float(-1));
+        };
         int64_t id_cur = row_id(blockIdx.x), lead_cur = lead_id(blockIdx.x);
         float pn_cur = norm_of(id_cur);
         int hint_cur = hint_of(lead_cur);
         uint64_t mask_cur = mask_of(blockIdx.x);
+        float2 rb_cur = bound_of(blockIdx.x);
         int64_t id_nxt = row_id(blockIdx.x + step), lead_nxt = lead_id(blockIdx.x + step);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -973,10 +992,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int hint_nxt = hint_of(lead_nxt);
             const uint64_t tmask = mask_cur;
             const uint64_t mask_nxt = mask_of(tile + step);
+            const float2 rb = rb_cur;
+            const float2 rb_nxt = bound_of(tile + step);
+            const int forced = __float_as_int(rb.y);
             const int64_t id_nn = row_id(tile + 2 * step), lead_nn = lead_id(tile + 2 * step);
             const uint64_t pn2 = dev::pack2(pn, pn);
             const float pc = pn + cmax;
-            RowMin m{__int_as_float(0x7f800000), -1e38f, -1e38f, 0x7fffffff};
+            RowMin m{rb.x, -1e38f, -1e38f, kNoLabel};
             for (int i = 0; i < tiles_n; ++i) {
                 const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
                 if (!((tmask >> ct) & 1ull)) continue;  // pruned centroid tile (the first, ct0, never is)
@@ -1017,9 +1039,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                     } else if (p.cn_smem) {
-                        fold_chunk<kGaps>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m);
+                        fold_chunk<kGaps>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m, forced);
                     } else {
-                        fold_chunk<kGaps>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m);
+                        fold_chunk<kGaps>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m, forced);
                     }
                 }
                 if (seeding && i == 0 && (tmask & (tmask - 1ull)) != 0) {  // (more tiles follow in this row tile)
@@ -1070,6 +1092,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             id_cur = id_nxt, lead_cur = lead_nxt, pn_cur = pn_nxt, hint_cur = hint_nxt, mask_cur = mask_nxt;
+            rb_cur = rb_nxt;
             id_nxt = id_nn, lead_nxt = lead_nn;
         }
     }
@@ -1149,6 +1172,8 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         p.tile_mask = argmin->tile_mask;
         p.best_dist = argmin->best_dist;
         p.best_dist_stride = argmin->best_dist_stride;
+        p.row_bound = argmin->row_bound;
+        MXK_REQUIRE(!(p.row_bound && p.gaps), "gemm_mx: row bounds and gaps are exclusive");
         MXK_REQUIRE(!p.tile_mask || (n + kBN - 1) / kBN <= 64, "gemm_mx: a tile mask covers at most 64 centroid tiles");
     }
     p.err = device_error_word();

@@ -77,6 +77,12 @@ struct MxArgmin {
     // best_dist[point * best_dist_stride]
     float* best_dist = nullptr;
     int best_dist_stride = 1;
+    // optional, per GEMM row (the order of pid): (an upper bound on the row's
+    // distance to its nearest centroid, the row's previous label, as int bits),
+    // or (inf, -1).  The epilogue starts each row's minimum at the bound and
+    // always evaluates the chunk holding the previous label exactly; the
+    // result is unchanged.
+    const float2* row_bound = nullptr;
 };
 // Dense: out[m x n] = A . B^T.  Argmin: labels of the m rows against n centroids.
 // rows_dev (optional) = device-resident m (m is then an upper bound).
@@ -112,10 +118,11 @@ int launch_centroid_geometry(int k, int d, const float* centroids, const float* 
                              cudaStream_t stream);
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
-// and the current (cst) and previous (cst_old) centroid stats.
+// and the current (cst) and previous (cst_old) centroid stats; row_bound
+// (optional, one per row) receives MxArgmin::row_bound's records.
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, const int* stop, cudaStream_t stream);
+                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

@@ -223,6 +223,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
     float4 *cstats = nullptr, *tstats = nullptr;  // [2][k] per-centroid stats by iteration parity; [ctiles]
     uint64_t* tmask = nullptr;
+    float2* rbound = nullptr;  // per row in visiting order: (distance bound, previous label)
     if (prune) {
         MXK_CHECK(ws.alloc(&pinfo, n));
         MXK_CHECK(ws.alloc(&chat, kd));
@@ -232,6 +233,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&cstats, 2 * (int64_t)k));
         MXK_CHECK(ws.alloc(&tstats, ctiles));
         MXK_CHECK(ws.alloc(&tmask, (n + kPointTileRows - 1) / kPointTileRows));
+        MXK_CHECK(ws.alloc(&rbound, n));
     }
     int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)
     MXK_CHECK(ws.alloc(&loop, 4));
@@ -281,8 +283,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             MXK_CHECK(launch_centroid_geometry(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, gram, dmin,
                                                cdelta, cst, tstats, loop, stream));
         if (prune_it)
-            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, loop,
-                                       stream));
+            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
+                                       loop, stream));
         MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         if (it < options->fp32_iterations) {
             // kmeans.cu:31-34: FP32 product, assignment without pid (gap init -1).
@@ -319,6 +321,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.gaps = nullptr;
             am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
             am.tile_mask = prune_it ? tmask : nullptr;
+            am.row_bound = prune_it ? rbound : nullptr;
             am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, loop + 3, stream,

@@ -176,13 +176,16 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     const int* __restrict__ prev_label, const float4* __restrict__ pinfo, const float4* __restrict__ cst,
     const float4* __restrict__ cst_old,
     const float4* __restrict__ tst, const float* __restrict__ delta, const float* __restrict__ dmin,
-    uint64_t* __restrict__ mask, const int* __restrict__ stop) {
+    uint64_t* __restrict__ mask, float2* __restrict__ row_bound, const int* __restrict__ stop) {
     if (stop && *stop) return;
     const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
     const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
     const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
     const float inf = __int_as_float(0x7f800000);
     uint64_t m = 0;
+    // (bound on the row's nearest distance, its previous label) for the GEMM's
+    // screen; (inf, -1) when no finite bound holds
+    float2 rb = make_float2(inf, __int_as_float(-1));
     if (row < rows) {
         const int64_t x = pid ? pid[row] : row;
         const int a = prev_label[x];
@@ -198,6 +201,10 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
             const float um = u + 1e-4f * (fabsf(u) + fabsf(ps.x) + fabsf(now.x)) + 1e-30f;
             if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(ps.x) < inf) {  // false for NaN too: keep every tile
                 m = 1ull << (a / tile_cols);  // its own tile
+                // The screen only needs some upper bound: a wider margin costs
+                // nothing measurable and keeps it far from the rounding terms.
+                const float us = um + 1e-3f * (fabsf(um) + fabsf(ps.x) + fabsf(now.x));
+                if (fabsf(us) < inf) rb = make_float2(us, __int_as_float(a));
                 const float* dm = dmin + (int64_t)a * tiles;
                 for (int t = 0; t < tiles; ++t) {
                     const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
@@ -209,6 +216,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
             }
         }
     }
+    if (row_bound && row < rows) row_bound[row] = rb;
     // union over the 128 rows
     m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
         ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
@@ -266,14 +274,15 @@ int launch_centroid_geometry(int k, int d, const float* centroids, const float* 
 
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, const int* stop, cudaStream_t stream) {
+                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream) {
     if (rows <= 0) return MXK_OK;
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
     const int64_t blocks = (rows + kPointTileRows - 1) / kPointTileRows;
     LaunchScope scope("tile_mask", stream);
     tile_mask_kernel<<<(unsigned)blocks, 128, 0, stream>>>(rows, k, d, tiles, kCentroidTileRows, pid, prev_label,
-                                                           pinfo, cst, cst_old, tst, delta, dmin, mask, stop);
+                                                           pinfo, cst, cst_old, tst, delta, dmin, mask, row_bound,
+                                                           stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
