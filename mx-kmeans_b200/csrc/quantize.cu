@@ -183,6 +183,26 @@ __global__ void __launch_bounds__(256) l2_norm_kernel(int64_t rows, int d, const
     if (row0 + lane < rows) norms[row0 + lane] = sum;
 }
 
+// The same sums for a few rows (the centroids, every iteration): one thread per
+// row, its features read as 128-bit loads, all in flight at once, and
+// accumulated in feature order as above.  d % 4 == 0, rows 16-byte aligned.
+__global__ void __launch_bounds__(64) l2_norm_rows_kernel(int64_t rows, int d, const float* __restrict__ x,
+                                                          float* __restrict__ norms) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int f = 0; f < d / 4; ++f) {
+        const float4 v = __ldg(xr + f);
+        sum = fmaf(v.x, v.x, sum);
+        sum = fmaf(v.y, v.y, sum);
+        sum = fmaf(v.z, v.z, sum);
+        sum = fmaf(v.w, v.w, sum);
+    }
+    norms[row] = sum;
+}
+
 // One thread per point, one 32-feature block at a time (eight 128-bit loads of
 // the block's contiguous 128 bytes): block maximum, the FP4 (E2M1) and FP6 (E3M2,
 // as the reference) scales, and the reconstruction errors of features 1..31
@@ -399,9 +419,14 @@ int launch_quantize(int bits, int64_t rows, int d, const float* points, const in
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream) {
     if (rows <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && x && norms, "compute_l2_norm: bad arguments");
-    const int64_t blocks = (rows + 255) / 256;
     LaunchScope scope("l2_norm", stream);
-    l2_norm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, d, x, norms);
+    if (rows <= 65536 && d % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+        // few rows: spread them over the SMs, one per thread
+        l2_norm_rows_kernel<<<(unsigned)((rows + 63) / 64), 64, 0, stream>>>(rows, d, x, norms);
+    } else {
+        const int64_t blocks = (rows + 255) / 256;
+        l2_norm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, d, x, norms);
+    }
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
