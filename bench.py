@@ -387,8 +387,9 @@ def main():
         tflops = executed / seconds / 1e12
         peak_tf = 2.0 * pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
         # algorithmic DRAM bytes per launch: each point's FP32 row (quantized in
-        # the kernel), its id, norm, previous label, new label and distance
-        alg_bytes = rows * (4.0 * D_PAD + 20.0)
+        # the kernel), its id, norm, previous label, new label and distance,
+        # and in the pruned iterations (all but the first) its 8-byte bound record
+        alg_bytes = rows * (4.0 * D_PAD + 20.0 + 8.0 * (ITERS - 1) / ITERS)
         gbs = alg_bytes * iters / seconds / 1e9
         peak_gbs = pk.get("hbm_gbs", 6650.0)
         # the binding roofline is the one whose ideal time is longer
@@ -400,8 +401,8 @@ def main():
                     "frac": gbs / peak_gbs if hbm_bound else tflops / peak_tf, "traffic": traffic,
                     "algorithmic_bytes_per_launch": alg_bytes,
                     "tensor_tflops_executed": tflops, "tensor_frac_executed": tflops / peak_tf,
-                    "traffic_unit": "DRAM bytes per unpruned launch (ncu capture scaled to these rows; "
-                                    "profiles/mx_gemm_argmin_config4.md)",
+                    "traffic_unit": "DRAM bytes per launch of a pruned iteration (ncu capture of iteration 10 "
+                                    "scaled to these rows; profiles/mx_gemm_argmin_config4.md)",
                     "kernel": "mx_gemm_argmin", "ms_per_iteration": gemm[1] / max(iters, 1),
                     "executed_flops_per_iteration": executed / max(iters, 1),
                     "nominal_flops_per_iteration": flops_per_iter,
