@@ -60,28 +60,49 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
     int run = 0;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int64_t i = begin; i < end; ++i) {
-        const int64_t pnt = order ? (int64_t)order[i] : i;
-        const int lab = labels[pnt];
-        if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
-        if (lab != cur) {
-            if (cur >= 0) {
-                float* dst = sums + (int64_t)cur * d + 4 * lane;
+    // Rows are taken kBatch at a time: their ids, labels and feature vectors
+    // are all requested before the first is added, so each warp keeps several
+    // rows in flight; the additions stay in row order.
+    constexpr int kBatch = NJ <= 2 ? 4 : (NJ <= 4 ? 2 : 1);
+    for (int64_t i0 = begin; i0 < end; i0 += kBatch) {
+        int64_t pnt[kBatch];
+        int lab[kBatch];
+        float4 xb[kBatch][NJ];
 #pragma unroll
-                for (int j = 0; j < NJ; ++j)
-                    red_add_v4(dst + 128 * j, acc[j]), acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (lane == 0) atomicAdd(counts + cur, run);
+        for (int u = 0; u < kBatch; ++u)
+            pnt[u] = i0 + u < end ? (order ? (int64_t)order[i0 + u] : i0 + u) : -1;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) lab[u] = pnt[u] >= 0 ? labels[pnt[u]] : -1;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            if (pnt[u] >= 0) {
+                const float* src = points + pnt[u] * d + 4 * lane;
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) xb[u][j] = ldg_stream4(src + 128 * j);
             }
-            cur = lab;
-            run = 0;
         }
-        const float* src = points + pnt * d + 4 * lane;
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            const float4 x = ldg_stream4(src + 128 * j);
-            acc[j].x += x.x, acc[j].y += x.y, acc[j].z += x.z, acc[j].w += x.w;
+        for (int u = 0; u < kBatch; ++u) {
+            if (pnt[u] < 0) break;
+            if (bad_label(lab[u], k, lane == 0 ? err : nullptr)) continue;
+            if (lab[u] != cur) {
+                if (cur >= 0) {
+                    float* dst = sums + (int64_t)cur * d + 4 * lane;
+#pragma unroll
+                    for (int j = 0; j < NJ; ++j)
+                        red_add_v4(dst + 128 * j, acc[j]), acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (lane == 0) atomicAdd(counts + cur, run);
+                }
+                cur = lab[u];
+                run = 0;
+            }
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                const float4 x = xb[u][j];
+                acc[j].x += x.x, acc[j].y += x.y, acc[j].z += x.z, acc[j].w += x.w;
+            }
+            ++run;
         }
-        ++run;
     }
     if (cur < 0) return;
     float* dst = sums + (int64_t)cur * d + 4 * lane;
@@ -257,23 +278,33 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
         return MXK_OK;
     }
     if (aligned && d % 128 == 0 && d <= 1024) {
-        const int64_t warps_total = (int64_t)sms * 64;  // 8 CTAs of 256 threads per SM
-        int64_t per_warp = (n + warps_total - 1) / warps_total;
-        if (per_warp < 16) per_warp = 16;
-        const int64_t warps = (n + per_warp - 1) / per_warp;
-        const int64_t blocks = (warps * 32 + 255) / 256;
-        LaunchScope scope("accumulate_runs", stream);
+        // one wave: as many warps as the SMs hold at once, each a contiguous
+        // range of rows
+        auto launch = [&](auto kernel) -> int {
+            int per_sm = 0;
+            MXK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0));
+            if (per_sm < 1) per_sm = 1;
+            const int64_t warps_total = (int64_t)sms * per_sm * 8;
+            int64_t per_warp = (n + warps_total - 1) / warps_total;
+            if (per_warp < 16) per_warp = 16;
+            const int64_t warps = (n + per_warp - 1) / per_warp;
+            const int64_t blocks = (warps * 32 + 255) / 256;
+            LaunchScope scope("accumulate_runs", stream);
+            kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, order, sums, counts, per_warp, err,
+                                                         stop);
+            MXK_CUDA(cudaGetLastError());
+            return MXK_OK;
+        };
         switch (d / 128) {
-#define MXK_ACC_CASE(J) \
-    case J: accumulate_runs_kernel<J><<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, order, sums, counts, \
-                                                                       per_warp, err, stop);                        \
-        break;
-            MXK_ACC_CASE(1) MXK_ACC_CASE(2) MXK_ACC_CASE(3) MXK_ACC_CASE(4) MXK_ACC_CASE(5) MXK_ACC_CASE(6)
-            MXK_ACC_CASE(7) MXK_ACC_CASE(8)
-#undef MXK_ACC_CASE
+            case 1: return launch(accumulate_runs_kernel<1>);
+            case 2: return launch(accumulate_runs_kernel<2>);
+            case 3: return launch(accumulate_runs_kernel<3>);
+            case 4: return launch(accumulate_runs_kernel<4>);
+            case 5: return launch(accumulate_runs_kernel<5>);
+            case 6: return launch(accumulate_runs_kernel<6>);
+            case 7: return launch(accumulate_runs_kernel<7>);
+            default: return launch(accumulate_runs_kernel<8>);
         }
-        MXK_CUDA(cudaGetLastError());
-        return MXK_OK;
     }
     LaunchScope scope("accumulate_scalar", stream);
     accumulate_scalar_kernel<<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err, stop);
