@@ -28,6 +28,12 @@ inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileR
     return (rows + tile_rows - 1) / tile_rows * (d / 128) * ((tile_rows + 127) / 128) * 512;
 }
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
+// launch_l2_norm's norms (bit-identical) and, per point, the pruning pass's
+// pinfo = (+inf: the slot the GEMM writes the point's distance into,
+// |x|^2 - |x^|^2, |x^|^2, |x|^2) for its MXFP8 round trip x^, in one pass over
+// the points.  d % 128 == 0, points 16-byte aligned.
+int launch_point_norm_stats(int64_t n, int d, const float* points, float* norms, float4* pinfo,
+                            cudaStream_t stream);
 // Rows of an MXFP8 matrix (d bytes per row, d / 32 row-major scale bytes)
 // gathered in the order pid (null: identity) into contiguous rows, scales in the
 // kPointTileRows atom layout.  stop: the Lloyd loop's stop word (optional).
@@ -101,11 +107,6 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
 // Exact pruning of centroid tiles (see prune.cu for the bounds).  Supported for
 // at most 64 centroid tiles and d % 128 == 0, d <= 1024.
 bool prune_supported(int64_t k, int d);
-// Per point, once per run: pinfo = (+inf: the slot the GEMM writes the point's
-// distance into, |x|^2 - |x^|^2, |x^|^2, |x|^2) for its MXFP8 round trip x^
-// (pn: the norms the GEMM uses).
-int launch_point_quant_stats(int64_t n, int d, const float* points, const float* pn, float4* pinfo,
-                             cudaStream_t stream);
 // Centroid geometry: chat (k x d dequantized centroids), cst (k x (|c|^2 -
 // |c^|^2, |c^|^2, |c|^2 as cn, 0)), tst (per tile: min beta, max |c^|^2, max
 // |c|^2, non-finite flag) and, with prev: delta (k upper bounds of |c^ -

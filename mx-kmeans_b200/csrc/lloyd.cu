@@ -252,8 +252,10 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     }
 
     // Once per run (kmeans.cu:24-27).
-    MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
-    if (prune) MXK_CHECK(launch_point_quant_stats(n, d, points, pnorm, pinfo, stream));
+    if (prune)  // the points' norms and their pruning terms in one pass
+        MXK_CHECK(launch_point_norm_stats(n, d, points, pnorm, pinfo, stream));
+    else
+        MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
     if (cache) MXK_CHECK(launch_quantize(8, n, d, points, nullptr, qnat, snat, nullptr, nullptr, stream, 0));
     if (!kForced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));

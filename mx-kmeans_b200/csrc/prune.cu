@@ -60,25 +60,6 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// Per point, once per run (one warp per row): pinfo = (distance slot, alpha =
-// |x|^2 - |x^|^2, |x^|^2, |x|^2), |x|^2 being the norm the GEMM uses; the GEMM
-// writes each point's distance into the first slot.
-__global__ void __launch_bounds__(256) point_quant_stats_kernel(int64_t n, int d, const float* __restrict__ points,
-                                                                const float* __restrict__ pn,
-                                                                float4* __restrict__ pinfo) {
-    const int lane = threadIdx.x & 31;
-    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (p >= n) return;
-    const float* row = points + p * d;
-    float h = 0.0f;
-    for (int j = 4 * lane; j < d; j += 128) {
-        const float4 xh = mxfp8_round_trip4(__ldg(reinterpret_cast<const float4*>(row + j)), lane);
-        h = fmaf(xh.x, xh.x, fmaf(xh.y, xh.y, fmaf(xh.z, xh.z, fmaf(xh.w, xh.w, h))));
-    }
-    h = warp_sum(h);
-    if (lane == 0) pinfo[p] = make_float4(__int_as_float(0x7f800000), pn[p] - h, h, pn[p]);
-}
-
 // Per centroid (one warp per row): the dequantized row c^ into chat, stats
 // cst[a] = (beta = |c|^2 - |c^|^2, |c^|^2, |c|^2, 0), and delta[a] >= |c^_a -
 // c^_a_old| (the previous centroids' round trip; +inf without prev).
@@ -230,16 +211,6 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
 
 bool prune_supported(int64_t k, int d) {
     return (k + kCentroidTileRows - 1) / kCentroidTileRows <= kMaxPruneTiles && d % 128 == 0 && d <= 1024;
-}
-
-int launch_point_quant_stats(int64_t n, int d, const float* points, const float* pn, float4* pinfo,
-                             cudaStream_t stream) {
-    if (n <= 0) return MXK_OK;
-    MXK_REQUIRE(d % 128 == 0, "point stats: d must be a multiple of 128");
-    LaunchScope scope("point_quant_stats", stream);
-    point_quant_stats_kernel<<<(unsigned)((n * 32 + 255) / 256), 256, 0, stream>>>(n, d, points, pn, pinfo);
-    MXK_CUDA(cudaGetLastError());
-    return MXK_OK;
 }
 
 int64_t gram_scratch_floats(int k) { return (int64_t)std::min(k, kGramRows) * k; }

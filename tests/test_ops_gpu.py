@@ -20,9 +20,11 @@ def _to(torch, a):
 def test_l2_norm_bit_exact(torch_cuda, mxk, orc):
     torch = torch_cuda
     g = np.random.default_rng(0)
-    # (up to 65536 rows with d % 4 == 0 take the row-per-thread kernel, the rest
-    # the shared-memory transpose)
-    for n, d in [(1, 1), (33, 100), (4097, 128), (1000, 768), (70001, 132), (300, 30)]:
+    # (up to 65536 rows with d % 4 == 0 take the row-per-thread kernel, more rows
+    # with d % 128 == 0 the 32-row staged kernel, the rest the shared-memory
+    # transpose)
+    for n, d in [(1, 1), (33, 100), (4097, 128), (1000, 768), (70001, 132), (300, 30), (70001, 128),
+                 (65601, 256)]:
         x = (g.standard_normal((n, d)) * 10).astype(np.float32)
         out = torch.empty(n, dtype=torch.float32, device="cuda:0")
         mxk.compute_l2_norm(_to(torch, x), out)
