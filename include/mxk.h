@@ -200,9 +200,19 @@ int mxk_kmeans_mixed_sharded(void* comm, int64_t n_local, int d, int k, const fl
  * initialisation on HOST arrays; same selections as the reference for a seed. */
 int mxk_host_init_kmeanspp(const float* points, int64_t n, int d, int k, uint32_t seed, float* out);
 int mxk_host_init_farthest(const float* points, int64_t n, int d, int k, float* out);
-/* Dense CSV with header, d features (+ optional ignored label column), zero
- * padded to padded_d; rejects non-finite values and row-count mismatches. */
+/* read_points, include/host_utils.hpp:40-67: dense CSV with header, d features
+ * (+ optional ignored label column), zero padded to padded_d; rejects
+ * non-finite values and row-count mismatches with the reference's messages.
+ * Parsed on all host threads; the values are bit-identical to std::stof's. */
 int mxk_host_read_points(const char* path, int64_t n, int d, int padded_d, float* out);
+/* The same with an explicit thread count (<= 0: all hardware threads) and
+ * chunk size in bytes (<= 0: automatic); results do not depend on either. */
+int mxk_host_read_points_ex(const char* path, int64_t n, int d, int padded_d, int threads,
+                            int64_t chunk_bytes, float* out);
+/* Binary fast path (no reference counterpart; the reference reads CSV only):
+ * n x d little-endian float32 values, row-major, no header, exactly n*d*4
+ * bytes; zero padded to padded_d; non-finite values rejected as in the CSV. */
+int mxk_host_read_points_f32(const char* path, int64_t n, int d, int padded_d, float* out);
 int mxk_host_write_labels(const char* path, const int* labels, int64_t n);
 
 /* ---- kernel timing (CUDA events around each launch on its stream) ---------- */

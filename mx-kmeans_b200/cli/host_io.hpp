@@ -1,9 +1,8 @@
 // Host-side input/output and centroid initialisation of the mxkmeans CLI.
 //
 // Interface-compatible with ParCIS/MX-KMeans include/host_utils.hpp:1-141:
-//   * CSV: a header row, then rows of d features and optionally one ignored
-//     trailing label column; values must parse completely as finite floats; the
-//     row count must equal --n-samples; features are zero-padded to padded_d.
+//   * CSV input (read on all host threads, same accept/reject rules and
+//     messages): point_reader.hpp;
 //   * labels: "clusters" header, one label per line.
 //   * K-Means++ (D^2 sampling with std::mt19937(seed), the first index from
 //     uniform_int_distribution<int>(0, n-1), each next index by a
@@ -24,23 +23,9 @@
 #include <string>
 #include <vector>
 
-namespace mxk_cli {
+#include "point_reader.hpp"
 
-inline std::vector<std::string> csv_cells(const std::string& line) {
-    std::vector<std::string> out;
-    size_t start = 0;
-    while (true) {
-        const size_t comma = line.find(',', start);
-        if (comma == std::string::npos) {
-            if (start < line.size()) out.push_back(line.substr(start));
-            break;
-        }
-        out.push_back(line.substr(start, comma - start));
-        start = comma + 1;
-    }
-    if (!line.empty() && line.back() == ',') out.emplace_back();
-    return out;
-}
+namespace mxk_cli {
 
 inline float parse_float(const std::string& text) {
     size_t used = 0;
@@ -55,40 +40,6 @@ inline int parse_int(const std::string& text) {
     const int v = std::stoi(text, &used);
     if (used != text.size()) throw std::invalid_argument("Invalid integer: " + text);
     return v;
-}
-
-inline bool blank(const std::string& line) { return line.find_first_not_of(" \t\r") == std::string::npos; }
-
-inline std::vector<float> read_points(const std::string& path, int64_t n, int d, int padded_d) {
-    std::ifstream in(path);
-    if (!in) throw std::runtime_error("Cannot open input: " + path);
-    std::string line;
-    if (!std::getline(in, line)) throw std::runtime_error("Input is empty");
-    const size_t columns = csv_cells(line).size();
-    if (columns != size_t(d) && columns != size_t(d) + 1)
-        throw std::runtime_error("CSV header must contain d features and optionally one label column");
-    std::vector<float> points(size_t(n) * padded_d, 0.0f);
-    int64_t row = 0;
-    while (std::getline(in, line)) {
-        if (blank(line)) continue;
-        if (row >= n) throw std::runtime_error("CSV contains more rows than --n-samples");
-        const auto cells = csv_cells(line);
-        if (cells.size() != columns)
-            throw std::runtime_error("Wrong column count at data row " + std::to_string(row + 1));
-        float* dst = points.data() + size_t(row) * padded_d;
-        for (int j = 0; j < d; ++j) {
-            try {
-                dst[j] = parse_float(cells[j]);
-            } catch (const std::exception&) {
-                throw std::runtime_error("Invalid feature at data row " + std::to_string(row + 1) + ", column " +
-                                         std::to_string(j + 1));
-            }
-        }
-        ++row;
-    }
-    if (in.bad()) throw std::runtime_error("Error while reading input: " + path);
-    if (row != n) throw std::runtime_error("CSV row count does not match --n-samples");
-    return points;
 }
 
 inline void write_labels(const std::string& path, const std::vector<int>& labels) {

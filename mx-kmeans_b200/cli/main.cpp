@@ -3,8 +3,10 @@
 // Options, validation, CSV input, label output and the stdout timing record
 // follow ParCIS/MX-KMeans src/main.cu:1-134.  Changes: the device check asks for
 // compute capability 10.x (B200), the 32-bit index limits on N*D and N*K are
-// lifted (the library indexes in 64 bits and never builds an N x K buffer), and
-// --gpus N row-shards the points over N GPUs of this node (one host thread per
+// lifted (the library indexes in 64 bits and never builds an N x K buffer), the
+// CSV is parsed on all host threads (same rules and messages), an input path
+// ending in .f32 is read as raw float32 rows, and --gpus N row-shards the
+// points over N GPUs of this node (one host thread per
 // GPU, NCCL allreduce of the per-cluster sums and counts each iteration).
 #include <cuda_runtime.h>
 #include <getopt.h>
@@ -13,6 +15,7 @@
 #include <cstdio>
 #include <filesystem>
 #include <iostream>
+#include <memory>
 #include <string>
 #include <thread>
 #include <vector>
@@ -38,6 +41,7 @@ Required:
   -d, --dimensions D      Number of feature columns (padded internally to 128)
   -k, --clusters K        Cluster count, at least 4 and a multiple of 4
   -i, --input-file PATH   Dense CSV with a header; optional final label column
+                          (a .f32 file: raw little-endian float32, N x D rows)
 
 Options:
   -o, --out-filename PATH Label CSV (default: labels.csv)
@@ -151,16 +155,24 @@ int main(int argc, char** argv) {
             if (prop.major != 10)
                 throw std::runtime_error("This build requires an sm_100 Blackwell data-center GPU, such as B200");
         }
-        const auto points = mxk_cli::read_points(args.input, args.n, args.d, d);
+        // Every element is written by the reader (features, then zero pads), so
+        // the buffer is left uninitialised and first touched by the reader's threads.
+        const size_t point_floats = size_t(args.n) * size_t(d);
+        std::unique_ptr<float[]> point_buffer(new float[point_floats]);
+        if (mxk_cli::is_f32_path(args.input))
+            mxk_cli::read_points_f32_into(args.input, args.n, args.d, d, point_buffer.get());
+        else
+            mxk_cli::read_points_into(args.input, args.n, args.d, d, point_buffer.get());
+        const float* points = point_buffer.get();
         // Initial centroids on GPU 0 (mxk_init_*: the same rows as the reference's
         // host_utils.hpp functions pick, at GPU speed).
         std::vector<float> initial(size_t(args.k) * d);
         {
             check_cuda(cudaSetDevice(0), "cudaSetDevice");
             float *dev_points = nullptr, *dev_centroids = nullptr;
-            check_cuda(cudaMalloc(&dev_points, sizeof(float) * points.size()), "cudaMalloc");
+            check_cuda(cudaMalloc(&dev_points, sizeof(float) * point_floats), "cudaMalloc");
             check_cuda(cudaMalloc(&dev_centroids, sizeof(float) * initial.size()), "cudaMalloc");
-            check_cuda(cudaMemcpy(dev_points, points.data(), sizeof(float) * points.size(), cudaMemcpyHostToDevice),
+            check_cuda(cudaMemcpy(dev_points, points, sizeof(float) * point_floats, cudaMemcpyHostToDevice),
                        "cudaMemcpy");
             const int st = args.initialization == "farthest"
                                ? mxk_init_farthest(args.n, d, args.k, dev_points, dev_centroids, nullptr)
@@ -193,7 +205,7 @@ int main(int argc, char** argv) {
                     check_cuda(cudaMalloc(&s.points, sizeof(float) * size_t(std::max<int64_t>(s.rows, 1)) * d), "cudaMalloc");
                     check_cuda(cudaMalloc(&s.centroids, sizeof(float) * initial.size()), "cudaMalloc");
                     check_cuda(cudaMalloc(&s.labels, sizeof(int) * size_t(std::max<int64_t>(s.rows, 1))), "cudaMalloc");
-                    check_cuda(cudaMemcpy(s.points, points.data() + size_t(s.row0) * d, sizeof(float) * size_t(s.rows) * d,
+                    check_cuda(cudaMemcpy(s.points, points + size_t(s.row0) * d, sizeof(float) * size_t(s.rows) * d,
                                           cudaMemcpyHostToDevice),
                                "cudaMemcpy");
                     if (G > 1) check(mxk_comm_init(&s.comm, G, g, uid));

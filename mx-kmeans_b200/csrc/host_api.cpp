@@ -1,6 +1,7 @@
 // C entry points for the host-side pieces of the CLI (CSV reader and centroid
 // initialisation), so embedding programs and tests can use them without the
-// executable.  Mirrors ParCIS/MX-KMeans include/host_utils.hpp:40-141.
+// executable.  Mirrors ParCIS/MX-KMeans include/host_utils.hpp:40-141; the CSV
+// reader runs on all host threads (point_reader.hpp).
 #include <cstring>
 #include <exception>
 #include <string>
@@ -40,10 +41,25 @@ int mxk_host_init_farthest(const float* points, int64_t n, int d, int k, float* 
 }
 
 int mxk_host_read_points(const char* path, int64_t n, int d, int padded_d, float* out) {
+    return mxk_host_read_points_ex(path, n, d, padded_d, 0, 0, out);
+}
+
+int mxk_host_read_points_ex(const char* path, int64_t n, int d, int padded_d, int threads, int64_t chunk_bytes,
+                            float* out) {
     if (!path || !out || n <= 0 || d <= 0 || padded_d < d) return mxk::fail(MXK_ERR_INVALID, "read_points: bad arguments");
     try {
-        const auto v = mxk_cli::read_points(path, n, d, padded_d);
-        std::memcpy(out, v.data(), v.size() * sizeof(float));
+        mxk_cli::read_points_into(path, n, d, padded_d, out, threads, chunk_bytes);
+        return MXK_OK;
+    } catch (const std::exception& e) {
+        return mxk::fail(MXK_ERR_INVALID, e.what());
+    }
+}
+
+int mxk_host_read_points_f32(const char* path, int64_t n, int d, int padded_d, float* out) {
+    if (!path || !out || n <= 0 || d <= 0 || padded_d < d)
+        return mxk::fail(MXK_ERR_INVALID, "read_points_f32: bad arguments");
+    try {
+        mxk_cli::read_points_f32_into(path, n, d, padded_d, out);
         return MXK_OK;
     } catch (const std::exception& e) {
         return mxk::fail(MXK_ERR_INVALID, e.what());

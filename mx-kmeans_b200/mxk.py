@@ -18,6 +18,7 @@ class MxkError(RuntimeError):
     def __init__(self, status, message):
         super().__init__(f"mxk status {status}: {message}")
         self.status = status
+        self.message = message
 
 
 class MxkInvalidArgument(MxkError, ValueError):
@@ -73,6 +74,8 @@ SIGNATURES = {
     "mxk_host_init_kmeanspp": ([_P, _I64, _I, _I, ctypes.c_uint32, _P], _I),
     "mxk_host_init_farthest": ([_P, _I64, _I, _I, _P], _I),
     "mxk_host_read_points": ([ctypes.c_char_p, _I64, _I, _I, _P], _I),
+    "mxk_host_read_points_ex": ([ctypes.c_char_p, _I64, _I, _I, _I, _I64, _P], _I),
+    "mxk_host_read_points_f32": ([ctypes.c_char_p, _I64, _I, _I, _P], _I),
     "mxk_host_write_labels": ([ctypes.c_char_p, _P, _I64], _I),
     "mxk_profile_enable": ([_I], _I),
     "mxk_profile_read": ([ctypes.POINTER(KernelStat), _I, ctypes.POINTER(_I)], _I),
@@ -309,10 +312,24 @@ def host_init_farthest(points, k):
     return out
 
 
-def host_read_points(path, n, d, padded_d):
+def host_read_points(path, n, d, padded_d, threads=None, chunk_bytes=0):
+    """The reference's CSV reader (parallel); threads/chunk_bytes only change
+    how the file is split, never the result."""
     import numpy as np
     out = np.empty((n, padded_d), np.float32)
-    check(load().mxk_host_read_points(str(path).encode(), n, d, padded_d, _np(out)))
+    if threads is None and not chunk_bytes:
+        check(load().mxk_host_read_points(str(path).encode(), n, d, padded_d, _np(out)))
+    else:
+        check(load().mxk_host_read_points_ex(str(path).encode(), n, d, padded_d, threads or 0, chunk_bytes,
+                                             _np(out)))
+    return out
+
+
+def host_read_points_f32(path, n, d, padded_d):
+    """Raw little-endian float32 rows (n x d, no header), zero padded."""
+    import numpy as np
+    out = np.empty((n, padded_d), np.float32)
+    check(load().mxk_host_read_points_f32(str(path).encode(), n, d, padded_d, _np(out)))
     return out
 
 

@@ -38,3 +38,18 @@ extern "C" int ref_read_points(const char* path, int n, int d, int padded_d, flo
         return 1;
     }
 }
+// The same, also copying the reader's exception text into msg (cap bytes).
+extern "C" int ref_read_points_msg(const char* path, int n, int d, int padded_d, float* out, char* msg, int cap) {
+    try {
+        const auto v = read_points(path, n, d, padded_d);
+        std::memcpy(out, v.data(), v.size() * sizeof(float));
+        if (cap > 0) msg[0] = '\0';
+        return 0;
+    } catch (const std::exception& e) {
+        if (cap > 0) {
+            std::strncpy(msg, e.what(), size_t(cap) - 1);
+            msg[cap - 1] = '\0';
+        }
+        return 1;
+    }
+}

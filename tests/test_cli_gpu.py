@@ -2,7 +2,8 @@
 initialisation, Lloyd, label file and stdout record out.  The same run is
 replayed through the reference's own CSV reader and K-Means++ / farthest-first
 (oracle/_ref/libref_host.so) and this library's kmeans_mixed; integer-valued
-points keep every sum exact, so the labels must agree exactly."""
+points keep every sum exact, so the labels must agree exactly.  The same points
+given as a raw float32 (.f32) file give the same labels."""
 import ctypes
 import os
 import subprocess
@@ -58,3 +59,13 @@ def test_cli_matches_reference_host_path(torch_cuda, mxk, orc, tmp_path, init):
     it = mxk.kmeans_mixed(xt, ct, lab, mxk.Options(max_iterations=25, tolerance=0.0))
     assert it == iters
     assert np.array_equal(lab.cpu().numpy(), labels_cli)
+
+    # the same points as raw float32 rows (.f32 input): same run, same labels
+    raw = tmp_path / "points.f32"
+    x.astype("<f4").tofile(raw)
+    out2 = tmp_path / "labels2.csv"
+    r2 = subprocess.run([CLI, "-n", str(n), "-d", str(d), "-k", str(k), "-i", str(raw), "-o", str(out2), "-m", "25",
+                         "-t", "0", "-s", str(seed), "--init", init], capture_output=True, text=True, timeout=300)
+    assert r2.returncode == 0, r2.stderr
+    assert r2.stdout.strip().splitlines()[-1].split(",")[4] == str(iters)
+    assert open(out2).read() == open(out).read()

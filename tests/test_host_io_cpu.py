@@ -86,3 +86,217 @@ def test_csv_reader_matches_reference(mxk, ref_host, tmp_path, text, n, ok):
     else:
         with pytest.raises(ValueError):
             mxk.host_read_points(p, n, 2, 128)
+
+
+# ---- parallel CSV reader against the reference's own read_points -----------
+#
+# The reader splits the file into chunks at line boundaries and parses them on
+# several threads, with an exact fast path for plain decimals.  Whatever the
+# chunking, it must accept and reject the same files as the reference's
+# sequential reader, with the same message, and produce the same floats bit for
+# bit (std::stof's correctly rounded results, -0 included).
+
+def _ref_read(ref_host, path, n, d, dp):
+    out = np.zeros((n, dp), np.float32)
+    msg = ctypes.create_string_buffer(512)
+    rc = ref_host.ref_read_points_msg(str(path).encode(), n, d, dp, ctypes.c_void_p(out.ctypes.data), msg, 512)
+    return rc, out, msg.value.decode()
+
+
+def _ours(mxk, path, n, d, dp, threads=None, chunk=0):
+    try:
+        return 0, mxk.host_read_points(path, n, d, dp, threads=threads, chunk_bytes=chunk), ""
+    except ValueError as e:
+        return 1, None, e.message
+
+
+def _same(ref, got):
+    rc, out, msg = ref
+    grc, gout, gmsg = got
+    assert grc == rc, (msg, gmsg)
+    if rc == 0:
+        assert np.array_equal(gout.view(np.uint32), out.view(np.uint32))
+    else:
+        assert gmsg == msg
+
+
+@pytest.mark.parametrize("text,n,ok", CSV_CASES)
+@pytest.mark.parametrize("chunk", [1, 3, 7])
+def test_csv_reader_chunked_matches_reference(mxk, ref_host, tmp_path, text, n, ok, chunk):
+    p = tmp_path / "pts.csv"
+    p.write_text(text)
+    _same(_ref_read(ref_host, p, n, 2, 128), _ours(mxk, p, n, 2, 128, threads=3, chunk=chunk))
+
+
+TRICKY = ["0", "-0", "+0", "-0.0", "0.000", "1", "-1", "+1", "1.", ".5", "-.5", "5e0", "1e-3", "1E+3", " 7",
+          "\t7", "7 ", "7\t", "7\r", "  -3.25  ", "1e-38", "1.17549435e-38", "1.1754942e-38", "1e-40", "1e-45",
+          "0e-99", "0e999999", "3.4028235e38", "3.4028236e38", "3.40282357e38", "1e39", "-1e39", "16777217",
+          "16777219", "33554435", "0.1", "0.2", "0.3", "123456789012345678", "1234567890123456789",
+          "12345678901234567890", "9007199254740993", "0.1000000000000000055511151231257827", "0x1p3", "0X1.8p1",
+          "0x", "inf", "-inf", "nan", "NaN", "infinity", "", " ", "e5", "1e", "1e+", "1.2.3", "--1", "+-1", "1x",
+          "1 2", ".", "-", "\v7", "\f7", "7\v", "1e22", "1e23", "9e22", "4.5e-23", "1e-22", "2e-22",
+          "00000000000000000000001.5", "1.50000000000000000000000", "0.000000000000000000000000000001"]
+
+
+def test_csv_reader_tricky_cells_match_reference(mxk, ref_host, tmp_path):
+    for i, cell in enumerate(TRICKY):
+        p = tmp_path / f"c{i}.csv"
+        with open(p, "w", newline="") as f:
+            f.write("a,b,label\n" + f"{cell},2.5,x\n" + f"-1,{cell},y\n")
+        for chunk in (0, 4):
+            _same(_ref_read(ref_host, p, 2, 2, 128), _ours(mxk, p, 2, 2, 128, threads=2, chunk=chunk))
+
+
+def _random_decimals(g, count):
+    """Plain decimals of 1-19 significant digits and powers of ten across the
+    float range: the fast path's whole domain and its edges."""
+    out = []
+    for _ in range(count):
+        nd = int(g.integers(1, 20))
+        digits = "".join(str(int(v)) for v in g.integers(0, 10, nd))
+        sign = g.choice(["", "-", "+"], p=[0.6, 0.35, 0.05])
+        form = int(g.integers(0, 3))
+        e = int(g.integers(-48, 40))
+        if form == 0:  # d.ddd e+-x
+            s = f"{sign}{digits[0]}.{digits[1:]}e{e}"
+        elif form == 1:  # ddd.ddd
+            cut = int(g.integers(0, nd + 1))
+            s = f"{sign}{digits[:cut]}.{digits[cut:]}" if cut < nd else f"{sign}{digits}"
+            if s in (sign + ".", "."):
+                s = sign + "0"
+        else:  # ddd e+-x
+            s = f"{sign}{digits}E{e:+d}"
+        out.append(s)
+    return out
+
+
+def test_csv_reader_random_decimals_bit_exact(mxk, ref_host, tmp_path):
+    """About 200k random plain decimals, parsed by the reference (std::stof per
+    cell) and by the parallel reader (fast path + strtof), compared bit for bit,
+    including which ones are rejected (denormal and overflowing values)."""
+    g = np.random.default_rng(123)
+    d = 64
+    for trial in range(4):
+        n = 800
+        cells = _random_decimals(g, n * d)
+        p = tmp_path / f"r{trial}.csv"
+        with open(p, "w") as f:
+            f.write(",".join(f"f{j}" for j in range(d)) + "\n")
+            for r in range(n):
+                f.write(",".join(cells[r * d:(r + 1) * d]) + "\n")
+        ref = _ref_read(ref_host, p, n, d, 128)
+        if ref[0]:
+            # a rejected value stops the reference at its first one; compare
+            # that, then each row separately so the accepted cells count too
+            _same(ref, _ours(mxk, p, n, d, 128, threads=4))
+            for r in range(n):
+                q = tmp_path / "row.csv"
+                q.write_text(",".join(f"f{j}" for j in range(d)) + "\n" + ",".join(cells[r * d:(r + 1) * d]) + "\n")
+                _same(_ref_read(ref_host, q, 1, d, 128), _ours(mxk, q, 1, d, 128, threads=1))
+        else:
+            _same(ref, _ours(mxk, p, n, d, 128, threads=4, chunk=997))
+
+
+def test_csv_reader_fast_path_domain_exhaustive_mantissas(mxk, ref_host, tmp_path):
+    """Mantissas up to 2^53 times every power of ten the fast path takes
+    (1e-22..1e22), plus integers on and next to float rounding midpoints, where
+    rounding the correctly rounded double to float could differ from strtof."""
+    g = np.random.default_rng(7)
+    cells = []
+    for e in range(-22, 23):
+        for m in g.integers(1, 2 ** 53, 40, dtype=np.int64).tolist() + [2 ** 53, 2 ** 53 - 1, 1, 9, 10 ** 15]:
+            cells.append(f"{m}e{e}")
+    for k in range(24, 54):
+        for off in (-1, 0, 1):
+            base = (1 << k) + (1 << (k - 24)) * 1  # float midpoint between 2^k and its successor
+            cells.append(str(base + off))
+            cells.append(str(3 * (1 << k) + (1 << (k - 23)) + off))
+    d = 8
+    while len(cells) % d:
+        cells.append("1")
+    n = len(cells) // d
+    p = tmp_path / "m.csv"
+    with open(p, "w") as f:
+        f.write(",".join("x" * 1 for _ in range(d)) + "\n")
+        for r in range(n):
+            f.write(",".join(cells[r * d:(r + 1) * d]) + "\n")
+    ref = _ref_read(ref_host, p, n, d, 128)
+    got = _ours(mxk, p, n, d, 128, threads=4, chunk=513)
+    if ref[0] == 0:
+        _same(ref, got)
+    else:  # values beyond the float range are rejected: check row by row
+        for r in range(n):
+            q = tmp_path / "row.csv"
+            q.write_text(",".join("x" for _ in range(d)) + "\n" + ",".join(cells[r * d:(r + 1) * d]) + "\n")
+            _same(_ref_read(ref_host, q, 1, d, 128), _ours(mxk, q, 1, d, 128, threads=1))
+
+
+def test_csv_reader_error_row_independent_of_chunking(mxk, ref_host, tmp_path):
+    """Several bad lines in different chunks: the first in file order is the one
+    reported, with the reference's data row number (blank lines not counted)."""
+    g = np.random.default_rng(3)
+    d, n = 5, 3000
+    x = g.standard_normal((n, d)).astype(np.float32)
+    lines = ["a,b,c,d,e"]
+    for r in range(n):
+        lines.append(",".join(repr(float(v)) for v in x[r]))
+        if r % 97 == 0:
+            lines.append("  \r")
+    good = "\n".join(lines) + "\n"
+    p = tmp_path / "ok.csv"
+    p.write_text(good)
+    ref = _ref_read(ref_host, p, n, d, 8)
+    assert ref[0] == 0
+    for threads, chunk in [(1, 0), (8, 64), (5, 1)]:
+        _same(ref, _ours(mxk, p, n, d, 8, threads=threads, chunk=chunk))
+    # n too small / too large
+    for nn in (n - 1, n + 1):
+        _same(_ref_read(ref_host, p, nn, d, 8), _ours(mxk, p, nn, d, 8, threads=8, chunk=64))
+    bad = list(lines)
+    bad[2500] = bad[2500] + ",9"          # wrong column count, late
+    bad[1800] = bad[1800].replace(",", ",1e-41,", 1).rsplit(",", 1)[0]  # denormal, earlier
+    bad[2900] = "1,2,3,4,nan"
+    q = tmp_path / "bad.csv"
+    q.write_text("\n".join(bad) + "\n")
+    ref = _ref_read(ref_host, q, n, d, 8)
+    assert ref[0] == 1 and "Invalid feature" in ref[2]
+    for threads, chunk in [(1, 0), (8, 64), (3, 5)]:
+        _same(ref, _ours(mxk, q, n, d, 8, threads=threads, chunk=chunk))
+
+
+def test_csv_reader_nul_and_binary_junk(mxk, ref_host, tmp_path):
+    p = tmp_path / "nul.csv"
+    p.write_bytes(b"a,b\n1\x00,2\n")
+    _same(_ref_read(ref_host, p, 1, 2, 4), _ours(mxk, p, 1, 2, 4, threads=2, chunk=2))
+    p.write_bytes(b"a,b\n1,2\n\x00\n")
+    _same(_ref_read(ref_host, p, 1, 2, 4), _ours(mxk, p, 1, 2, 4, threads=2, chunk=2))
+    p.write_bytes(b"a,b\n1,2")  # no final newline
+    _same(_ref_read(ref_host, p, 1, 2, 4), _ours(mxk, p, 1, 2, 4, threads=2, chunk=1))
+    d = tmp_path / "dir"
+    d.mkdir()
+    _same(_ref_read(ref_host, d, 1, 2, 4), _ours(mxk, d, 1, 2, 4))
+    _same(_ref_read(ref_host, tmp_path / "missing.csv", 1, 2, 4), _ours(mxk, tmp_path / "missing.csv", 1, 2, 4))
+
+
+# ---- binary float32 input ---------------------------------------------------
+
+def test_f32_reader(mxk, tmp_path):
+    g = np.random.default_rng(5)
+    n, d = 1001, 96
+    x = g.standard_normal((n, d)).astype(np.float32)
+    x[3, 4] = -0.0
+    p = tmp_path / "pts.f32"
+    x.astype("<f4").tofile(p)
+    got = mxk.host_read_points_f32(p, n, d, 128)
+    assert np.array_equal(got[:, :d].view(np.uint32), x.view(np.uint32))
+    assert not got[:, d:].any()
+    assert np.array_equal(mxk.host_read_points_f32(p, n, d, d), x)
+    with pytest.raises(ValueError, match="exactly n \\* d float32"):
+        mxk.host_read_points_f32(p, n + 1, d, 128)
+    x[700, 5] = np.nan
+    x[900, 0] = np.inf
+    x.tofile(p)
+    with pytest.raises(ValueError, match="Invalid feature at data row 701, column 6"):
+        mxk.host_read_points_f32(p, n, d, 128)
+    with pytest.raises(ValueError, match="Cannot open input"):
+        mxk.host_read_points_f32(tmp_path / "none.f32", n, d, 128)
