@@ -41,12 +41,23 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 // Launch bookkeeping: counts every kernel this library launches and, when
 // profiling is on, brackets the launch with CUDA events on its stream.
+// Around each kernel launch: counts it, times it on its stream with CUDA
+// events while profiling is on (mxk_profile_enable), and marks it with an NVTX
+// range of the kernel's name for timeline tools (a no-op without one attached).
 struct LaunchScope {
     LaunchScope(const char* name, cudaStream_t stream);
     ~LaunchScope();
     const char* name;
     cudaStream_t stream;
     cudaEvent_t start = nullptr, stop = nullptr;
+};
+
+// An NVTX range for a host-side phase (one Lloyd call, one iteration).
+struct PhaseRange {
+    explicit PhaseRange(const char* name);
+    ~PhaseRange();
+    PhaseRange(const PhaseRange&) = delete;
+    PhaseRange& operator=(const PhaseRange&) = delete;
 };
 
 // Device-wide error word: kernels with bounded waits set it on timeout.

@@ -155,6 +155,7 @@ struct LoopMirror {
 int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
               const mxk_options* options, int* iterations, cudaStream_t stream, bool cache_points = false) {
     MXK_REQUIRE(options && iterations, "kmeans_mixed: null options or iterations");
+    PhaseRange call_range("kmeans_mixed");
     MXK_REQUIRE(k > 0 && d > 0 && n >= 0, "kmeans_mixed: require n >= 0, d > 0, k > 0");
     MXK_REQUIRE(d % 128 == 0, "kmeans_mixed: d must be padded to a multiple of 128");
     MXK_REQUIRE(points || n == 0, "kmeans_mixed: null points");
@@ -264,6 +265,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
     bool cached_stale = true;  // the gathered copy of the cached rows does not follow the current order
     for (int it = 0; it < options->max_iterations; ++it) {
+        PhaseRange iteration_range("lloyd_iteration");
         // From the second iteration on, visit points grouped by their label of
         // the previous (or, every other iteration, the one before) iteration
         // (order.cu); the first iteration keeps ascending point order.

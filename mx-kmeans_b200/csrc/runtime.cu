@@ -7,6 +7,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "common.cuh"
 
 namespace mxk {
@@ -68,6 +70,7 @@ int fail_cuda(const char* what, cudaError_t err) {
 void clear_error() { g_last_error.clear(); }
 
 LaunchScope::LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
+    nvtxRangePushA(n);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (g_profiling.load(std::memory_order_relaxed)) {
         if (cudaEventCreate(&start) == cudaSuccess && cudaEventCreate(&stop) == cudaSuccess)
@@ -85,7 +88,11 @@ LaunchScope::~LaunchScope() {
         std::lock_guard<std::mutex> lock(g_mutex);
         g_pending.push_back(PendingTiming{dev, name, start, stop});
     }
+    nvtxRangePop();
 }
+
+PhaseRange::PhaseRange(const char* name) { nvtxRangePushA(name); }
+PhaseRange::~PhaseRange() { nvtxRangePop(); }
 
 unsigned* device_error_word() {
     int dev = 0;
