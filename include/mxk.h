@@ -193,6 +193,15 @@ int mxk_comm_destroy(void* comm);
 int mxk_kmeans_mixed_sharded(void* comm, int64_t n_local, int d, int k, const float* points,
                              float* centroids, int* labels, const mxk_options* options,
                              int* iterations, void* stream);
+/* kmeans_mixed over num_gpus GPUs of this node (devices 0..num_gpus-1) from
+ * HOST buffers: points n x d (d as kmeans_mixed), centroids k x d in/out,
+ * labels n out.  Rows are split into contiguous shards (n / num_gpus each, the
+ * first n % num_gpus one more), one host thread per GPU, centroids replicated,
+ * sums and counts all-reduced each iteration (mxk_kmeans_mixed_sharded); with
+ * num_gpus == 1 it is mxk_kmeans_mixed on device 0.  Blocking; restores the
+ * caller's current device. */
+int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                           const mxk_options* options, int num_gpus, int* iterations);
 
 /* ---- host-side helpers of the CLI (include/host_utils.hpp:40-141) -------- */
 

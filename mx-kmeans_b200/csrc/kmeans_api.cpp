@@ -4,6 +4,7 @@
 #include <string>
 
 #include "kmeans.cuh"
+#include "kmeans_multi.cuh"
 #include "mxk.h"
 
 namespace {
@@ -20,6 +21,14 @@ int kmeans_mixed(int n, int d, int k, const float* points, float* centroids, int
     mxk_options o{options.max_iterations, options.fp32_iterations, options.tolerance, options.verbose ? 1 : 0};
     int iterations = 0;
     throw_on(mxk_kmeans_mixed(n, d, k, points, centroids, labels, &o, &iterations, nullptr));
+    return iterations;
+}
+
+int kmeans_mixed_multi(int64_t n, int d, int k, const float* host_points, float* host_centroids, int* host_labels,
+                       const KMeansOptions& options, int num_gpus) {
+    mxk_options o{options.max_iterations, options.fp32_iterations, options.tolerance, options.verbose ? 1 : 0};
+    int iterations = 0;
+    throw_on(mxk_kmeans_mixed_multi(n, d, k, host_points, host_centroids, host_labels, &o, num_gpus, &iterations));
     return iterations;
 }
 

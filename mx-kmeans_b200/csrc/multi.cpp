@@ -1,0 +1,158 @@
+// kmeans_mixed over several GPUs of this node from host buffers: the
+// "kmeans_mixed_multi" entry of the multi-GPU path (the reference,
+// ParCIS/MX-KMeans src/kmeans.cu:12-68, runs on one GPU only).
+//
+// Rows are split into contiguous shards (n / G rows each, the first n % G
+// shards one more), shard g lives on device g, centroids are replicated, and
+// every Lloyd iteration all-reduces the K x D sums and K counts over NCCL
+// (mxk_kmeans_mixed_sharded).  One host thread drives each GPU.  Uploads run
+// first on every GPU; the communicator is created only once all of them have
+// succeeded, so a failed upload or allocation cannot leave the other ranks
+// waiting in NCCL initialisation.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "mxk.h"
+
+namespace mxk {
+int fail(int status, const std::string& message);
+}
+
+namespace {
+
+struct Shard {
+    int device = 0;
+    int64_t row0 = 0, rows = 0;
+    cudaStream_t stream = nullptr;
+    float* points = nullptr;
+    float* centroids = nullptr;
+    int* labels = nullptr;
+    void* comm = nullptr;
+    int iterations = 0;
+    int status = MXK_OK;
+    std::string error;
+
+    bool record(int st) {
+        if (st == MXK_OK) return true;
+        status = st;
+        error = mxk_last_error();
+        return false;
+    }
+    bool record_cuda(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        status = MXK_ERR_CUDA;
+        error = std::string(what) + ": " + cudaGetErrorString(e);
+        return false;
+    }
+    void release() {
+        if (cudaSetDevice(device) != cudaSuccess) return;
+        if (comm) mxk_comm_destroy(comm);
+        if (points) cudaFree(points);
+        if (centroids) cudaFree(centroids);
+        if (labels) cudaFree(labels);
+        if (stream) cudaStreamDestroy(stream);
+        comm = nullptr;
+        points = centroids = nullptr;
+        labels = nullptr;
+        stream = nullptr;
+    }
+};
+
+template <class F>
+void on_every_gpu(std::vector<Shard>& shards, F&& body) {
+    std::vector<std::thread> threads;
+    threads.reserve(shards.size());
+    for (auto& s : shards) threads.emplace_back([&body, &s] { body(s); });
+    for (auto& t : threads) t.join();
+}
+
+}  // namespace
+
+extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                                      const mxk_options* options, int num_gpus, int* iterations) {
+    if (!points || !centroids || !labels || !options || !iterations)
+        return mxk::fail(MXK_ERR_INVALID, "kmeans_mixed_multi: null pointer");
+    if (n <= 0 || d <= 0 || k <= 0 || num_gpus < 1)
+        return mxk::fail(MXK_ERR_INVALID, "kmeans_mixed_multi: require n > 0, d > 0, k > 0 and num_gpus >= 1");
+    int visible = 0;
+    if (cudaGetDeviceCount(&visible) != cudaSuccess) {
+        cudaGetLastError();
+        return mxk::fail(MXK_ERR_CUDA, "kmeans_mixed_multi: no CUDA device");
+    }
+    if (num_gpus > visible) return mxk::fail(MXK_ERR_INVALID, "kmeans_mixed_multi: num_gpus exceeds the visible GPUs");
+    int caller_device = 0;
+    cudaGetDevice(&caller_device);
+
+    const int G = num_gpus;
+    const size_t centroid_bytes = sizeof(float) * size_t(k) * size_t(d);
+    std::vector<Shard> shards(static_cast<size_t>(G));
+    for (int g = 0; g < G; ++g) {
+        Shard& s = shards[size_t(g)];
+        s.device = g;
+        s.row0 = n / G * g + std::min<int64_t>(g, n % G);
+        s.rows = n / G + (g < n % G ? 1 : 0);
+    }
+
+    // Phase 1: allocate and upload the shard and the initial centroids.
+    on_every_gpu(shards, [&](Shard& s) {
+        const size_t rows = size_t(std::max<int64_t>(s.rows, 1));
+        if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice") ||
+            !s.record_cuda(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
+            !s.record_cuda(cudaMalloc(&s.points, sizeof(float) * rows * size_t(d)), "cudaMalloc") ||
+            !s.record_cuda(cudaMalloc(&s.centroids, centroid_bytes), "cudaMalloc") ||
+            !s.record_cuda(cudaMalloc(&s.labels, sizeof(int) * rows), "cudaMalloc"))
+            return;
+        if (!s.record_cuda(cudaMemcpyAsync(s.points, points + size_t(s.row0) * size_t(d),
+                                           sizeof(float) * size_t(s.rows) * size_t(d), cudaMemcpyHostToDevice,
+                                           s.stream),
+                           "cudaMemcpyAsync") ||
+            !s.record_cuda(cudaMemcpyAsync(s.centroids, centroids, centroid_bytes, cudaMemcpyHostToDevice, s.stream),
+                           "cudaMemcpyAsync"))
+            return;
+        s.record_cuda(cudaStreamSynchronize(s.stream), "cudaStreamSynchronize");
+    });
+    bool uploaded = true;
+    for (auto& s : shards) uploaded = uploaded && s.status == MXK_OK;
+
+    // Phase 2 (only when every upload succeeded): communicator, Lloyd, labels.
+    unsigned char uid[128] = {};
+    if (uploaded && G > 1 && mxk_comm_unique_id(uid) != MXK_OK) {
+        shards[0].record(MXK_ERR_COMM);
+        uploaded = false;
+    }
+    if (uploaded) {
+        on_every_gpu(shards, [&](Shard& s) {
+            if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice")) return;
+            if (G > 1) {
+                if (!s.record(mxk_comm_init(&s.comm, G, s.device, uid))) return;
+                if (!s.record(mxk_kmeans_mixed_sharded(s.comm, s.rows, d, k, s.points, s.centroids, s.labels, options,
+                                                       &s.iterations, s.stream)))
+                    return;
+            } else if (!s.record(mxk_kmeans_mixed(s.rows, d, k, s.points, s.centroids, s.labels, options,
+                                                  &s.iterations, s.stream))) {
+                return;
+            }
+            if (!s.record_cuda(cudaMemcpyAsync(labels + s.row0, s.labels, sizeof(int) * size_t(s.rows),
+                                               cudaMemcpyDeviceToHost, s.stream),
+                               "cudaMemcpyAsync"))
+                return;
+            s.record_cuda(cudaStreamSynchronize(s.stream), "cudaStreamSynchronize");
+        });
+    }
+    // Every rank finalizes the centroids identically; rank 0's copy is returned.
+    Shard& first = shards[0];
+    if (uploaded && first.status == MXK_OK)
+        if (first.record_cuda(cudaSetDevice(first.device), "cudaSetDevice"))
+            first.record_cuda(cudaMemcpy(centroids, first.centroids, centroid_bytes, cudaMemcpyDeviceToHost),
+                              "cudaMemcpy");
+    for (auto& s : shards) s.release();
+    cudaSetDevice(caller_device);
+    for (auto& s : shards)
+        if (s.status != MXK_OK) return mxk::fail(s.status, "kmeans_mixed_multi: GPU " + std::to_string(s.device) + ": " + s.error);
+    *iterations = first.iterations;
+    return MXK_OK;
+}

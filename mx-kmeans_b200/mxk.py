@@ -71,6 +71,7 @@ SIGNATURES = {
     "mxk_comm_init": ([ctypes.POINTER(_P), _I, _I, ctypes.c_char_p], _I),
     "mxk_comm_destroy": ([_P], _I),
     "mxk_kmeans_mixed_sharded": ([_P, _I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
+    "mxk_kmeans_mixed_multi": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), _I, ctypes.POINTER(_I)], _I),
     "mxk_host_init_kmeanspp": ([_P, _I64, _I, _I, ctypes.c_uint32, _P], _I),
     "mxk_host_init_farthest": ([_P, _I64, _I, _I, _P], _I),
     "mxk_host_read_points": ([ctypes.c_char_p, _I64, _I, _I, _P], _I),
@@ -293,6 +294,20 @@ def profile_read():
 
 def _np(a):
     return ctypes.c_void_p(a.ctypes.data)
+
+
+def kmeans_mixed_multi(points, centroids, labels, options, num_gpus):
+    """kmeans_mixed over num_gpus GPUs of this node from HOST numpy arrays
+    (points n x d float32, centroids k x d float32 in/out, labels n int32 out)."""
+    import numpy as np
+    for a, t in ((points, np.float32), (centroids, np.float32), (labels, np.int32)):
+        if a.dtype != t or not a.flags.c_contiguous:
+            raise TypeError("kmeans_mixed_multi: contiguous float32 points/centroids and int32 labels required")
+    it = ctypes.c_int(0)
+    check(load().mxk_kmeans_mixed_multi(points.shape[0], points.shape[1], centroids.shape[0], _np(points),
+                                        _np(centroids), _np(labels), ctypes.byref(options), num_gpus,
+                                        ctypes.byref(it)))
+    return it.value
 
 
 def host_init_kmeanspp(points, k, seed):

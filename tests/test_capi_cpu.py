@@ -47,8 +47,24 @@ def test_cpp_dropin_symbols(mxk):
                 "assign_precisions(int, int, float const*, float const*, float, float, int*)",
                 "quantize_rows(int, int, int, float const*, int const*, void*, Scale*, float*)",
                 "gemm_fp32(int, int, int, float const*, float const*, float*)",
-                "gemm_mx(int, int, int, int, void const*, Scale const*, MXFP8 const*, Scale const*, float*)"]:
+                "gemm_mx(int, int, int, int, void const*, Scale const*, MXFP8 const*, Scale const*, float*)",
+                # additive multi-GPU entry (include/kmeans_multi.cuh)
+                "kmeans_mixed_multi(long, int, int, float const*, float*, int*, KMeansOptions const&, int)"]:
         assert sig in out, f"C++ drop-in symbol missing: {sig}"
+
+
+def test_multi_gpu_entry_validates_before_cuda(mxk):
+    import numpy as np
+    lib = mxk.load()
+    it = mxk.ctypes.c_int(0)
+    opts = mxk.Options(max_iterations=1, tolerance=0.0)
+    st = lib.mxk_kmeans_mixed_multi(4, 128, 4, None, None, None, mxk.ctypes.byref(opts), 1, mxk.ctypes.byref(it))
+    assert st == mxk.ERR_INVALID and b"null pointer" in lib.mxk_last_error()
+    x = np.zeros((8, 128), np.float32)
+    c = np.zeros((4, 128), np.float32)
+    lab = np.zeros(8, np.int32)
+    with pytest.raises(ValueError, match="num_gpus >= 1"):
+        mxk.kmeans_mixed_multi(x, c, lab, opts, 0)
 
 
 def test_errors_are_reported_without_a_gpu(mxk):

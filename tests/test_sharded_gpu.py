@@ -1,4 +1,5 @@
-"""Row-sharded kmeans_mixed over NCCL on two GPUs (skipped with fewer).
+"""Row-sharded kmeans_mixed over NCCL on two GPUs (skipped with fewer), and the
+host-buffer multi-GPU entry kmeans_mixed_multi on one and two GPUs.
 
 Each rank runs mxk.kmeans_mixed_sharded on its contiguous shard; rank 0 also runs
 the single-GPU kmeans_mixed on all points from the same initial centroids.  The
@@ -60,3 +61,27 @@ def test_two_gpu_sharded_matches_single_gpu(n, d, k, seed, iters):
     assert np.array_equal(out[0]["cent"], out[1]["cent"])
     assert np.array_equal(out[0]["cent"], single_cent)
     assert np.array_equal(labels, single_labels)
+
+
+@pytest.mark.parametrize("gpus", [1, 2])
+def test_multi_entry_matches_single_gpu(torch_cuda, mxk, gpus):
+    """mxk_kmeans_mixed_multi (host buffers, one thread per GPU, NCCL inside the
+    library) against kmeans_mixed on one GPU: bit-identical on integer data."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < gpus:
+        pytest.skip(f"needs {gpus} GPUs")
+    n, d, k, seed, iters = 20011, 128, 40, 9, 8
+    x, c0 = _blob_data(n, d, k, seed)
+    opts = mxk.Options(max_iterations=iters, tolerance=0.0)
+    xf = torch.from_numpy(x).cuda()
+    cf = torch.from_numpy(c0).cuda()
+    lf = torch.empty(n, dtype=torch.int32, device="cuda")
+    single_iters = mxk.kmeans_mixed(xf, cf, lf, opts)
+    torch.cuda.synchronize()
+    cent = np.ascontiguousarray(c0.copy())
+    labels = np.full(n, -1, np.int32)
+    it = mxk.kmeans_mixed_multi(np.ascontiguousarray(x), cent, labels, opts, gpus)
+    assert it == single_iters
+    assert np.array_equal(labels, lf.cpu().numpy())
+    assert np.array_equal(cent, cf.cpu().numpy())
+    assert torch.cuda.current_device() == 0
