@@ -49,6 +49,7 @@ struct LaunchScope {
     ~LaunchScope();
     const char* name;
     cudaStream_t stream;
+    int device = 0;
     cudaEvent_t start = nullptr, stop = nullptr;
 };
 

@@ -132,7 +132,8 @@ constexpr int kLookahead = 8;
 constexpr int kResortEvery = 2;
 
 // Pinned host copies of the loop state words (one slot per iteration in flight)
-// and the events that say when each copy has landed.
+// and the events that say when each copy has landed.  Leased per call from a
+// per-device pool (MirrorLease) and kept until exit.
 struct LoopMirror {
     int* host = nullptr;
     cudaEvent_t ev[kLookahead + 1] = {};
@@ -150,6 +151,54 @@ struct LoopMirror {
         for (cudaEvent_t& e : ev) MXK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         return MXK_OK;
     }
+};
+
+// Pinned memory and events are allocated once per device and reused by later
+// calls: allocating them takes driver locks that another process (an NVML
+// client such as nvidia-smi) can hold for tens of milliseconds, longer than the
+// iterations enqueued ahead cover, so a per-call allocation could leave the GPU
+// idle.
+std::mutex g_mirror_mutex;
+std::vector<LoopMirror*> g_mirror_pool[64];
+
+struct MirrorLease {
+    LoopMirror* m = nullptr;
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    int acquire(cudaStream_t s) {
+        stream = s;
+        MXK_CUDA(cudaGetDevice(&device));
+        if (device < 0 || device >= 64) return fail(MXK_ERR_CUDA, "kmeans_mixed: device ordinal out of range");
+        {
+            std::lock_guard<std::mutex> lock(g_mirror_mutex);
+            if (!g_mirror_pool[device].empty()) {
+                m = g_mirror_pool[device].back();
+                g_mirror_pool[device].pop_back();
+                return MXK_OK;
+            }
+        }
+        auto* fresh = new LoopMirror;
+        const int st = fresh->init();
+        if (st != MXK_OK) {
+            delete fresh;
+            return st;
+        }
+        m = fresh;
+        return MXK_OK;
+    }
+    ~MirrorLease() {
+        if (!m) return;
+        // After an error return, copies from and into the slots can still be in
+        // flight on the stream; the next call must not reuse the slots before.
+        if (cudaStreamSynchronize(stream) != cudaSuccess) {
+            cudaGetLastError();
+            for (cudaEvent_t e : m->ev)
+                if (e) cudaEventSynchronize(e);
+        }
+        std::lock_guard<std::mutex> lock(g_mirror_mutex);
+        g_mirror_pool[device].push_back(m);
+    }
+    LoopMirror* operator->() const { return m; }
 };
 
 int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
@@ -238,12 +287,12 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     }
     int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)
     MXK_CHECK(ws.alloc(&loop, 4));
-    LoopMirror mirror;
-    MXK_CHECK(mirror.init());
-    mirror.host[0] = mirror.host[1] = mirror.host[2] = 0;
-    mirror.host[3] = (int)n;
+    MirrorLease mirror;
+    MXK_CHECK(mirror.acquire(stream));
+    mirror->host[0] = mirror->host[1] = mirror->host[2] = 0;
+    mirror->host[3] = (int)n;
     // (slot 0 is next written by iteration 0's state copy, after this one in stream order)
-    MXK_CUDA(cudaMemcpyAsync(loop, mirror.host, sizeof(int) * 4, cudaMemcpyHostToDevice, stream));
+    MXK_CUDA(cudaMemcpyAsync(loop, mirror->host, sizeof(int) * 4, cudaMemcpyHostToDevice, stream));
     float* dots = nullptr;
     int64_t chunk_rows = 0;
     if (options->fp32_iterations > 0 && n > 0) {
@@ -379,8 +428,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         }
         MXK_CHECK(launch_finalize(d, k, sums, counts, prev, centroids, shift, stream, loop, options->tolerance));
         const int slot = it % (kLookahead + 1);
-        MXK_CUDA(cudaMemcpyAsync(mirror.host + 4 * slot, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
-        MXK_CUDA(cudaEventRecord(mirror.ev[slot], stream));
+        MXK_CUDA(cudaMemcpyAsync(mirror->host + 4 * slot, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+        MXK_CUDA(cudaEventRecord(mirror->ev[slot], stream));
         // Read the state of iteration it - lookahead.  FP32 iterations (whose
         // kernels do not consult the stop word) and verbose runs are read at once,
         // so no FP32 iteration is ever enqueued after the loop has stopped.
@@ -388,15 +437,15 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         const int seen = it - lookahead;
         if (seen >= 0) {
             const int sslot = seen % (kLookahead + 1);
-            MXK_CUDA(cudaEventSynchronize(mirror.ev[sslot]));
-            if (mirror.host[4 * sslot]) break;  // stopped at or before iteration `seen`
+            MXK_CUDA(cudaEventSynchronize(mirror->ev[sslot]));
+            if (mirror->host[4 * sslot]) break;  // stopped at or before iteration `seen`
         }
     }
-    MXK_CUDA(cudaMemcpyAsync(mirror.host, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+    MXK_CUDA(cudaMemcpyAsync(mirror->host, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
     MXK_CUDA(cudaStreamSynchronize(stream));
     MXK_CHECK(check_device_error(stream));
-    if (mirror.host[2]) return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");
-    *iterations = mirror.host[1];
+    if (mirror->host[2]) return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");
+    *iterations = mirror->host[1];
     return MXK_OK;
 }
 

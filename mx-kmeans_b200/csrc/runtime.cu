@@ -1,6 +1,7 @@
 // Host runtime of libmxkmeans: error reporting, launch accounting and kernel
 // timing, the per-device error word, and tensor-map encoding.
 #include <atomic>
+#include <deque>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -32,28 +33,74 @@ struct KernelStat {
 };
 
 std::mutex g_mutex;
-std::vector<PendingTiming> g_pending;
+std::deque<PendingTiming> g_pending;
 std::vector<KernelStat> g_stats;
 unsigned* g_error_words[64] = {};
+// Timing events of finished launches, per device, reused by later launches:
+// creating events can wait on driver locks that another process (an NVML
+// client such as nvidia-smi) holds for milliseconds, which would stall the
+// enqueueing thread on every launch while profiling.
+std::vector<cudaEvent_t> g_event_pool[64];
 
-void drain_pending_locked() {
-    for (auto& p : g_pending) {
-        float ms = 0.0f;
-        if (cudaEventSynchronize(p.stop) == cudaSuccess && cudaEventElapsedTime(&ms, p.start, p.stop) == cudaSuccess) {
-            KernelStat* st = nullptr;
-            for (auto& s : g_stats)
-                if (s.device == p.device && s.name == p.name) st = &s;
-            if (!st) {
-                g_stats.push_back(KernelStat{p.device, p.name});
-                st = &g_stats.back();
-            }
-            st->launches += 1;
-            st->total_ms += ms;
+bool take_events_locked(int device, cudaEvent_t* a, cudaEvent_t* b) {
+    auto& pool = g_event_pool[device];
+    for (cudaEvent_t* e : {a, b}) {
+        if (!pool.empty()) {
+            *e = pool.back();
+            pool.pop_back();
+        } else if (cudaEventCreate(e) != cudaSuccess) {
+            cudaGetLastError();
+            *e = nullptr;
         }
+    }
+    if (*a && *b) return true;
+    if (*a) pool.push_back(*a);
+    if (*b) pool.push_back(*b);
+    *a = *b = nullptr;
+    return false;
+}
+
+// Adds a finished launch's time to the statistics and recycles its events.
+void account_locked(const PendingTiming& p) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, p.start, p.stop) == cudaSuccess) {
+        KernelStat* st = nullptr;
+        for (auto& s : g_stats)
+            if (s.device == p.device && s.name == p.name) st = &s;
+        if (!st) {
+            g_stats.push_back(KernelStat{p.device, p.name});
+            st = &g_stats.back();
+        }
+        st->launches += 1;
+        st->total_ms += ms;
+        g_event_pool[p.device].push_back(p.start);
+        g_event_pool[p.device].push_back(p.stop);
+    } else {
+        cudaGetLastError();
         cudaEventDestroy(p.start);
         cudaEventDestroy(p.stop);
     }
+}
+
+// Waits for every pending launch and accounts for it.
+void drain_pending_locked() {
+    for (auto& p : g_pending) {
+        if (cudaEventSynchronize(p.stop) != cudaSuccess) cudaGetLastError();
+        account_locked(p);
+    }
     g_pending.clear();
+}
+
+// Accounts for the launches at the front of the queue that have finished
+// (without waiting), so a long profiled run keeps reusing a bounded set of events.
+void harvest_finished_locked() {
+    while (!g_pending.empty()) {
+        const cudaError_t e = cudaEventQuery(g_pending.front().stop);
+        if (e == cudaErrorNotReady) break;
+        if (e != cudaSuccess) cudaGetLastError();
+        account_locked(g_pending.front());
+        g_pending.pop_front();
+    }
 }
 }  // namespace
 
@@ -73,20 +120,21 @@ LaunchScope::LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
     nvtxRangePushA(n);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (g_profiling.load(std::memory_order_relaxed)) {
-        if (cudaEventCreate(&start) == cudaSuccess && cudaEventCreate(&stop) == cudaSuccess)
-            cudaEventRecord(start, stream);
-        else
-            start = stop = nullptr;
+        bool ok = cudaGetDevice(&device) == cudaSuccess && device >= 0 && device < 64;
+        if (ok) {
+            std::lock_guard<std::mutex> lock(g_mutex);
+            if (g_event_pool[device].size() < 2) harvest_finished_locked();
+            ok = take_events_locked(device, &start, &stop);
+        }
+        if (ok) cudaEventRecord(start, stream);
     }
 }
 
 LaunchScope::~LaunchScope() {
     if (start && stop) {
         cudaEventRecord(stop, stream);
-        int dev = 0;
-        cudaGetDevice(&dev);
         std::lock_guard<std::mutex> lock(g_mutex);
-        g_pending.push_back(PendingTiming{dev, name, start, stop});
+        g_pending.push_back(PendingTiming{device, name, start, stop});
     }
     nvtxRangePop();
 }
@@ -227,7 +275,24 @@ int mxk_release_workspace(void) {
 int mxk_profile_enable(int on) {
     std::lock_guard<std::mutex> lock(mxk::g_mutex);
     mxk::drain_pending_locked();
-    if (on) mxk::g_stats.clear();
+    if (on) {
+        mxk::g_stats.clear();
+        // events for the first launches, created here rather than while timing
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+            auto& pool = mxk::g_event_pool[dev];
+            while (pool.size() < 1024) {
+                cudaEvent_t e = nullptr;
+                if (cudaEventCreate(&e) != cudaSuccess) {
+                    cudaGetLastError();
+                    break;
+                }
+                pool.push_back(e);
+            }
+        } else {
+            cudaGetLastError();
+        }
+    }
     mxk::g_profiling.store(on ? 1 : 0);
     return MXK_OK;
 }
