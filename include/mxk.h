@@ -222,6 +222,8 @@ int mxk_host_read_points_ex(const char* path, int64_t n, int d, int padded_d, in
  * n x d little-endian float32 values, row-major, no header, exactly n*d*4
  * bytes; zero padded to padded_d; non-finite values rejected as in the CSV. */
 int mxk_host_read_points_f32(const char* path, int64_t n, int d, int padded_d, float* out);
+/* write_labels, include/host_utils.hpp:69-76: "clusters" then one label per
+ * line, the same bytes as the reference (formatted on all host threads). */
 int mxk_host_write_labels(const char* path, const int* labels, int64_t n);
 
 /* ---- kernel timing (CUDA events around each launch on its stream) ---------- */

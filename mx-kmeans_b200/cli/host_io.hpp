@@ -3,7 +3,8 @@
 // Interface-compatible with ParCIS/MX-KMeans include/host_utils.hpp:1-141:
 //   * CSV input (read on all host threads, same accept/reject rules and
 //     messages): point_reader.hpp;
-//   * labels: "clusters" header, one label per line.
+//   * labels: "clusters" header, one label per line (formatted on all host
+//     threads, same bytes).
 //   * K-Means++ (D^2 sampling with std::mt19937(seed), the first index from
 //     uniform_int_distribution<int>(0, n-1), each next index by a
 //     uniform_real_distribution<double>(0, total) draw against the running sum of
@@ -13,6 +14,7 @@
 #pragma once
 
 #include <algorithm>
+#include <charconv>
 #include <cmath>
 #include <cstdint>
 #include <fstream>
@@ -42,13 +44,41 @@ inline int parse_int(const std::string& text) {
     return v;
 }
 
-inline void write_labels(const std::string& path, const std::vector<int>& labels) {
+// The reference's label file (host_utils.hpp:69-76): "clusters", then one
+// decimal label per line.  The text is formatted on all host threads in blocks
+// (std::to_chars, the same digits as operator<<) and written in order, so the
+// bytes are those of the reference's ofstream loop.
+inline void write_labels(const std::string& path, const int* labels, int64_t n, int threads = 0) {
     std::ofstream out(path);
     if (!out) throw std::runtime_error("Cannot open output: " + path);
     out << "clusters\n";
-    for (int v : labels) out << v << '\n';
+    constexpr int64_t kBlock = int64_t(1) << 20;
+    const int64_t blocks = (n + kBlock - 1) / kBlock;
+    threads = detail::reader_threads(threads);
+    // format a window of blocks in parallel, then write it, to bound memory
+    const int64_t window = std::max<int64_t>(1, threads) * 2;
+    std::vector<std::string> text(size_t(std::min(blocks, window)));
+    for (int64_t b0 = 0; b0 < blocks && out; b0 += window) {
+        const int64_t nb = std::min(window, blocks - b0);
+        detail::parallel_for(int(nb), threads, [&](int i) {
+            const int64_t r0 = (b0 + i) * kBlock, r1 = std::min(n, r0 + kBlock);
+            std::string& t = text[size_t(i)];
+            t.resize(size_t(r1 - r0) * 12);
+            char* p = t.data();
+            for (int64_t r = r0; r < r1; ++r) {
+                p = std::to_chars(p, p + 11, labels[r]).ptr;
+                *p++ = '\n';
+            }
+            t.resize(size_t(p - t.data()));
+        });
+        for (int64_t i = 0; i < nb && out; ++i) out.write(text[size_t(i)].data(), std::streamsize(text[size_t(i)].size()));
+    }
     out.close();
     if (!out) throw std::runtime_error("Failed to write output: " + path);
+}
+
+inline void write_labels(const std::string& path, const std::vector<int>& labels) {
+    write_labels(path, labels.data(), int64_t(labels.size()));
 }
 
 // Squared distance of row p to a center, accumulated in double.

@@ -69,7 +69,7 @@ int mxk_host_read_points_f32(const char* path, int64_t n, int d, int padded_d, f
 int mxk_host_write_labels(const char* path, const int* labels, int64_t n) {
     if (!path || (!labels && n > 0)) return mxk::fail(MXK_ERR_INVALID, "write_labels: bad arguments");
     try {
-        mxk_cli::write_labels(path, std::vector<int>(labels, labels + n));
+        mxk_cli::write_labels(path, labels, n);
         return MXK_OK;
     } catch (const std::exception& e) {
         return mxk::fail(MXK_ERR_INVALID, e.what());

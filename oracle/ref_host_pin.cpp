@@ -53,3 +53,12 @@ extern "C" int ref_read_points_msg(const char* path, int n, int d, int padded_d,
         return 1;
     }
 }
+// write_labels (host_utils.hpp:69-76); returns 1 when it throws.
+extern "C" int ref_write_labels(const char* path, const int* labels, int64_t n) {
+    try {
+        write_labels(path, std::vector<int>(labels, labels + n));
+        return 0;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}

@@ -300,3 +300,48 @@ def test_f32_reader(mxk, tmp_path):
         mxk.host_read_points_f32(p, n, d, 128)
     with pytest.raises(ValueError, match="Cannot open input"):
         mxk.host_read_points_f32(tmp_path / "none.f32", n, d, 128)
+
+
+# ---- label file -------------------------------------------------------------
+
+_REF_WRITER = r"""
+import ctypes, sys
+lib = ctypes.CDLL(sys.argv[1])
+data = open(sys.argv[2], "rb").read()
+n = len(data) // 4
+arr = (ctypes.c_int * max(n, 1)).from_buffer_copy(data or bytes(4))
+lib.ref_write_labels.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int64]
+sys.exit(lib.ref_write_labels(sys.argv[3].encode(), ctypes.cast(arr, ctypes.c_void_p), n))
+"""
+
+
+def test_label_writer_bytes_match_reference(mxk, orc, ref_host, tmp_path):
+    """Labels formatted on several threads in blocks: the file is byte for byte
+    the reference's ofstream output (header, one decimal label per line),
+    including negative and extreme values and sizes across block boundaries.
+    The reference's writer runs in a child process that loads nothing but
+    ctypes and the reference library (in a process that has loaded numpy's
+    bundled runtime libraries first, its ofstream faults)."""
+    import subprocess
+    import sys
+    g = np.random.default_rng(1)
+    ref_so = os.path.join(orc.REF_DIR, "libref_host.so")
+    script = tmp_path / "ref_writer.py"
+    script.write_text(_REF_WRITER)
+    for n in (0, 1, 7, (1 << 20) - 1, (1 << 20) + 3, 3 * (1 << 20) + 5):
+        lab = g.integers(0, 2048, n).astype(np.int32)
+        if n > 4:
+            lab[:4] = [np.iinfo(np.int32).min, np.iinfo(np.int32).max, -1, 0]
+        a, b, raw = tmp_path / "ours.csv", tmp_path / "ref.csv", tmp_path / "labels.bin"
+        assert mxk.load().mxk_host_write_labels(str(a).encode(), mxk._np(lab) if n else None, n) == mxk.OK
+        expected = ("clusters\n" + "".join(f"{v}\n" for v in lab.tolist())).encode()
+        assert a.read_bytes() == expected
+        if n < (1 << 21):
+            lab.astype("<i4").tofile(raw)
+            r = subprocess.run([sys.executable, str(script), ref_so, str(raw), str(b)], capture_output=True)
+            assert r.returncode == 0, r.stderr
+            assert a.read_bytes() == b.read_bytes()
+    d = tmp_path / "adir"
+    d.mkdir()
+    assert mxk.load().mxk_host_write_labels(str(d).encode(), None, 0) == mxk.ERR_INVALID
+    assert b"Cannot open output" in mxk.load().mxk_last_error()
