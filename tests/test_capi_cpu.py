@@ -111,3 +111,26 @@ int main() {
                    check=True, timeout=120)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0 and r.stdout.strip() == "0"
+
+
+def test_missing_library_fails_loudly(mxk, tmp_path):
+    """No fallback: without the built library the binding raises instead of
+    computing anything another way."""
+    with pytest.raises(FileNotFoundError, match="is not built"):
+        mxk.load(str(tmp_path / "libmxkmeans.so"))
+
+
+def test_product_never_reaches_the_oracle():
+    """The oracle is test infrastructure: nothing in the library, its headers,
+    the CLI or the binding names, imports or links it."""
+    hits = []
+    for base in (os.path.join(ROOT, "mx-kmeans_b200"), os.path.join(ROOT, "include")):
+        for dirpath, _, files in os.walk(base):
+            if "_build" in dirpath:
+                continue
+            for f in files:
+                if f.endswith((".cu", ".cuh", ".cpp", ".hpp", ".h", ".py", "Makefile")):
+                    text = open(os.path.join(dirpath, f), errors="replace").read()
+                    if re.search(r"\boracle\b|liboracle|_ref/", text):
+                        hits.append(os.path.join(dirpath, f))
+    assert not hits, f"product files reference the oracle: {hits}"
