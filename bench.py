@@ -70,6 +70,23 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def update_roofline(stats, rows, peak_gbs):
+    """Achieved HBM bandwidth of the centroid update (the label-run or
+    privatised accumulation pass, one launch per iteration) from its CUDA-event
+    times in `stats` ({kernel: (launches, total_ms)}): algorithmic bytes per
+    launch = each point's FP32 row, its id and its label, rows * (4 D_pad + 8).
+    None when the pass did not run."""
+    launches = sum(stats.get(k, (0, 0.0))[0] for k in ("accumulate_runs", "accumulate_private"))
+    total_ms = sum(stats.get(k, (0, 0.0))[1] for k in ("accumulate_runs", "accumulate_private"))
+    if not launches or total_ms <= 0.0:
+        return None
+    alg_bytes = rows * (4.0 * D_PAD + 8.0)
+    gbs = alg_bytes * launches / (total_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s", "frac": gbs / peak_gbs,
+            "algorithmic_bytes_per_launch": alg_bytes, "ms_per_launch": total_ms / launches,
+            "launches": launches, "kernel": "accumulate_runs"}
+
+
 # ----------------------------------------------------------------------------- data
 
 def make_dataset(torch, n, device):
@@ -411,6 +428,7 @@ def main():
                     "peak_source": f"hbm_gbs, 2 x bf16_tflops_sustained of {pk_kind} MEASURED_PEAKS.json "
                                    "(dense MXFP8 tensor rate is twice BF16)"}
     kernel_ms = {k: {"launches": v[0], "total_ms": round(v[1], 3)} for k, v in sorted(stats.items(), key=lambda kv: -kv[1][1])}
+    update = update_roofline(stats, rows, pk.get("hbm_gbs", 6650.0))
 
     cpu = None
     if rank == 0 and world == 1 and not args.quick:
@@ -425,7 +443,8 @@ def main():
                            "iterations_per_step": iters / args.steps, "parallelism": f"row-shard x{world}",
                            "l2": "inputs (4.3 GB of points per step) larger than the 126 MB L2"},
                 "e2e": e2e,
-                "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+                "gpu_launches": int(launches), "roofline": roofline, "update_roofline": update,
+                "cpu_baseline": cpu, "clocks": clocks,
                 "cached_points": cached,
                 "kernel_ms": kernel_ms}
         print(json.dumps(line), flush=True)

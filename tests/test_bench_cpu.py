@@ -1,0 +1,42 @@
+"""Host-side arithmetic of bench.py (no GPU): the update pass's HBM roofline
+from CUDA-event kernel times, the GEMM traffic read from the committed ncu
+summary, and the peak denominators."""
+import os
+import sys
+
+import pytest
+
+from conftest import ROOT
+
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+def test_update_roofline_arithmetic():
+    rows = bench.N_POINTS
+    stats = {"accumulate_runs": (100, 71.882), "mx_gemm_argmin": (100, 312.5)}
+    r = bench.update_roofline(stats, rows, 6535.4)
+    per_launch = rows * (4.0 * bench.D_PAD + 8.0)
+    assert r["algorithmic_bytes_per_launch"] == per_launch
+    assert r["achieved"] == pytest.approx(per_launch * 100 / 0.071882 / 1e9)
+    assert r["frac"] == pytest.approx(r["achieved"] / 6535.4)
+    assert r["unit"] == "GB/s" and r["bound"] == "hbm" and r["launches"] == 100
+    assert r["ms_per_launch"] == pytest.approx(0.71882)
+    # the privatised variant counts as the same pass
+    r2 = bench.update_roofline({"accumulate_private": (10, 7.1882)}, rows, 6535.4)
+    assert r2["achieved"] == pytest.approx(r["achieved"])
+
+
+def test_update_roofline_absent():
+    assert bench.update_roofline({}, 1000, 6535.4) is None
+    assert bench.update_roofline({"accumulate_runs": (0, 0.0)}, 1000, 6535.4) is None
+
+
+def test_measured_traffic_and_peaks():
+    t = bench.measured_traffic(bench.N_POINTS)
+    assert t is not None and t > 0
+    assert bench.measured_traffic(bench.N_POINTS // 2) == pytest.approx(t / 2)
+    pk, kind = bench.peaks()
+    assert kind in ("measured", "fallback")
+    assert pk["hbm_gbs"] > 0 and pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) > 0
+    assert os.path.exists(os.path.join(ROOT, "profiles", "mx_gemm_argmin_config4.md"))
