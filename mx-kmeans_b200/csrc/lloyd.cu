@@ -29,6 +29,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -38,6 +39,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "precision.hpp"
+#include "watchdog.hpp"
 
 namespace mxk {
 
@@ -49,6 +51,7 @@ struct NcclApi {
     ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
@@ -69,6 +72,7 @@ static NcclApi& nccl() {
         MXK_SYM(CommInitRank, "ncclCommInitRank");
         MXK_SYM(CommDestroy, "ncclCommDestroy");
         MXK_SYM(CommAbort, "ncclCommAbort");
+        MXK_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
         MXK_SYM(AllReduce, "ncclAllReduce");
         MXK_SYM(GroupStart, "ncclGroupStart");
         MXK_SYM(GroupEnd, "ncclGroupEnd");
@@ -85,9 +89,60 @@ static int fail_nccl(const char* what, ncclResult_t r) {
 }
 
 struct Comm {
-    ncclComm_t comm = nullptr;
+    ncclComm_t comm = nullptr;  // null once aborted by the watchdog
     int nranks = 1, rank = 0;
 };
+
+// Seconds without progress after which a sharded run aborts its communicator
+// (environment variable MXK_COMM_TIMEOUT_S; unset or <= 0: wait without limit,
+// as a blocking synchronize does).
+static double comm_timeout_s() {
+    static const double v = [] {
+        const char* e = std::getenv("MXK_COMM_TIMEOUT_S");
+        return e ? std::atof(e) : 0.0;
+    }();
+    return v;
+}
+
+// Waits for ev.  In a sharded run with MXK_COMM_TIMEOUT_S set, polls the event
+// and the communicator's asynchronous error instead (guarded_wait): a failed
+// peer, or no progress within the limit, aborts the communicator -- its
+// collectives in flight then return -- and the call reports an error instead
+// of blocking for good.  An aborted communicator must be destroyed and made
+// again.
+static int wait_event(Comm* comm, cudaEvent_t ev) {
+    const double limit = comm_timeout_s();
+    if (!comm || comm->nranks <= 1 || !comm->comm || limit <= 0.0 || !nccl().CommGetAsyncError ||
+        !nccl().CommAbort) {
+        MXK_CUDA(cudaEventSynchronize(ev));
+        return MXK_OK;
+    }
+    NcclApi& api = nccl();
+    cudaError_t query_error = cudaSuccess;
+    ncclResult_t peer_error = ncclSuccess;
+    const WaitResult r = guarded_wait(
+        [&] {
+            const cudaError_t e = cudaEventQuery(ev);
+            if (e == cudaSuccess) return Probe::kReady;
+            if (e == cudaErrorNotReady) return Probe::kPending;
+            query_error = e;
+            return Probe::kFailed;
+        },
+        [&] {
+            ncclResult_t async = ncclSuccess;
+            const ncclResult_t q = api.CommGetAsyncError(comm->comm, &async);
+            peer_error = q != ncclSuccess ? q : async;
+            return peer_error != ncclSuccess && peer_error != ncclInProgress;
+        },
+        limit, monotonic_seconds, short_pause);
+    if (r == WaitResult::kReady) return MXK_OK;
+    if (r == WaitResult::kFailed) return fail_cuda("cudaEventQuery", query_error);
+    api.CommAbort(comm->comm);
+    comm->comm = nullptr;
+    if (r == WaitResult::kPeerFailed)
+        return fail_nccl("sharded Lloyd: a peer rank failed, communicator aborted", peer_error);
+    return fail(MXK_ERR_TIMEOUT, "sharded Lloyd: no progress within MXK_COMM_TIMEOUT_S seconds, communicator aborted");
+}
 
 // ---------------------------------------------------------------------------
 // Workspace: stream-ordered allocations from the library's per-device pool,
@@ -437,11 +492,15 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         const int seen = it - lookahead;
         if (seen >= 0) {
             const int sslot = seen % (kLookahead + 1);
-            MXK_CUDA(cudaEventSynchronize(mirror->ev[sslot]));
+            MXK_CHECK(wait_event(comm, mirror->ev[sslot]));
             if (mirror->host[4 * sslot]) break;  // stopped at or before iteration `seen`
         }
     }
     MXK_CUDA(cudaMemcpyAsync(mirror->host, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+    if (sharded && comm_timeout_s() > 0.0) {  // the last iterations' collectives, under the watchdog
+        MXK_CUDA(cudaEventRecord(mirror->ev[0], stream));
+        MXK_CHECK(wait_event(comm, mirror->ev[0]));
+    }
     MXK_CUDA(cudaStreamSynchronize(stream));
     MXK_CHECK(check_device_error(stream));
     if (mirror->host[2]) return fail(MXK_ERR_NONFINITE, "Non-finite centroid shift; check the input scale");

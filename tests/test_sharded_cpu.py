@@ -170,3 +170,49 @@ def test_bootstrap_comm_fails_when_a_rank_leaves():
     out = _spawn(_bootstrap, 2, True)
     assert 0 in out and out[0][0] == "error", out
     assert out[0][2] < 60  # ended by the group's timeout, not a hang
+
+
+WATCHDOG_TEST = r'''
+#include <cstdio>
+#include "watchdog.hpp"
+using namespace mxk;
+struct Fake { int polls = 0, ready_at, peer_at; double t = 0.0; };
+static WaitResult run(Fake& f, double limit) {
+    return guarded_wait(
+        [&] { ++f.polls; return f.polls >= f.ready_at ? Probe::kReady : Probe::kPending; },
+        [&] { return f.peer_at > 0 && f.polls >= f.peer_at; },
+        limit, [&] { return f.t; }, [&] { f.t += 0.5; });
+}
+int main() {
+    int bad = 0;
+    { Fake f{0, 1, 0}; bad += run(f, 10.0) != WaitResult::kReady || f.polls != 1; }       // done at once
+    { Fake f{0, 7, 0}; bad += run(f, 10.0) != WaitResult::kReady || f.polls != 7; }       // done after polling
+    { Fake f{0, 1000, 4}; bad += run(f, 10.0) != WaitResult::kPeerFailed || f.polls != 4; } // peer fails first
+    { Fake f{0, 1000, 0}; bad += run(f, 2.0) != WaitResult::kTimedOut || f.t > 2.5; }     // no progress
+    { Fake f{0, 4, 4}; bad += run(f, 10.0) != WaitResult::kReady; }                       // completion wins a tie
+    {   // a failed query is reported as such, not as a timeout
+        int n = 0; double t = 0.0;
+        WaitResult r = guarded_wait([&] { return ++n < 3 ? Probe::kPending : Probe::kFailed; }, [] { return false; },
+                                    10.0, [&] { return t; }, [&] { t += 1.0; });
+        bad += r != WaitResult::kFailed || n != 3;
+    }
+    std::printf("%d\n", bad);
+    return bad != 0;
+}
+'''
+
+
+def test_comm_watchdog_logic(tmp_path):
+    """The sharded loop's opt-in host watchdog (MXK_COMM_TIMEOUT_S): a wait ends
+    ready when the work completes, with a peer failure as soon as the
+    communicator reports one, with a timeout when nothing progresses within the
+    limit, and with the query's own failure otherwise.  Fake probes and clock,
+    so no GPU, NCCL or real failure is involved."""
+    import subprocess
+    src = tmp_path / "w.cpp"
+    src.write_text(WATCHDOG_TEST)
+    exe = tmp_path / "w"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "mx-kmeans_b200", "csrc"), str(src),
+                    "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "0", r.stdout + r.stderr
