@@ -10,7 +10,9 @@
 //     uniform_real_distribution<double>(0, total) draw against the running sum of
 //     double squared distances) and farthest-first (from row 0, float distances,
 //     first maximum).  The draw sequence and the distance arithmetic are kept as
-//     in the reference so a seed selects the same centroids.
+//     in the reference so a seed selects the same centroids; the per-point
+//     distances run on all host threads, the running sum, the draws and the
+//     scans stay sequential.
 #pragma once
 
 #include <algorithm>
@@ -91,6 +93,24 @@ inline double sq_dist_double(const float* row, const float* center, int d) {
     return s;
 }
 
+// body(p0, p1) over contiguous point ranges on all host threads when the pass
+// is large enough to pay for them.  Each point's value is computed by one
+// thread with the sequential arithmetic, so results do not depend on the split.
+template <class F>
+void for_point_blocks(int64_t n, int d, F&& body) {
+    const int threads = detail::reader_threads(0);
+    if (threads <= 1 || n * int64_t(d) < (int64_t(1) << 20)) {
+        body(int64_t(0), n);
+        return;
+    }
+    const int blocks = threads * 4;
+    const int64_t per = (n + blocks - 1) / blocks;
+    detail::parallel_for(blocks, threads, [&](int b) {
+        const int64_t p0 = std::min(n, int64_t(b) * per), p1 = std::min(n, p0 + per);
+        if (p0 < p1) body(p0, p1);
+    });
+}
+
 inline std::vector<float> init_kmeanspp(const std::vector<float>& points, int64_t n, int d, int k, uint32_t seed) {
     std::mt19937 rng(seed);
     std::vector<float> centers(size_t(k) * d);
@@ -101,13 +121,15 @@ inline std::vector<float> init_kmeanspp(const std::vector<float>& points, int64_
         const float* src = points.data() + size_t(pick) * d;
         std::copy(src, src + d, centers.begin() + size_t(c) * d);
         chosen[pick] = 1;
-        double total = 0.0;
         const float* center = centers.data() + size_t(c) * d;
-        for (int64_t p = 0; p < n; ++p) {
-            const double v = sq_dist_double(points.data() + size_t(p) * d, center, d);
-            dist[p] = chosen[p] ? 0.0 : std::min(dist[p], v);
-            total += dist[p];
-        }
+        for_point_blocks(n, d, [&](int64_t p0, int64_t p1) {
+            for (int64_t p = p0; p < p1; ++p) {
+                const double v = sq_dist_double(points.data() + size_t(p) * d, center, d);
+                dist[p] = chosen[p] ? 0.0 : std::min(dist[p], v);
+            }
+        });
+        double total = 0.0;  // in point order, as the reference accumulates it
+        for (int64_t p = 0; p < n; ++p) total += dist[p];
         if (c + 1 == k) break;
         pick = -1;
         if (total > 0.0) {
@@ -139,15 +161,17 @@ inline std::vector<float> init_farthest(const std::vector<float>& points, int64_
     for (int c = 0; c < k; ++c) {
         const float* src = points.data() + size_t(pick) * d;
         std::copy(src, src + d, centers.begin() + size_t(c) * d);
-        for (int64_t p = 0; p < n; ++p) {
-            const float* row = points.data() + size_t(p) * d;
-            float s = 0.0f;
-            for (int j = 0; j < d; ++j) {
-                const float diff = row[j] - src[j];
-                s += diff * diff;
+        for_point_blocks(n, d, [&](int64_t p0, int64_t p1) {
+            for (int64_t p = p0; p < p1; ++p) {
+                const float* row = points.data() + size_t(p) * d;
+                float s = 0.0f;
+                for (int j = 0; j < d; ++j) {
+                    const float diff = row[j] - src[j];
+                    s += diff * diff;
+                }
+                dist[p] = std::min(dist[p], s);
             }
-            dist[p] = std::min(dist[p], s);
-        }
+        });
         dist[pick] = -1.0f;
         pick = std::max_element(dist.begin(), dist.end()) - dist.begin();
     }

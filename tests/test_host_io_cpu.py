@@ -43,7 +43,10 @@ def ref_host(orc):
     return lib
 
 
-@pytest.mark.parametrize("seed,n,d,k", [(1, 1000, 64, 32), (9, 3000, 128, 64), (123, 257, 7, 12)])
+# (the last case is above the size where the per-point distances run on all
+# host threads)
+@pytest.mark.parametrize("seed,n,d,k", [(1, 1000, 64, 32), (9, 3000, 128, 64), (123, 257, 7, 12),
+                                        (5, 20011, 64, 24)])
 def test_init_matches_reference_code(mxk, ref_host, seed, n, d, k):
     g = np.random.default_rng(seed)
     pts = (g.standard_normal((n, d)) * g.uniform(0.1, 10)).astype(np.float32)
