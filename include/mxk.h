@@ -84,6 +84,16 @@ int mxk_assign_precisions(int64_t n, int d, const float* upper, const float* gap
  * disagreements, [1] = smallest disagreeing pattern (all ones when none). */
 int mxk_check_mxfp8_scale_codec(unsigned long long* result, void* stream);
 
+/* Self-check, no reference counterpart: failure detection of the kernels'
+ * bounded waits.  One CTA waits on an mbarrier that nothing arrives on: warp 0
+ * through the bounded wait every pipelined kernel of this library uses, with
+ * limit_cycles (> 0, at most the kernels' own limit of 2^33 cycles), warp 1
+ * with the kernels' own limit, leaving when warp 0's timeout raises the CTA's
+ * abort flag.  outcome: 2 device ints, 1 = that warp's wait completed, 0 = it
+ * gave up.  Returns what a public call reports after such a wait,
+ * MXK_ERR_TIMEOUT, with the device error word cleared for the next call. */
+int mxk_check_wait_timeout(long long limit_cycles, int* outcome, void* stream);
+
 /* gemm_mx, include/kmeans.cuh:46-47 / src/kernels/gemm.cu:348-363.
  * out[m x n] (row-major FP32) = A[m x k] (packed MX{bits}) . B[n x k]^T (MXFP8),
  * scales row-major per 32 features.  tcgen05 block-scaled MMA; k % 128 == 0. */
@@ -182,6 +192,34 @@ int mxk_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centro
 int mxk_kmeans_mixed_cached(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
                             const mxk_options* options, int* iterations, void* stream);
 
+/* Test hook, no counterpart in the reference.  Precision policy of the Lloyd
+ * calls that start after it, process-wide.  0 (default): the reference's
+ * select_precision (include/precision.hpp:20-26), which always returns MXFP8.
+ * 1: the candidate that function computes and discards (precision_candidate,
+ * include/precision.hpp:10-17), so points with a large two-largest distance
+ * gap go to the MXFP4 / MXFP6 groups and the loop runs the reference's
+ * per-precision sequence (src/kmeans.cu:42-57: policy, stable compaction, one
+ * quantize + GEMM + assignment per group).  Other values: MXK_ERR_INVALID. */
+int mxk_set_precision_policy(int policy);
+
+/* Diagnostics, no counterpart in the reference (whose only per-iteration output
+ * is the verbose group-size line, src/kmeans.cu:58-60).  Arms a trace of the
+ * NEXT Lloyd call (mxk_kmeans_mixed, _cached or _sharded) made on the current
+ * device.  For each iteration i < max_iterations that call copies, into the
+ * caller's device buffers (any may be NULL; they must stay valid until the call
+ * returns): centroids + i*k*d <- the centroids iteration i assigns against;
+ * labels + i*n <- the labels it assigns (the shard's rows in a sharded call);
+ * group_sizes + 3*i <- the rows of its MXFP4, MXFP6 and MXFP8 groups (zeros in
+ * an FP32 iteration).  Entries of iterations enqueued after the stopping rule
+ * fired hold the stopped state (the final centroids and labels, empty groups). */
+typedef struct {
+    float* centroids;
+    int* labels;
+    int* group_sizes;
+    int max_iterations;
+} mxk_trace;
+int mxk_trace_next_call(const mxk_trace* trace);
+
 /* ---- multi-GPU (no counterpart in the reference, which is single-GPU) ------ */
 
 /* Row-sharded Lloyd: each rank holds n_local rows; centroids are replicated; per
@@ -190,6 +228,12 @@ int mxk_kmeans_mixed_cached(int64_t n, int d, int k, const float* points, float*
 int mxk_comm_unique_id(unsigned char id[128]);
 int mxk_comm_init(void** comm, int nranks, int rank, const unsigned char id[128]);
 int mxk_comm_destroy(void* comm);
+/* Test hook, no reference counterpart: the sharded Lloyd loop of `rank`
+ * (mxk_kmeans_mixed_sharded, and the ranks of mxk_kmeans_mixed_multi) returns
+ * MXK_ERR_CUDA when it reaches `iteration`, on the host, after the work it has
+ * enqueued has finished: a rank that leaves between steps.  rank < 0 disarms.
+ * Process-wide. */
+int mxk_inject_rank_failure(int rank, int iteration);
 int mxk_kmeans_mixed_sharded(void* comm, int64_t n_local, int d, int k, const float* points,
                              float* centroids, int* labels, const mxk_options* options,
                              int* iterations, void* stream);

@@ -153,13 +153,13 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // word and the CTA-wide abort flag) if the phase does not complete in time or
 // another thread of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned* err_word) {
+                                          unsigned* err_word, long long limit_cycles = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - start > kWaitLimitCycles) {
+        if (clock64() - start > limit_cycles) {
             *abort_flag = 1;
             if (err_word) atomicOr(err_word, 1u << MXK_ERR_TIMEOUT);
             return false;

@@ -42,8 +42,11 @@ int launch_gather_mxfp8_rows(int64_t rows, int d, const uint8_t* src, const uint
 int launch_point_bounds(int64_t n, int d, const float* points, const float* norms, float* upper,
                         cudaStream_t stream);
 // lc/ec either as host values (lc_dev == nullptr) or read from device memory.
+// policy 0: select_precision (the reference's rule, always 8); 1: the candidate
+// precision_candidate returns (mxk_set_precision_policy).
 int launch_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc, float ec,
-                             const float* lc_ec_dev, int* precision, int* group_counts, cudaStream_t stream);
+                             const float* lc_ec_dev, int* precision, int* group_counts, cudaStream_t stream,
+                             int policy = 0);
 // stats[0] = sqrt(max errors), stats[1] = sqrt(max norms)  (src/kmeans.cu:38-41)
 int launch_centroid_stats(int k, const float* errors, const float* norms, float* stats, cudaStream_t stream);
 // Stable per-precision compaction of point ids (src/kmeans.cu:45-52).

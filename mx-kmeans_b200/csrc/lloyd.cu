@@ -22,11 +22,15 @@
 // returned iteration count are those of the iteration that met the rule.
 //
 // The reference's precision policy ignores the two-largest distance gap
-// (include/precision.hpp:20-26), so the driver's fused assignment does not track
-// it; gaps stay at their initial zeros, exactly what select_precision receives
-// in the reference's first iteration and which it never reads.
+// (include/precision.hpp:20-26), so under it the driver's fused assignment does
+// not track the gap and puts every point in the MXFP8 group without running the
+// policy, the point bounds or the compaction (the same groups).  The test hook
+// mxk_set_precision_policy(1) lets precision_candidate's choice stand instead;
+// the driver then runs the reference's full sequence: point bounds, gaps, the
+// policy kernel, the stable compaction and one quantize + GEMM per group.
 #include <dlfcn.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -91,7 +95,17 @@ static int fail_nccl(const char* what, ncclResult_t r) {
 struct Comm {
     ncclComm_t comm = nullptr;  // null once aborted by the watchdog
     int nranks = 1, rank = 0;
+    // Set by mxk_kmeans_mixed_multi, whose ranks are threads of one process: a
+    // flag any rank raises when it fails, so that the others stop waiting for
+    // its collectives (their host waits poll it and abort their communicator).
+    std::atomic<int>* group_failed = nullptr;
 };
+
+// Test hook (mxk_inject_rank_failure): the sharded loop of this rank returns an
+// error on the host when it reaches this iteration, after the work it has
+// enqueued has finished (a rank that leaves between steps).
+static std::atomic<int> g_inject_rank{-1};
+static std::atomic<int> g_inject_iteration{-1};
 
 // Seconds without progress after which a sharded run aborts its communicator
 // (environment variable MXK_COMM_TIMEOUT_S; unset or <= 0: wait without limit,
@@ -110,10 +124,17 @@ static double comm_timeout_s() {
 // collectives in flight then return -- and the call reports an error instead
 // of blocking for good.  An aborted communicator must be destroyed and made
 // again.
+// The same polling (without a time limit unless MXK_COMM_TIMEOUT_S is set)
+// runs whenever the communicator belongs to a group of threads of this process
+// (mxk_kmeans_mixed_multi), which a failed rank signals through its flag.
+static bool polled_waits(const Comm* comm) {
+    return comm && comm->nranks > 1 && comm->comm && (comm_timeout_s() > 0.0 || comm->group_failed) &&
+           nccl().CommGetAsyncError && nccl().CommAbort;
+}
+
 static int wait_event(Comm* comm, cudaEvent_t ev) {
     const double limit = comm_timeout_s();
-    if (!comm || comm->nranks <= 1 || !comm->comm || limit <= 0.0 || !nccl().CommGetAsyncError ||
-        !nccl().CommAbort) {
+    if (!polled_waits(comm)) {
         MXK_CUDA(cudaEventSynchronize(ev));
         return MXK_OK;
     }
@@ -129,6 +150,10 @@ static int wait_event(Comm* comm, cudaEvent_t ev) {
             return Probe::kFailed;
         },
         [&] {
+            if (comm->group_failed && comm->group_failed->load()) {
+                peer_error = ncclRemoteError;
+                return true;
+            }
             ncclResult_t async = ncclSuccess;
             const ncclResult_t q = api.CommGetAsyncError(comm->comm, &async);
             peer_error = q != ncclSuccess ? q : async;
@@ -142,6 +167,31 @@ static int wait_event(Comm* comm, cudaEvent_t ev) {
     if (r == WaitResult::kPeerFailed)
         return fail_nccl("sharded Lloyd: a peer rank failed, communicator aborted", peer_error);
     return fail(MXK_ERR_TIMEOUT, "sharded Lloyd: no progress within MXK_COMM_TIMEOUT_S seconds, communicator aborted");
+}
+
+// ---------------------------------------------------------------------------
+// Precision policy of the Lloyd loop (mxk_set_precision_policy): 0 = the
+// reference's select_precision (always MXFP8), 1 = the candidate it computes
+// and discards, which puts points in the MXFP4/MXFP6 groups.
+
+static std::atomic<int> g_precision_policy{0};
+
+// One-shot per-device trace of the next Lloyd call (mxk_trace_next_call).
+struct TraceRequest {
+    float* centroids = nullptr;
+    int* labels = nullptr;
+    int* group_sizes = nullptr;
+    int max_iterations = 0;
+};
+static std::mutex g_trace_mutex;
+static TraceRequest g_trace[64];
+
+static TraceRequest take_trace(int device) {
+    std::lock_guard<std::mutex> lock(g_trace_mutex);
+    if (device < 0 || device >= 64) return TraceRequest{};
+    const TraceRequest t = g_trace[device];
+    g_trace[device] = TraceRequest{};
+    return t;
 }
 
 // ---------------------------------------------------------------------------
@@ -275,12 +325,17 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     int *precision = nullptr, *ids = nullptr, *gcount = nullptr, *cscratch = nullptr, *counts = nullptr;
     uint8_t *qpoints = nullptr, *pscales = nullptr, *qcent = nullptr, *cscales = nullptr;
     // With the forced-MXFP8 policy the precision inputs and groups are not
-    // needed (see kSelectPrecisionIsForcedMxfp8); the general path keeps them.
-    constexpr bool kForced8 = kSelectPrecisionIsForcedMxfp8;
+    // needed (see kSelectPrecisionIsForcedMxfp8); the general path keeps them
+    // and runs when mxk_set_precision_policy selects the candidate rule.
+    const int policy = g_precision_policy.load();
+    const bool forced8 = kSelectPrecisionIsForcedMxfp8 && policy == 0;
+    int device = 0;
+    MXK_CUDA(cudaGetDevice(&device));
+    const TraceRequest trace = take_trace(device);
     MXK_REQUIRE(n < (1ll << 31), "kmeans_mixed: n must be below 2^31");
     MXK_CHECK(ws.alloc(&pnorm, n));
     MXK_CHECK(ws.alloc(&gaps, n));
-    if (!kForced8) {
+    if (!forced8) {
         MXK_CHECK(ws.alloc(&upper, ((n + 31) / 32) * 96));
         MXK_CHECK(ws.alloc(&precision, n));
         MXK_CHECK(ws.alloc(&ids, 3 * n));
@@ -294,20 +349,20 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     // never change, so they are quantized once per call and only regathered
     // when the visiting order changes (the reference re-quantizes every
     // iteration; the results are the same).
-    const bool cache = cache_points && kForced8;
+    const bool cache = cache_points && forced8;
     uint8_t *qnat = nullptr, *snat = nullptr;
     if (cache) {
         MXK_CHECK(ws.alloc(&qnat, n * d));
         MXK_CHECK(ws.alloc(&snat, n * d / 32));
     }
     // (the fused quantize at d = 128 never materializes the MXFP8 point rows)
-    const bool need_qpoints = !kForced8 || d != 128 || cache;
+    const bool need_qpoints = !forced8 || d != 128 || cache;
     if (need_qpoints) {
         MXK_CHECK(ws.alloc(&qpoints, n * d));
         MXK_CHECK(ws.alloc(&pscales, scale_atom_bytes(n, d)));
     }
     MXK_CHECK(ws.alloc(&cnorm, k));
-    if (!kForced8) {
+    if (!forced8) {
         MXK_CHECK(ws.alloc(&cerr, k));
         MXK_CHECK(ws.alloc(&stats, 2));
     }
@@ -322,7 +377,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
     // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
     // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
-    const bool prune = kForced8 && n > 0 && prune_supported(k, d);
+    const bool prune = forced8 && n > 0 && prune_supported(k, d);
     const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *gram = nullptr;
     float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
@@ -362,13 +417,24 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     else
         MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
     if (cache) MXK_CHECK(launch_quantize(8, n, d, points, nullptr, qnat, snat, nullptr, nullptr, stream, 0));
-    if (!kForced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
+    if (!forced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
 
     const bool sharded = comm && comm->nranks > 1;
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+    if (sharded && !comm->comm)
+        return fail(MXK_ERR_COMM, "kmeans_mixed_sharded: the communicator was aborted; destroy and re-create it");
+    const int inject_at = sharded && comm->rank == g_inject_rank.load() ? g_inject_iteration.load() : -1;
     bool cached_stale = true;  // the gathered copy of the cached rows does not follow the current order
     for (int it = 0; it < options->max_iterations; ++it) {
+        if (it == inject_at) {
+            // the injected failure: drain what this rank has enqueued (its peers
+            // take part in those collectives), then leave between steps
+            MXK_CUDA(cudaEventRecord(mirror->ev[kLookahead], stream));
+            MXK_CHECK(wait_event(comm, mirror->ev[kLookahead]));
+            return fail(MXK_ERR_CUDA, "injected rank failure (mxk_inject_rank_failure) at iteration " +
+                                          std::to_string(it));
+        }
         PhaseRange iteration_range("lloyd_iteration");
         // From the second iteration on, visit points grouped by their label of
         // the previous (or, every other iteration, the one before) iteration
@@ -394,6 +460,12 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
                                        loop, stream));
         MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
+        const bool traced = it < trace.max_iterations;
+        if (traced && trace.centroids)
+            MXK_CUDA(cudaMemcpyAsync(trace.centroids + (int64_t)it * kd, centroids, sizeof(float) * kd,
+                                     cudaMemcpyDeviceToDevice, stream));
+        if (traced && trace.group_sizes)  // FP32 iterations record no MX groups
+            MXK_CUDA(cudaMemsetAsync(trace.group_sizes + 3 * it, 0, sizeof(int) * 3, stream));
         if (it < options->fp32_iterations) {
             // kmeans.cu:31-34: FP32 product, assignment without pid (gap init -1).
             for (int64_t r0 = 0; r0 < n; r0 += chunk_rows) {
@@ -404,7 +476,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             }
             if (options->verbose && (!comm || comm->rank == 0))
                 std::fprintf(stderr, "iteration=%d precision=FP32\n", it + 1);
-        } else if (kForced8) {
+        } else if (forced8) {
             // Every point is in the MXFP8 group, in the visiting sequence `ord`;
             // the group's row count is loop[3] (n, or 0 once the loop stopped).
             MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
@@ -434,6 +506,9 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.best_dist_stride = 4;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, loop + 3, stream,
                                      true, fused_q ? points : nullptr, n));
+            if (traced && trace.group_sizes)  // (0, 0, rows of the MXFP8 group)
+                MXK_CUDA(cudaMemcpyAsync(trace.group_sizes + 3 * it + 2, loop + 3, sizeof(int),
+                                         cudaMemcpyDeviceToDevice, stream));
             if (options->verbose && (!comm || comm->rank == 0))
                 std::fprintf(stderr, "iteration=%d fp4=0 fp6=0 fp8=%lld\n", it + 1, (long long)n);
         } else {
@@ -441,7 +516,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream,
                                       kCentroidTileRows));
             MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
-            MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream));
+            MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream,
+                                               policy));
             MXK_CHECK(launch_group_compaction(n, precision, ord, ids, gcount, cscratch, stream, loop));
             static const int group_bits[3] = {4, 6, 8};
             for (int g = 0; g < 3; ++g) {
@@ -456,18 +532,30 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 am.centroid_norms = cnorm;
                 am.pid = ids + g * n;
                 am.labels = labels;
-                am.gaps = nullptr;
+                // the candidate rule reads each point's two-largest gap of the last
+                // MX iteration (assignment.cu:53-55); the reference's rule ignores it
+                am.gaps = policy ? gaps : nullptr;
                 am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
                 MXK_CHECK(launch_gemm_mx(group_bits[g], n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am,
                                          gcount + g, stream, true, fused_q ? points : nullptr, n));
             }
+            if (traced && trace.group_sizes)
+                MXK_CUDA(cudaMemcpyAsync(trace.group_sizes + 3 * it, gcount, sizeof(int) * 3, cudaMemcpyDeviceToDevice,
+                                         stream));
             if (options->verbose && (!comm || comm->rank == 0)) {
-                int h[3] = {0, 0, 0};
-                MXK_CUDA(cudaMemcpyAsync(h, gcount, sizeof(h), cudaMemcpyDeviceToHost, stream));
-                MXK_CUDA(cudaStreamSynchronize(stream));
+                // pinned slot of this iteration, read after the event (the
+                // watchdog's guarded wait in a sharded run)
+                const int vslot = it % (kLookahead + 1);
+                int* h = mirror->host + 4 * vslot;
+                MXK_CUDA(cudaMemcpyAsync(h, gcount, sizeof(int) * 3, cudaMemcpyDeviceToHost, stream));
+                MXK_CUDA(cudaEventRecord(mirror->ev[vslot], stream));
+                MXK_CHECK(wait_event(comm, mirror->ev[vslot]));
                 std::fprintf(stderr, "iteration=%d fp4=%d fp6=%d fp8=%d\n", it + 1, h[0], h[1], h[2]);
             }
         }
+        if (traced && trace.labels)
+            MXK_CUDA(cudaMemcpyAsync(trace.labels + (int64_t)it * n, labels, sizeof(int) * n, cudaMemcpyDeviceToDevice,
+                                     stream));
         // kmeans.cu:62-65
         MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
         MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
@@ -497,7 +585,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         }
     }
     MXK_CUDA(cudaMemcpyAsync(mirror->host, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
-    if (sharded && comm_timeout_s() > 0.0) {  // the last iterations' collectives, under the watchdog
+    if (polled_waits(comm)) {  // the last iterations' collectives, under the watchdog
         MXK_CUDA(cudaEventRecord(mirror->ev[0], stream));
         MXK_CHECK(wait_event(comm, mirror->ev[0]));
     }
@@ -509,6 +597,20 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
 }
 
 }  // namespace
+
+// For mxk_kmeans_mixed_multi (multi.cpp): the shared failure flag of its
+// in-process ranks, and the abort of a failed rank's communicator (frees it).
+void comm_attach_group_flag(void* comm, std::atomic<int>* flag) {
+    if (comm) static_cast<Comm*>(comm)->group_failed = flag;
+}
+
+void comm_abort(void* comm) {
+    auto* c = static_cast<Comm*>(comm);
+    if (!c) return;
+    if (c->comm && nccl().CommAbort) nccl().CommAbort(c->comm);
+    c->comm = nullptr;
+}
+
 }  // namespace mxk
 
 extern "C" {
@@ -522,6 +624,27 @@ int mxk_kmeans_mixed_cached(int64_t n, int d, int k, const float* points, float*
                             const mxk_options* options, int* iterations, void* stream) {
     return mxk::run_lloyd(nullptr, n, d, k, points, centroids, labels, options, iterations, mxk::as_stream(stream),
                           true);
+}
+
+int mxk_set_precision_policy(int policy) {
+    MXK_REQUIRE(policy == 0 || policy == 1, "set_precision_policy: policy must be 0 (reference) or 1 (candidate)");
+    mxk::g_precision_policy.store(policy);
+    return MXK_OK;
+}
+
+int mxk_trace_next_call(const mxk_trace* trace) {
+    MXK_REQUIRE(trace != nullptr && trace->max_iterations >= 0, "trace_next_call: bad arguments");
+    int device = 0;
+    MXK_CUDA(cudaGetDevice(&device));
+    MXK_REQUIRE(device >= 0 && device < 64, "trace_next_call: device ordinal out of range");
+    mxk::TraceRequest t;
+    t.centroids = trace->centroids;
+    t.labels = trace->labels;
+    t.group_sizes = trace->group_sizes;
+    t.max_iterations = trace->max_iterations;
+    std::lock_guard<std::mutex> lock(mxk::g_trace_mutex);
+    mxk::g_trace[device] = t;
+    return MXK_OK;
 }
 
 int mxk_comm_unique_id(unsigned char id[128]) {
@@ -555,6 +678,12 @@ int mxk_comm_init(void** comm, int nranks, int rank, const unsigned char id[128]
         }
     }
     *comm = c;
+    return MXK_OK;
+}
+
+int mxk_inject_rank_failure(int rank, int iteration) {
+    mxk::g_inject_rank.store(rank);
+    mxk::g_inject_iteration.store(iteration);
     return MXK_OK;
 }
 

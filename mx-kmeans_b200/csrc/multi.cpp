@@ -8,10 +8,14 @@
 // (mxk_kmeans_mixed_sharded).  One host thread drives each GPU.  Uploads run
 // first on every GPU; the communicator is created only once all of them have
 // succeeded, so a failed upload or allocation cannot leave the other ranks
-// waiting in NCCL initialisation.
+// waiting in NCCL initialisation.  After that, a rank that fails raises a flag
+// shared by the ranks; the others' host waits poll it, abort their
+// communicators (which ends the collectives that wait for the failed rank) and
+// return an error, so the call reports the failure instead of hanging.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <string>
 #include <thread>
 #include <vector>
@@ -20,6 +24,8 @@
 
 namespace mxk {
 int fail(int status, const std::string& message);
+void comm_attach_group_flag(void* comm, std::atomic<int>* flag);
+void comm_abort(void* comm);
 }
 
 namespace {
@@ -50,6 +56,7 @@ struct Shard {
     }
     void release() {
         if (cudaSetDevice(device) != cudaSuccess) return;
+        if (comm && status != MXK_OK) mxk::comm_abort(comm);  // a failed rank's communicator is not destroyed in order
         if (comm) mxk_comm_destroy(comm);
         if (points) cudaFree(points);
         if (centroids) cudaFree(centroids);
@@ -124,14 +131,18 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
         shards[0].record(MXK_ERR_COMM);
         uploaded = false;
     }
+    std::atomic<int> group_failed{0};
     if (uploaded) {
         on_every_gpu(shards, [&](Shard& s) {
             if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice")) return;
             if (G > 1) {
                 if (!s.record(mxk_comm_init(&s.comm, G, s.device, uid))) return;
+                mxk::comm_attach_group_flag(s.comm, &group_failed);
                 if (!s.record(mxk_kmeans_mixed_sharded(s.comm, s.rows, d, k, s.points, s.centroids, s.labels, options,
-                                                       &s.iterations, s.stream)))
+                                                       &s.iterations, s.stream))) {
+                    group_failed.store(1);  // the other ranks stop waiting for this one
                     return;
+                }
             } else if (!s.record(mxk_kmeans_mixed(s.rows, d, k, s.points, s.centroids, s.labels, options,
                                                   &s.iterations, s.stream))) {
                 return;

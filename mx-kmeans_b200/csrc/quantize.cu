@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(256) point_bounds_kernel(int64_t n, int d, con
 __global__ void __launch_bounds__(256) precision_kernel(int64_t n, int d, const float* __restrict__ upper,
                                                         const float* __restrict__ gaps, float lc, float ec,
                                                         const float* __restrict__ lc_ec_dev, int* __restrict__ precision,
-                                                        int* __restrict__ group_counts) {
+                                                        int* __restrict__ group_counts, int policy) {
     const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (lc_ec_dev) {
         ec = lc_ec_dev[0];
@@ -322,7 +322,9 @@ __global__ void __launch_bounds__(256) precision_kernel(int64_t n, int d, const 
     if (p < n) {
         const size_t tile = (size_t)(p / 32) * 96;
         const int slot = (int)(p % 32);
-        prec = select_precision(upper[tile + 64 + slot], upper[tile + 32 + slot], lc, ec, d, gaps[p]);
+        // policy 0: the reference's select_precision; 1: the candidate it discards
+        prec = policy ? precision_candidate(upper[tile + 64 + slot], upper[tile + 32 + slot], lc, d, gaps[p])
+                      : select_precision(upper[tile + 64 + slot], upper[tile + 32 + slot], lc, ec, d, gaps[p]);
         precision[p] = prec;
     }
     if (group_counts) {
@@ -525,12 +527,13 @@ int launch_point_bounds(int64_t n, int d, const float* points, const float* norm
 }
 
 int launch_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc, float ec,
-                             const float* lc_ec_dev, int* precision, int* group_counts, cudaStream_t stream) {
+                             const float* lc_ec_dev, int* precision, int* group_counts, cudaStream_t stream,
+                             int policy) {
     if (n <= 0) return MXK_OK;
     const int64_t blocks = (n + 255) / 256;
     LaunchScope scope("assign_precisions", stream);
     precision_kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, upper, gaps, lc, ec, lc_ec_dev, precision,
-                                                          group_counts);
+                                                          group_counts, policy);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }

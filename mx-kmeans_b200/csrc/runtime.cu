@@ -247,7 +247,51 @@ int encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uin
 
 }  // namespace mxk
 
+namespace mxk {
+namespace {
+
+// Self-check of the kernels' failure detection: warp 0 waits on an mbarrier
+// that nothing arrives on, through dev::mbar_wait (the wait every pipelined
+// kernel here uses) with the given limit, so it times out, records
+// MXK_ERR_TIMEOUT in the error word and raises the CTA's abort flag; warp 1
+// waits on the same barrier with the default limit and leaves through the
+// abort flag, as the other roles of an aborted GEMM CTA do.
+__global__ void wait_timeout_selftest_kernel(long long limit_cycles, unsigned* err, int* outcome) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        dev::mbar_init(&bar, 1);
+        abort_flag = 0;
+        dev::fence_barrier_init();
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        volatile int* af = &abort_flag;
+        const bool completed = warp == 0 ? dev::mbar_wait(&bar, 0, af, err, limit_cycles)
+                                         : dev::mbar_wait(&bar, 0, af, err);
+        outcome[warp] = completed ? 1 : 0;  // both must report "gave up"
+    }
+}
+
+}  // namespace
+}  // namespace mxk
+
 extern "C" {
+
+int mxk_check_wait_timeout(long long limit_cycles, int* outcome, void* stream) {
+    MXK_REQUIRE(limit_cycles > 0 && limit_cycles <= mxk::dev::kWaitLimitCycles && outcome,
+                "check_wait_timeout: limit must be in (0, the kernels' own limit] and outcome non-null");
+    unsigned* err = mxk::device_error_word();
+    if (!err) return mxk::fail(MXK_ERR_CUDA, "check_wait_timeout: cannot allocate the device error word");
+    cudaStream_t s = mxk::as_stream(stream);
+    {
+        mxk::LaunchScope scope("wait_timeout_selftest", s);
+        mxk::wait_timeout_selftest_kernel<<<1, 64, 0, s>>>(limit_cycles, err, outcome);
+        MXK_CUDA(cudaGetLastError());
+    }
+    return mxk::check_device_error(s);
+}
 
 const char* mxk_last_error(void) { return mxk::g_last_error.c_str(); }
 

@@ -3,8 +3,9 @@
 // A blocking wait on a stream whose next collective needs a peer that has
 // failed never returns.  guarded_wait polls instead: the completion probe
 // (an event query), then the peer probe (the communicator's asynchronous
-// error), and gives up once the wait has made no progress for `limit_s`
-// seconds.  The caller aborts the communicator on kPeerFailed / kTimedOut, which
+// error, or a failure another rank of the same process has reported), and
+// gives up once the wait has made no progress for `limit_s` seconds (no time
+// limit when limit_s <= 0: only a failed peer ends the wait).  The caller aborts the communicator on kPeerFailed / kTimedOut, which
 // makes the collectives in flight return, and reports an error instead of
 // hanging.  Plain host code with injectable probes and clock, so its logic is
 // tested without a GPU.
@@ -28,7 +29,7 @@ WaitResult guarded_wait(Done&& done, PeerFailed&& peer_failed, double limit_s, N
         if (p == Probe::kReady) return WaitResult::kReady;
         if (p == Probe::kFailed) return WaitResult::kFailed;
         if (peer_failed()) return WaitResult::kPeerFailed;
-        if (now() - start > limit_s) return WaitResult::kTimedOut;
+        if (limit_s > 0.0 && now() - start > limit_s) return WaitResult::kTimedOut;
         pause();
     }
 }

@@ -35,6 +35,13 @@ class Options(ctypes.Structure):
         super().__init__(max_iterations, fp32_iterations, tolerance, int(bool(verbose)))
 
 
+class Trace(ctypes.Structure):
+    """mxk_trace: device buffers the next Lloyd call fills per iteration."""
+
+    _fields_ = [("centroids", ctypes.c_void_p), ("labels", ctypes.c_void_p), ("group_sizes", ctypes.c_void_p),
+                ("max_iterations", ctypes.c_int)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_uint64), ("total_ms", ctypes.c_double)]
 
@@ -53,6 +60,7 @@ SIGNATURES = {
     "mxk_precompute_point_bounds": ([_I64, _I, _P, _P, _P, _P], _I),
     "mxk_assign_precisions": ([_I64, _I, _P, _P, _F, _F, _P, _P], _I),
     "mxk_check_mxfp8_scale_codec": ([_P, _P], _I),
+    "mxk_check_wait_timeout": ([ctypes.c_longlong, _P, _P], _I),
     "mxk_release_workspace": ([], _I),
     "mxk_gemm_tiles_multiplied": ([ctypes.POINTER(ctypes.c_ulonglong), _I], _I),
     "mxk_init_farthest": ([_I64, _I, _I, _P, _P, _P], _I),
@@ -67,9 +75,12 @@ SIGNATURES = {
     "mxk_assign_f32_fused": ([_I64, _I, _I, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "mxk_kmeans_mixed": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_kmeans_mixed_cached": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
+    "mxk_set_precision_policy": ([_I], _I),
+    "mxk_trace_next_call": ([ctypes.POINTER(Trace)], _I),
     "mxk_comm_unique_id": ([ctypes.c_char_p], _I),
     "mxk_comm_init": ([ctypes.POINTER(_P), _I, _I, ctypes.c_char_p], _I),
     "mxk_comm_destroy": ([_P], _I),
+    "mxk_inject_rank_failure": ([_I, _I], _I),
     "mxk_kmeans_mixed_sharded": ([_P, _I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), ctypes.POINTER(_I), _P], _I),
     "mxk_kmeans_mixed_multi": ([_I64, _I, _I, _P, _P, _P, ctypes.POINTER(Options), _I, ctypes.POINTER(_I)], _I),
     "mxk_host_init_kmeanspp": ([_P, _I64, _I, _I, ctypes.c_uint32, _P], _I),
@@ -177,6 +188,13 @@ def check_mxfp8_scale_codec(result, stream=None):
     check(load().mxk_check_mxfp8_scale_codec(_ptr(result), _stream(stream)))
 
 
+def check_wait_timeout(limit_cycles, outcome, stream=None):
+    """Run the bounded-wait self-check (an mbarrier nothing arrives on); returns
+    the status the library reports (MXK_ERR_TIMEOUT expected) without raising.
+    outcome: 2 int32 device words, 0 = that warp's wait gave up."""
+    return load().mxk_check_wait_timeout(int(limit_cycles), _ptr(outcome), _stream(stream))
+
+
 def gemm_mx(bits, m, n, k, a, a_scales, b, b_scales, out, stream=None):
     check(load().mxk_gemm_mx(bits, m, n, k, _ptr(a), _ptr(a_scales), _ptr(b), _ptr(b_scales), _ptr(out),
                              _stream(stream)))
@@ -230,6 +248,23 @@ def kmeans_mixed(points, centroids, labels, options=None, stream=None, cache_poi
     return iters.value
 
 
+def set_precision_policy(policy):
+    """0: the reference's select_precision (always MXFP8, the default); 1: the
+    candidate it computes and discards (test hook for the 4/6/8 groups)."""
+    check(load().mxk_set_precision_policy(int(policy)))
+
+
+def trace_next_call(max_iterations, centroids=None, labels=None, group_sizes=None):
+    """Arm a trace of the next Lloyd call on the current device: per iteration i <
+    max_iterations, centroids[i] <- the centroids it assigns against, labels[i] <-
+    its labels, group_sizes[i] <- its (MXFP4, MXFP6, MXFP8) group rows.  The
+    tensors are device tensors of shape [max_iterations, ...] (or None)."""
+    t = Trace(None if centroids is None else centroids.data_ptr(),
+              None if labels is None else labels.data_ptr(),
+              None if group_sizes is None else group_sizes.data_ptr(), int(max_iterations))
+    check(load().mxk_trace_next_call(ctypes.byref(t)))
+
+
 def comm_unique_id():
     buf = ctypes.create_string_buffer(128)
     check(load().mxk_comm_unique_id(buf))
@@ -247,6 +282,12 @@ class Comm:
         if self.handle:
             check(load().mxk_comm_destroy(self.handle))
             self.handle = ctypes.c_void_p()
+
+
+def inject_rank_failure(rank, iteration):
+    """Test hook: the sharded loop of `rank` leaves with an error when it reaches
+    `iteration` (rank < 0 disarms)."""
+    check(load().mxk_inject_rank_failure(int(rank), int(iteration)))
 
 
 def shard_rows(n, world, rank):

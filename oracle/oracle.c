@@ -291,14 +291,23 @@ void orc_point_bounds(int64_t n, int d, const float* points, const float* norms,
     }
 }
 
-void orc_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc,
-                           float ec, int* precision) {
+/* policy 0: select_precision (the reference); 1: the candidate it discards,
+ * the library's test hook mxk_set_precision_policy(1). */
+static void assign_precisions_policy(int64_t n, int d, const float* upper, const float* gaps, float lc,
+                                     float ec, int* precision, int policy) {
     for (int64_t p = 0; p < n; ++p) {
         const size_t tile = (size_t)(p / 32) * 96;
         const int lane = (int)(p % 32);
-        precision[p] = orc_select_precision(upper[tile + 64 + lane], upper[tile + 32 + lane], lc, ec, d,
-                                            gaps[p]);
+        precision[p] = policy ? orc_precision_candidate(upper[tile + 64 + lane], upper[tile + 32 + lane], lc, d,
+                                                        gaps[p])
+                              : orc_select_precision(upper[tile + 64 + lane], upper[tile + 32 + lane], lc, ec, d,
+                                                     gaps[p]);
     }
+}
+
+void orc_assign_precisions(int64_t n, int d, const float* upper, const float* gaps, float lc,
+                           float ec, int* precision) {
+    assign_precisions_policy(n, d, upper, gaps, lc, ec, precision, 0);
 }
 
 /* ------------------------------------------------------------------------- */
@@ -535,6 +544,13 @@ float orc_lloyd_step(int64_t n, int d, int k, const float* points, const float* 
 
 int orc_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
                      int max_iterations, int fp32_iterations, float tolerance, int threads) {
+    return orc_kmeans_mixed_ex(n, d, k, points, centroids, labels, max_iterations, fp32_iterations, tolerance,
+                               threads, 0, NULL);
+}
+
+int orc_kmeans_mixed_ex(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                        int max_iterations, int fp32_iterations, float tolerance, int threads, int policy,
+                        int* group_sizes) {
     if (n <= 0 || d <= 0 || k <= 0 || d % 32 || max_iterations <= 0) return -2;
     float* pn = (float*)malloc(sizeof(float) * (size_t)n);
     float* cn = (float*)malloc(sizeof(float) * (size_t)k);
@@ -571,13 +587,14 @@ int orc_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centro
                 if (cn[c] > nmax) nmax = cn[c];
             }
             const float ec = sqrtf(emax), lc = sqrtf(nmax);
-            orc_assign_precisions(n, d, upper, gaps, lc, ec, precision);
+            assign_precisions_policy(n, d, upper, gaps, lc, ec, precision, policy);
             static const int group_bits[3] = {4, 6, 8};
             for (int g = 0; g < 3; ++g) {
                 const int bits = group_bits[g];
                 int64_t rows = 0;
                 for (int64_t p = 0; p < n; ++p)
                     if (precision[p] == bits) ids[rows++] = (int)p; /* thrust::copy_if, stable */
+                if (group_sizes) group_sizes[3 * it + g] = (int)rows;
                 if (!rows) continue;
                 orc_quantize_rows(bits, rows, d, points, ids, qx, sx, NULL);
                 orc_dequantize_rows(bits, rows, d, qx, sx, xd);

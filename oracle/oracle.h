@@ -84,6 +84,13 @@ double orc_inertia(int64_t n, int d, const float* points, const float* centroids
  * -1 non-finite shift, -2 bad argument. threads<=0 uses all host cores. */
 int orc_kmeans_mixed(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
                      int max_iterations, int fp32_iterations, float tolerance, int threads);
+/* orc_kmeans_mixed with a precision policy (0: select_precision, the
+ * reference; 1: precision_candidate's choice, the library's test hook) and,
+ * when group_sizes is not NULL, the rows of the MXFP4/6/8 groups of every MX
+ * iteration at group_sizes[3 * it + g] (entries of FP32 iterations untouched). */
+int orc_kmeans_mixed_ex(int64_t n, int d, int k, const float* points, float* centroids, int* labels,
+                        int max_iterations, int fp32_iterations, float tolerance, int threads, int policy,
+                        int* group_sizes);
 
 /* One MX Lloyd step from given centroids (quantize, product, assign, update, shift):
  * the unit the step-parity tests and the CPU baseline use. */

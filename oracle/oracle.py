@@ -46,6 +46,7 @@ def lib():
             "orc_top2": [_I64, _I, _P, _P, _P, _P, _P, _P],
             "orc_update_centroids": [_I64, _I, _I, _P, _P, _P, _P, _P],
             "orc_kmeans_mixed": [_I64, _I, _I, _P, _P, _P, _I, _I, _F, _I],
+            "orc_kmeans_mixed_ex": [_I64, _I, _I, _P, _P, _P, _I, _I, _F, _I, _I, _P],
             "orc_lloyd_step": [_I64, _I, _I, _P, _P, _P, _P, _P, _I],
             "orc_lloyd_fp32": [_I64, _I, _I, _P, _P, _P, _I, _F, _I],
         }
@@ -199,14 +200,19 @@ def inertia(points, centroids, labels):
     return lib().orc_inertia(points.shape[0], points.shape[1], _p(points), _p(centroids), _p(labels))
 
 
-def kmeans_mixed(points, centroids, max_iterations=300, fp32_iterations=0, tolerance=1e-4, threads=0):
-    """-> (iterations, centroids, labels); iterations < 0 on a non-finite shift."""
+def kmeans_mixed(points, centroids, max_iterations=300, fp32_iterations=0, tolerance=1e-4, threads=0,
+                 policy=0, group_sizes=False):
+    """-> (iterations, centroids, labels[, group sizes [max_iterations, 3]]);
+    iterations < 0 on a non-finite shift.  policy 1 lets precision_candidate's
+    choice stand (the library's mxk_set_precision_policy(1))."""
     points = _c(points, np.float32)
     cent = _c(centroids, np.float32).copy()
     labels = np.zeros(points.shape[0], np.int32)
-    it = lib().orc_kmeans_mixed(points.shape[0], points.shape[1], cent.shape[0], _p(points), _p(cent), _p(labels),
-                                max_iterations, fp32_iterations, tolerance, threads)
-    return it, cent, labels
+    groups = np.zeros((max_iterations, 3), np.int32) if group_sizes else None
+    it = lib().orc_kmeans_mixed_ex(points.shape[0], points.shape[1], cent.shape[0], _p(points), _p(cent),
+                                   _p(labels), max_iterations, fp32_iterations, tolerance, threads, policy,
+                                   _p(groups))
+    return (it, cent, labels, groups) if group_sizes else (it, cent, labels)
 
 
 def lloyd_step(points, point_norms, centroids, threads=0, want_dots=False):

@@ -69,3 +69,54 @@ def blobs(n, d, k, seed, spread=10.0, sigma=1.0, pad_to=128):
     out = np.zeros((n, dp), np.float32)
     out[:, :d] = x
     return out
+
+
+def assert_centroids_close(cg, co, rtol=1e-4):
+    """Centroids within rtol relative: per centroid, |c_gpu - c_oracle| <= rtol |c_oracle|."""
+    err = np.linalg.norm(np.asarray(cg, np.float64) - co, axis=1)
+    lim = rtol * np.linalg.norm(np.asarray(co, np.float64), axis=1) + 1e-6
+    assert np.all(err <= lim), f"{int((err > lim).sum())} centroids differ by more than {rtol} relative"
+
+
+def gap_band_mismatches(orc, x, centroids, labels, fp32=False, tol=1e-5):
+    """North-star label rule for one assignment step: the labels a step assigned
+    against `centroids` may differ from the oracle's only where the oracle's
+    nearest and second-nearest distances are within tol of the distance scale
+    (|x|^2 + max |c|^2).  MX steps use the oracle's MX products
+    (src/kernels/gemm.cu + assignment.cu), FP32 steps its FP32 products
+    (gemm.cu:365-380).  Asserts the rule; returns the number of differing labels."""
+    x = np.ascontiguousarray(x, np.float32)
+    pn = orc.l2_norm(x)
+    cn = orc.l2_norm(centroids)
+    if fp32:
+        dots = orc.gemm_f32(x, centroids).astype(np.float32)
+        lo, _ = orc.assign_clusters(pn, cn, dots)
+    else:
+        _, _, lo, dots = orc.lloyd_step(x, pn, centroids, want_dots=True)
+    _, first, second = orc.top2(pn, cn, dots)
+    diff = np.asarray(labels) != lo
+    scale = pn + cn.max()
+    bad = diff & ((second - first) > tol * scale)
+    assert not bad.any(), (f"{int(bad.sum())} labels differ from the oracle with a top-2 gap above "
+                           f"{tol} of the distance scale (first rows {np.flatnonzero(bad)[:8].tolist()})")
+    return int(diff.sum())
+
+
+def traced_run(torch, mxk, x, c0, iterations, tolerance=0.0, fp32_iterations=0, cache_points=False):
+    """One Lloyd call on cuda:0 with the per-iteration trace armed.
+    -> (iterations run, final centroids, final labels, centroids [it][k][d] each
+    iteration assigned against, labels [it][n] each iteration assigned, group
+    sizes [it][3]) as numpy arrays."""
+    dev = "cuda:0"
+    xt = x if isinstance(x, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    ct = (c0.clone() if isinstance(c0, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(c0)).to(dev))
+    n, k, d = xt.shape[0], ct.shape[0], ct.shape[1]
+    tc = torch.zeros((iterations, k, d), dtype=torch.float32, device=dev)
+    tl = torch.full((iterations, n), -1, dtype=torch.int32, device=dev)
+    tg = torch.zeros((iterations, 3), dtype=torch.int32, device=dev)
+    lab = torch.full((n,), -1, dtype=torch.int32, device=dev)
+    mxk.trace_next_call(iterations, tc, tl, tg)
+    it = mxk.kmeans_mixed(xt, ct, lab, mxk.Options(max_iterations=iterations, tolerance=tolerance,
+                                                   fp32_iterations=fp32_iterations), cache_points=cache_points)
+    torch.cuda.synchronize()
+    return it, ct.cpu().numpy(), lab.cpu().numpy(), tc.cpu().numpy(), tl.cpu().numpy(), tg.cpu().numpy()

@@ -134,3 +134,12 @@ def test_product_never_reaches_the_oracle():
                     if re.search(r"\boracle\b|liboracle|_ref/", text):
                         hits.append(os.path.join(dirpath, f))
     assert not hits, f"product files reference the oracle: {hits}"
+
+
+def test_precision_policy_hook_values(mxk):
+    """mxk_set_precision_policy accepts 0 (the reference's rule) and 1 (the
+    candidate) and rejects anything else; it needs no GPU."""
+    mxk.set_precision_policy(1)
+    mxk.set_precision_policy(0)
+    with pytest.raises(ValueError):
+        mxk.set_precision_policy(2)

@@ -7,9 +7,24 @@ relative."""
 import numpy as np
 import pytest
 
-from conftest import blobs
+from conftest import assert_centroids_close, blobs, gap_band_mismatches, traced_run
 
 pytestmark = pytest.mark.gpu
+
+
+def check_steps(orc, x, it, c_final, tc, tl, fp32_iterations=0):
+    """Step-wise parity of a traced run: every iteration's labels against the
+    oracle's assignment from the same centroids (gap-band rule), and the centroids
+    the next iteration starts from against the oracle's update of those labels
+    (src/kernels/update.cu:7-31: per-cluster means, empty clusters keep theirs).
+    -> total number of labels inside the band that differ."""
+    differing = 0
+    for t in range(it):
+        differing += gap_band_mismatches(orc, x, tc[t], tl[t], fp32=t < fp32_iterations)
+        c_next = tc[t + 1] if t + 1 < it else c_final
+        co, _ = orc.update_centroids(x, tl[t], tc[t])
+        assert_centroids_close(c_next, co)
+    return differing
 
 
 def _to(torch, a):
@@ -58,15 +73,16 @@ def test_full_run_vs_oracle(torch_cuda, mxk, orc, n, d, k, iters):
     torch = torch_cuda
     x = blobs(n, d, k, seed=n + d, spread=10.0, sigma=1.0)
     c0 = x[np.random.default_rng(7).choice(n, k, replace=False)].copy()
-    it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=iters, tolerance=1e-4)
+    it_g, cg, lg, tc, tl, _ = traced_run(torch, mxk, x, c0, iters, tolerance=1e-4)
     it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=iters, tolerance=1e-4)
     ig, io = orc.inertia(x, cg, lg), orc.inertia(x, co, lo)
     assert abs(ig - io) <= 1e-4 * io
-    agree = np.mean(lg == lo)
-    assert agree > 0.999
-    if np.array_equal(lg, lo):
+    assert np.array_equal(tl[it_g - 1], lg)
+    # every iteration: labels by the gap-band rule, next centroids within 1e-4
+    differing = check_steps(orc, x, it_g, cg, tc, tl)
+    if differing == 0 and np.array_equal(lg, lo):
         assert it_g == it_o
-        assert np.allclose(cg, co, rtol=1e-4, atol=1e-4)
+        assert_centroids_close(cg, co)
 
 
 def test_fp32_iterations(torch_cuda, mxk, orc):
@@ -74,10 +90,13 @@ def test_fp32_iterations(torch_cuda, mxk, orc):
     n, d, k = 6000, 128, 16
     x = blobs(n, 64, k, seed=5)
     c0 = x[:k].copy()
-    it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=4, fp32_iterations=2, tolerance=0.0)
+    it_g, cg, lg, tc, tl, tg = traced_run(torch, mxk, x, c0, 4, fp32_iterations=2)
     it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=4, fp32_iterations=2, tolerance=0.0)
     assert it_g == it_o
-    assert np.mean(lg == lo) > 0.999
+    # two FP32 iterations (FP32 products, no MX groups), then two MX iterations
+    assert np.array_equal(tg[:2], np.zeros((2, 3), np.int32))
+    assert np.array_equal(tg[2:], np.array([[0, 0, n]] * 2, np.int32))
+    check_steps(orc, x, it_g, cg, tc, tl, fp32_iterations=2)
     assert abs(orc.inertia(x, cg, lg) - orc.inertia(x, co, lo)) <= 1e-4 * orc.inertia(x, co, lo)
 
 
@@ -166,18 +185,20 @@ def test_large_k_two_iterations_match_oracle(torch_cuda, mxk, orc):
     n, d, k = 56909, 128, 2048
     x = np.rint(blobs(n, 96, 256, seed=17, spread=20.0, sigma=3.0)).astype(np.float32)
     c0 = x[np.random.default_rng(3).choice(n, k, replace=False)].copy()
-    for iters in (1, 2):
-        it_g, cg, lg = _run(torch, mxk, x, c0, max_iterations=iters, tolerance=0.0)
-        it_o, co, lo = orc.kmeans_mixed(x, c0, max_iterations=iters, tolerance=0.0)
-        assert it_g == it_o == iters
-        same = lg == lo
-        assert same.mean() > 0.999
-        counts_g = np.bincount(lg, minlength=k)
-        counts_o = np.bincount(lo, minlength=k)
-        keep = (counts_g == counts_o) & (counts_g > 0)
-        keep[np.unique(np.concatenate([lg[~same], lo[~same]]))] = False
+    it_g, cg, lg, tc, tl, _ = traced_run(torch, mxk, x, c0, 2)
+    assert it_g == 2
+    check_steps(orc, x, it_g, cg, tc, tl)
+    for t in range(2):
+        # exact sums: every cluster whose members agree with the oracle's
+        # assignment from the same centroids has the oracle's centroid bit for bit
+        _, _, lo, _ = orc.lloyd_step(x, orc.l2_norm(x), tc[t])
+        co, _ = orc.update_centroids(x, tl[t], tc[t])
+        same = tl[t] == lo
+        keep = np.bincount(tl[t], minlength=k) > 0
+        keep[np.unique(np.concatenate([tl[t][~same], lo[~same]]))] = False
         assert keep.sum() > 0.9 * k
-        assert np.array_equal(cg[keep], co[keep])
+        c_next = tc[t + 1] if t + 1 < it_g else cg
+        assert np.array_equal(c_next[keep], co[keep])
 
 
 @pytest.mark.parametrize("n,d,k,init", [(30000, 256, 1024, "farthest"), (20000, 768, 2048, "kmeans++")])
@@ -269,3 +290,41 @@ def test_cached_points_equal_default(torch_cuda, mxk, n, d, k):
     assert out[0][0] == out[1][0]
     assert np.array_equal(out[0][2], out[1][2])
     assert np.array_equal(out[0][1], out[1][1])
+
+
+@pytest.mark.parametrize("n,d,k,blobs_k,seed", [(60000, 128, 2048, 1500, 3), (40000, 256, 1024, 700, 11),
+                                                (30000, 768, 2048, 1200, 19), (30000, 768, 8192, 3000, 23)])
+def test_pruned_assignment_equals_unpruned_nonint(torch_cuda, mxk, n, d, k, blobs_k, seed):
+    """Exact pruning on non-integer data at the configs[2..4] feature widths
+    (D = 128, 256, 768; up to 43 centroid tiles): every traced iteration's labels
+    equal an unpruned assignment (tcgen05 GEMM + argmin with no tile mask) of the
+    same points against the centroids that iteration used, bit for bit, over
+    six iterations; and the mask did skip tiles."""
+    torch = torch_cuda
+    iters = 6
+    x = blobs(n, d - 32 if d > 128 else 96, blobs_k, seed=seed, spread=5.0, sigma=0.75, pad_to=d)
+    xt = torch.from_numpy(x).cuda()
+    c0 = torch.empty((k, d), device="cuda")
+    mxk.init_kmeanspp(xt, c0, seed)
+    mxk.gemm_tiles_multiplied(reset=True)
+    it, _, _, tc, tl, _ = traced_run(torch, mxk, xt, c0, iters)
+    multiplied = mxk.gemm_tiles_multiplied(reset=True)
+    assert it == iters
+    unpruned = iters * ((n + 127) // 128) * ((k + 191) // 192)
+    assert multiplied < 0.9 * unpruned, f"pruning inactive: {multiplied} of {unpruned} tiles multiplied"
+    pn = torch.empty(n, device="cuda")
+    mxk.compute_l2_norm(xt, pn)
+    qx = torch.empty(n * d, dtype=torch.uint8, device="cuda")
+    sx = torch.empty(n * d // 32, dtype=torch.uint8, device="cuda")
+    mxk.quantize_rows(8, xt, qx, sx)
+    for t in range(1, iters):
+        ct = torch.from_numpy(tc[t]).cuda()
+        qc = torch.empty(k * d, dtype=torch.uint8, device="cuda")
+        sc = torch.empty(k * d // 32, dtype=torch.uint8, device="cuda")
+        mxk.quantize_rows(8, ct, qc, sc)
+        cn = torch.empty(k, device="cuda")
+        mxk.compute_l2_norm(ct, cn)
+        lab_u = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        mxk.assign_mx_fused(8, n, k, d, qx, sx, qc, sc, pn, cn, lab_u)
+        lu = lab_u.cpu().numpy()
+        assert np.array_equal(tl[t], lu), f"iteration {t}: {(tl[t] != lu).sum()} labels differ from unpruned"

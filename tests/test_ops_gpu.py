@@ -180,3 +180,23 @@ def test_reference_cuda_checks_binary():
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "CUDA checks passed" in r.stdout
+
+
+def test_bounded_wait_gives_up_and_reports_timeout(torch_cuda, mxk):
+    """Failure detection of the kernels' bounded waits, without a GPU fault: a
+    CTA waits on an mbarrier that nothing arrives on with a limit of 10^5 cycles.
+    The kernel returns (both waiting warps give up: one on its limit, one on the
+    CTA's abort flag), the call reports MXK_ERR_TIMEOUT, and the error word is
+    clear again for the next call."""
+    torch = torch_cuda
+    outcome = torch.full((2,), -1, dtype=torch.int32, device="cuda")
+    assert mxk.check_wait_timeout(100000, outcome) == mxk.ERR_TIMEOUT
+    assert b"timed out" in mxk.load().mxk_last_error()
+    assert outcome.tolist() == [0, 0]
+    # the next public call that reads the error word succeeds
+    a = torch.zeros(128 * 128, dtype=torch.uint8, device="cuda")
+    sa = torch.full((128 * 4,), 127, dtype=torch.uint8, device="cuda")
+    out = torch.full((128, 128), -1.0, device="cuda")
+    mxk.gemm_mx(8, 128, 128, 128, a, sa, a, sa, out)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0

@@ -168,3 +168,17 @@ def test_lloyd_fp32_and_mixed_agree_on_separated_data(orc):
     it2, c2, l2 = orc.lloyd_fp32(x, c0, 20, 1e-4)
     assert np.array_equal(l1, l2)
     assert abs(orc.inertia(x, c1, l1) - orc.inertia(x, c2, l2)) <= 1e-4 * orc.inertia(x, c2, l2)
+
+
+def test_oracle_candidate_policy_fills_every_group(orc):
+    """Under policy 1 (precision_candidate's choice, include/precision.hpp:10-17)
+    the oracle's loop puts points in the MXFP4, MXFP6 and MXFP8 groups once the
+    first iteration has produced gaps; policy 0 (the reference) keeps one MXFP8
+    group."""
+    from test_precision_groups_gpu import _data
+    x, c0 = _data(256)
+    it, _, _, g = orc.kmeans_mixed(x, c0, max_iterations=4, tolerance=0.0, policy=1, group_sizes=True)
+    assert it == 4 and np.array_equal(g[0], [0, 0, len(x)]) and np.all(g[1:] > 0)
+    assert np.all(g.sum(axis=1) == len(x))
+    it, _, _, g = orc.kmeans_mixed(x, c0, max_iterations=2, tolerance=0.0, policy=0, group_sizes=True)
+    assert np.array_equal(g, [[0, 0, len(x)]] * 2)

@@ -190,6 +190,8 @@ int main() {
     { Fake f{0, 1000, 4}; bad += run(f, 10.0) != WaitResult::kPeerFailed || f.polls != 4; } // peer fails first
     { Fake f{0, 1000, 0}; bad += run(f, 2.0) != WaitResult::kTimedOut || f.t > 2.5; }     // no progress
     { Fake f{0, 4, 4}; bad += run(f, 10.0) != WaitResult::kReady; }                       // completion wins a tie
+    { Fake f{0, 1000, 50}; bad += run(f, 0.0) != WaitResult::kPeerFailed || f.polls != 50; } // no time limit:
+                                                                                          // only a peer ends it
     {   // a failed query is reported as such, not as a timeout
         int n = 0; double t = 0.0;
         WaitResult r = guarded_wait([&] { return ++n < 3 ? Probe::kPending : Probe::kFailed; }, [] { return false; },
@@ -205,8 +207,9 @@ int main() {
 def test_comm_watchdog_logic(tmp_path):
     """The sharded loop's opt-in host watchdog (MXK_COMM_TIMEOUT_S): a wait ends
     ready when the work completes, with a peer failure as soon as the
-    communicator reports one, with a timeout when nothing progresses within the
-    limit, and with the query's own failure otherwise.  Fake probes and clock,
+    communicator (or another in-process rank) reports one, with a timeout when
+    nothing progresses within the limit (none without a limit), and with the
+    query's own failure otherwise.  Fake probes and clock,
     so no GPU, NCCL or real failure is involved."""
     import subprocess
     src = tmp_path / "w.cpp"
