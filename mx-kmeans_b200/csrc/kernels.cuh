@@ -21,9 +21,10 @@ namespace mxk {
 // block % 4 -- the image tcgen05.cp .32x128b.warpx4 copies into TMEM.
 constexpr int kPointTileRows = 128;
 constexpr int kCentroidTileRows = 192;
+// name: the launch's name in the library's kernel timing (mxk_profile_read).
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
                     uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream,
-                    int atom_rows = 0);
+                    int atom_rows = 0, const char* name = "quantize_mx");
 inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileRows) {
     return (rows + tile_rows - 1) / tile_rows * (d / 128) * ((tile_rows + 127) / 128) * 512;
 }

@@ -480,7 +480,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             // Every point is in the MXFP8 group, in the visiting sequence `ord`;
             // the group's row count is loop[3] (n, or 0 once the loop stopped).
             MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
-                                      kCentroidTileRows));
+                                      kCentroidTileRows, "quantize_centroids"));
             // MXFP8 at d = 128: the GEMM quantizes the point tiles itself from the
             // FP32 rows (same bytes as quantize_rows), so this pass disappears.
             const bool fused_q = d == 128 && !cache;
@@ -491,7 +491,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 cached_stale = false;
             } else if (!fused_q) {
                 MXK_CHECK(launch_quantize(8, n, d, points, ord, qpoints, pscales, nullptr, loop + 3, stream,
-                                          kPointTileRows));
+                                          kPointTileRows, "quantize_points"));
             }
             MxArgmin am;
             am.point_norms = pnorm;
@@ -514,7 +514,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         } else {
             MXK_CUDA(cudaMemsetAsync(cerr, 0, sizeof(float) * k, stream));
             MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, cerr, nullptr, stream,
-                                      kCentroidTileRows));
+                                      kCentroidTileRows, "quantize_centroids"));
             MXK_CHECK(launch_centroid_stats(k, cerr, cnorm, stats, stream));
             MXK_CHECK(launch_assign_precisions(n, d, upper, gaps, 0.0f, 0.0f, stats, precision, nullptr, stream,
                                                policy));
@@ -526,7 +526,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 const bool fused_q = group_bits[g] == 8 && d == 128;
                 if (!fused_q)
                     MXK_CHECK(launch_quantize(group_bits[g], n, d, points, ids + g * n, qpoints, pscales, nullptr,
-                                              gcount + g, stream, kPointTileRows));
+                                              gcount + g, stream, kPointTileRows, "quantize_points"));
                 MxArgmin am;
                 am.point_norms = pnorm;
                 am.centroid_norms = cnorm;

@@ -459,7 +459,8 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 }  // namespace
 
 int launch_quantize(int bits, int64_t rows, int d, const float* points, const int* pid, void* values,
-                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream, int atom_rows) {
+                    uint8_t* scales, float* max_errors, const int* rows_dev, cudaStream_t stream, int atom_rows,
+                    const char* name) {
     if (bits != 4 && bits != 6 && bits != 8) return fail(MXK_ERR_INVALID, "Precision must be 4, 6, or 8");
     if (rows <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && d % 32 == 0, "quantize_rows: d must be a positive multiple of 32");
@@ -474,7 +475,7 @@ int launch_quantize(int bits, int64_t rows, int d, const float* points, const in
     const int64_t cap = (int64_t)sm_count() * 16;  // grid-stride beyond 16 CTAs per SM
     if (blocks > cap) blocks = cap;
     auto* out = static_cast<uint8_t*>(values);
-    LaunchScope scope("quantize_mx", stream);
+    LaunchScope scope(name, stream);
     switch (bits) {
         case 8: quantize_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atom_rows); break;
         case 6: quantize_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(rows, d, points, pid, out, scales, max_errors, rows_dev, atom_rows); break;

@@ -13,7 +13,7 @@
 // floats (64 KB + 4 bytes): one partial per 2048-element chunk plus the total.
 // Every GPU that loads the library holds this array until the process exits.
 // It bounds the input to kMaxElements = 16384 * 2048 = 33,554,432 elements
-// (every BASELINE configuration's K x D is far below it); larger inputs are
+// (the benchmarked shapes' K x D, at most 8192 x 768, are far below it); larger inputs are
 // rejected with MXK_ERR_INVALID before any work is issued.
 //
 // All calls on a device share the one array and it keeps the previous call's

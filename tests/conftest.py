@@ -7,6 +7,9 @@ import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# The reference checkout, when present, sits beside this repository (override
+# with MXK_REFERENCE); only the tests that rebuild oracle/_ref need it.
+REFERENCE_DIR = os.environ.get("MXK_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 for sub in ("mx-kmeans_b200", "oracle"):
     p = os.path.join(ROOT, sub)
     if p not in sys.path:

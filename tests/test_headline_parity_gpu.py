@@ -1,4 +1,4 @@
-"""Parity of the benchmarked path itself: BASELINE configs[3] at its full size
+"""Parity of the benchmarked path itself: the benchmark's configs[3] at its full size
 (N = 8,388,608, D = 96 padded to 128, K = 2048, the bench's seeded blobs and
 K-Means++ centroids), 20 Lloyd iterations of kmeans_mixed with exact tile
 pruning and the fused quantizer, traced per iteration and checked step by step

@@ -9,7 +9,7 @@ import os
 import numpy as np
 import pytest
 
-from conftest import ROOT
+from conftest import REFERENCE_DIR, ROOT
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "reference_vectors.npz")
 
@@ -36,7 +36,7 @@ def test_init_reference_known_answers(mxk):
 def ref_host(orc):
     lib = orc.ref_lib("libref_host.so")
     if lib is None:
-        if not os.path.isdir("/root/reference"):
+        if not os.path.isdir(REFERENCE_DIR):
             pytest.skip("oracle/_ref not built and the reference checkout is absent")
         orc.build_ref()
         lib = orc.ref_lib("libref_host.so")

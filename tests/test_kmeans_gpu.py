@@ -309,15 +309,17 @@ def test_pruned_assignment_equals_unpruned_nonint(torch_cuda, mxk, n, d, k, blob
     mxk.gemm_tiles_multiplied(reset=True)
     it, _, _, tc, tl, _ = traced_run(torch, mxk, xt, c0, iters)
     multiplied = mxk.gemm_tiles_multiplied(reset=True)
-    assert it == iters
-    unpruned = iters * ((n + 127) // 128) * ((k + 191) // 192)
+    # (few points per cluster at K = 8192 settle after a few iterations: an exactly
+    # zero shift meets tol 0; iterations enqueued past the stop multiply nothing)
+    assert 3 <= it <= iters
+    unpruned = it * ((n + 127) // 128) * ((k + 191) // 192)
     assert multiplied < 0.9 * unpruned, f"pruning inactive: {multiplied} of {unpruned} tiles multiplied"
     pn = torch.empty(n, device="cuda")
     mxk.compute_l2_norm(xt, pn)
     qx = torch.empty(n * d, dtype=torch.uint8, device="cuda")
     sx = torch.empty(n * d // 32, dtype=torch.uint8, device="cuda")
     mxk.quantize_rows(8, xt, qx, sx)
-    for t in range(1, iters):
+    for t in range(1, it):
         ct = torch.from_numpy(tc[t]).cuda()
         qc = torch.empty(k * d, dtype=torch.uint8, device="cuda")
         sc = torch.empty(k * d // 32, dtype=torch.uint8, device="cuda")

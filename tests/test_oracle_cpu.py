@@ -9,10 +9,10 @@ import subprocess
 import numpy as np
 import pytest
 
-from conftest import ROOT, reference_fixture_a, reference_fixture_b
+from conftest import REFERENCE_DIR, ROOT, reference_fixture_a, reference_fixture_b
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "reference_vectors.npz")
-HAVE_REF = os.path.isdir("/root/reference")
+HAVE_REF = os.path.isdir(REFERENCE_DIR)
 
 
 @pytest.fixture(scope="module")

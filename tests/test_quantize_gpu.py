@@ -90,7 +90,7 @@ def test_random_rows(torch_cuda, mxk, orc, bits, d):
 
 
 def test_large_shape_sampled(torch_cuda, mxk, orc):
-    # Full-size property: 2^21 rows x 128 (BASELINE config 4 has 2^23); every row
+    # Full-size property: 2^21 rows x 128 (the benchmarked shape has 2^23); every row
     # checked through a checksum, 4096 sampled rows checked byte for byte.
     torch = torch_cuda
     n, d = 1 << 21, 128
