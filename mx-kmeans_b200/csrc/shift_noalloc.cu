@@ -25,8 +25,12 @@
 //
 // The host never uses the array's symbol as a pointer: on a device's first
 // call, with that device current, cudaGetSymbolAddress gives the device
-// address, which is cached per device and passed to the kernels.  That first
-// call therefore does set-up work and should come before any stream capture.
+// address, which is cached and passed to the kernels.  The cache is keyed by
+// the device and by the unique id of its current context, so after
+// cudaDeviceReset (a new primary context, the module loaded again, maybe at
+// another address) the next call looks the address up again.  A device's first
+// call (and the first after a reset) therefore does set-up work and should come
+// before any stream capture.
 #include <mutex>
 
 #include "common.cuh"
@@ -42,17 +46,50 @@ static __device__ __align__(256) float g_shift_scratch[kMaxPartials + 1];
 
 std::mutex g_scratch_mutex;
 float* g_scratch_ptr[64] = {};
+unsigned long long g_scratch_ctx[64] = {};  // unique id of the context the address belongs to
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id (never reused in the process) of the calling thread's current
+// context (the caller makes the device's primary context current first).
+int current_context_id(unsigned long long* id) {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    if (!get_current || !get_id) {
+        void* a = nullptr;
+        void* b = nullptr;
+        cudaDriverEntryPointQueryResult qa, qb;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) != cudaSuccess ||
+            qa != cudaDriverEntryPointSuccess || !a ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) != cudaSuccess ||
+            qb != cudaDriverEntryPointSuccess || !b)
+            return fail(MXK_ERR_CUDA, "centroid_shift_noalloc: cuCtxGetCurrent / cuCtxGetId unavailable");
+        get_current = reinterpret_cast<CtxGetCurrentFn>(a);
+        get_id = reinterpret_cast<CtxGetIdFn>(b);
+    }
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, id) != CUDA_SUCCESS)
+        return fail(MXK_ERR_CUDA, "centroid_shift_noalloc: no current CUDA context");
+    return MXK_OK;
+}
 
 int scratch_address(float** out) {
     int dev = 0;
     MXK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(MXK_ERR_UNSUPPORTED, "centroid_shift_noalloc: device ordinal >= 64");
+    // cudaSetDevice initialises the device's primary context and makes it
+    // current on this thread (it allocates nothing)
+    MXK_CUDA(cudaSetDevice(dev));
+    unsigned long long ctx = 0;
+    MXK_CHECK(current_context_id(&ctx));
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_ptr[dev]) {
+    if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_shift_scratch);
         if (e != cudaSuccess) return fail_cuda("cudaGetSymbolAddress(g_shift_scratch)", e);
         g_scratch_ptr[dev] = static_cast<float*>(p);
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_ptr[dev];
     return MXK_OK;
