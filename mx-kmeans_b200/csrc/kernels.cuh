@@ -115,11 +115,10 @@ bool prune_supported(int64_t k, int d);
 // |c^|^2, |c^|^2, |c|^2 as cn, 0)), tst (per tile: min beta, max |c^|^2, max
 // |c|^2, non-finite flag) and, with prev: delta (k upper bounds of |c^ -
 // c^_prev|) and dmin (k x tiles lower bounds of quantized centroid-to-tile
-// distances).  stop: the Lloyd loop's stop word (optional).
-// gram: gram_scratch_floats(k) floats of scratch.
-int64_t gram_scratch_floats(int k);
+// distances, from an FP32 Gram product reduced in registers).  stop: the
+// Lloyd loop's stop word (optional).
 int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
-                             float* gram, float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
+                             float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
                              cudaStream_t stream);
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances

@@ -379,7 +379,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
     const bool prune = forced8 && n > 0 && prune_supported(k, d);
     const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
-    float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *gram = nullptr;
+    float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr;
     float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
     float4 *cstats = nullptr, *tstats = nullptr;  // [2][k] per-centroid stats by iteration parity; [ctiles]
     uint64_t* tmask = nullptr;
@@ -387,7 +387,6 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (prune) {
         MXK_CHECK(ws.alloc(&pinfo, n));
         MXK_CHECK(ws.alloc(&chat, kd));
-        MXK_CHECK(ws.alloc(&gram, gram_scratch_floats(k)));
         MXK_CHECK(ws.alloc(&dmin, (int64_t)k * ctiles));
         MXK_CHECK(ws.alloc(&cdelta, k));
         MXK_CHECK(ws.alloc(&cstats, 2 * (int64_t)k));
@@ -454,7 +453,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         float4* cst = cstats + (int64_t)(it & 1) * k;
         const float4* cst_old = cstats + (int64_t)((it + 1) & 1) * k;
         if (prune && it >= options->fp32_iterations)  // this iteration's centroid stats (the next one's old ones)
-            MXK_CHECK(launch_centroid_geometry(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, gram, dmin,
+            MXK_CHECK(launch_centroid_geometry(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, dmin,
                                                cdelta, cst, tstats, loop, stream));
         if (prune_it)
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,

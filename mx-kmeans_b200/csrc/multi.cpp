@@ -132,6 +132,7 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
         uploaded = false;
     }
     std::atomic<int> group_failed{0};
+    std::atomic<int> first_failed{-1};  // the rank whose own failure the others then report
     if (uploaded) {
         on_every_gpu(shards, [&](Shard& s) {
             if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice")) return;
@@ -140,6 +141,8 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
                 mxk::comm_attach_group_flag(s.comm, &group_failed);
                 if (!s.record(mxk_kmeans_mixed_sharded(s.comm, s.rows, d, k, s.points, s.centroids, s.labels, options,
                                                        &s.iterations, s.stream))) {
+                    int none = -1;
+                    if (!group_failed.load()) first_failed.compare_exchange_strong(none, s.device);
                     group_failed.store(1);  // the other ranks stop waiting for this one
                     return;
                 }
@@ -162,6 +165,11 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
                               "cudaMemcpy");
     for (auto& s : shards) s.release();
     cudaSetDevice(caller_device);
+    // the rank that failed first is the cause; the others report their aborted waits
+    const int cause = first_failed.load();
+    if (cause >= 0 && shards[size_t(cause)].status != MXK_OK)
+        return mxk::fail(shards[size_t(cause)].status,
+                         "kmeans_mixed_multi: GPU " + std::to_string(cause) + ": " + shards[size_t(cause)].error);
     for (auto& s : shards)
         if (s.status != MXK_OK) return mxk::fail(s.status, "kmeans_mixed_multi: GPU " + std::to_string(s.device) + ": " + s.error);
     *iterations = first.iterations;

@@ -38,9 +38,14 @@
 namespace mxk {
 namespace {
 
-constexpr int kGeoThreads = 256;
-constexpr int kGramRows = 1024;  // centroid rows per Gram product
 constexpr int kMaxPruneTiles = 64;
+// Pair-bound kernel: a CTA covers 64 centroids a against one 192-centroid
+// tile T; 128 threads, each 8 rows x 12 columns of the FP32 Gram block,
+// feature chunks of 32 staged in shared memory.
+constexpr int kPairRows = 64;
+constexpr int kPairCols = kCentroidTileRows;  // 192
+constexpr int kPairChunk = 32;
+constexpr int kPairThreads = 128;
 
 // MXFP8 round trip of 4 consecutive features held by one lane; the 8 lanes of
 // each 32-feature block share its scale (quantize_rows' arithmetic, the values
@@ -93,52 +98,120 @@ __global__ void __launch_bounds__(256) centroid_quant_kernel(int k, int d, const
     }
 }
 
-// dmin[(a0 + i) * tiles + T], i < rows: a lower bound of min over c in T of
-// |c^ - c^_a|, from the Gram rows gram[i][b] = <c^_{a0+i}, c^_b> (FP32 SGEMM)
-// and the quantized squared norms cst[].y: |c^_a - c^_b|^2 = h_a + h_b - 2 G_ab,
-// less a bound on the rounding of the product, the norms and this sum.
-__global__ void __launch_bounds__(kGeoThreads) gram_pairs_kernel(int a0, int k, int d, int tiles, int tile_cols,
-                                                                 const float* __restrict__ gram,
-                                                                 const float4* __restrict__ cst,
-                                                                 float* __restrict__ dmin,
-                                                                 const int* __restrict__ stop) {
+// dmin[a * tiles + T]: a lower bound of min over c in T, c != a, of |c^ - c^_a|,
+// from the Gram entries G_ab = <c^_a, c^_b> (FP32, each accumulated by fmaf in
+// increasing feature order) and the quantized squared norms h = cst[].y:
+// |c^_a - c^_b|^2 = h_a + h_b - 2 G_ab, less (d + 16) u' (h_a + h_b + 2 |c^_a|
+// |c^_b|) for the rounding of the product, the norms and this sum; 0 when no
+// finite bound exists.  The Gram block is reduced to its per-row minima in
+// registers, so no K x K product is stored.
+__global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d, int tiles, const float* __restrict__ chat,
+                                                                   const float4* __restrict__ cst,
+                                                                   float* __restrict__ dmin,
+                                                                   const int* __restrict__ stop) {
     if (stop && *stop) return;
-    __shared__ unsigned best[kMaxPruneTiles];
-    const int a = a0 + blockIdx.x;
-    for (int t = threadIdx.x; t < kMaxPruneTiles; t += blockDim.x) best[t] = 0x7f800000u;
-    __syncthreads();
-    const float ha = cst[a].y;
-    const float rel = (float)(d + 16) * 1.2e-7f;
-    const float* g = gram + (int64_t)blockIdx.x * k;
-    for (int b = threadIdx.x; b < k; b += blockDim.x) {
-        const float hb = cst[b].y;
-        float lo = 0.0f;
-        if (b != a) {
-            const float d2 = ha + hb - 2.0f * g[b];
-            lo = d2 - rel * (ha + hb + 2.0f * sqrtf(ha) * sqrtf(hb));
-        }
-        if (lo == lo) atomicMin(&best[b / tile_cols], __float_as_uint(fmaxf(lo, 0.0f)));
+    __shared__ __align__(16) float As[kPairChunk][kPairRows];
+    __shared__ __align__(16) float Bs[kPairChunk][kPairCols];
+    __shared__ float hb_s[kPairCols], sb_s[kPairCols];
+    const int tid = threadIdx.x;
+    const int a0 = blockIdx.x * kPairRows, tile = blockIdx.y, b0 = tile * kPairCols;
+    const int ty = tid >> 4, tx = tid & 15;  // rows 8 ty .. +8, columns 12 tx .. +12
+    for (int j = tid; j < kPairCols; j += kPairThreads) {
+        const int b = b0 + j;
+        const float h = b < k ? cst[b].y : 0.0f;
+        hb_s[j] = h;
+        sb_s[j] = sqrtf(h);
     }
-    __syncthreads();
-    for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
-        const float lo = __uint_as_float(best[t]);  // +inf if every entry was NaN: then no bound
-        dmin[(int64_t)a * tiles + t] = lo < __int_as_float(0x7f800000) ? sqrtf(lo) * (1.0f - 1e-6f) : 0.0f;
+    float acc[8][12];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 12; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < d; k0 += kPairChunk) {
+        __syncthreads();
+        // rows fastest: consecutive threads store consecutive rows of a k line
+        for (int idx = tid; idx < kPairRows * (kPairChunk / 4); idx += kPairThreads) {
+            const int r = idx % kPairRows, q = idx / kPairRows;
+            const int a = a0 + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a < k) v = __ldg(reinterpret_cast<const float4*>(chat + (int64_t)a * d + k0 + 4 * q));
+            As[4 * q][r] = v.x, As[4 * q + 1][r] = v.y, As[4 * q + 2][r] = v.z, As[4 * q + 3][r] = v.w;
+        }
+        for (int idx = tid; idx < kPairCols * (kPairChunk / 4); idx += kPairThreads) {
+            const int r = idx % kPairCols, q = idx / kPairCols;
+            const int b = b0 + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (b < k) v = __ldg(reinterpret_cast<const float4*>(chat + (int64_t)b * d + k0 + 4 * q));
+            Bs[4 * q][r] = v.x, Bs[4 * q + 1][r] = v.y, Bs[4 * q + 2][r] = v.z, Bs[4 * q + 3][r] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < kPairChunk; ++kk) {
+            const float4 a_lo = *reinterpret_cast<const float4*>(&As[kk][8 * ty]);
+            const float4 a_hi = *reinterpret_cast<const float4*>(&As[kk][8 * ty + 4]);
+            const float4 b_0 = *reinterpret_cast<const float4*>(&Bs[kk][12 * tx]);
+            const float4 b_1 = *reinterpret_cast<const float4*>(&Bs[kk][12 * tx + 4]);
+            const float4 b_2 = *reinterpret_cast<const float4*>(&Bs[kk][12 * tx + 8]);
+            const float av[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+            const float bv[12] = {b_0.x, b_0.y, b_0.z, b_0.w, b_1.x, b_1.y, b_1.z, b_1.w, b_2.x, b_2.y, b_2.z, b_2.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 12; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+    }
+    const float rel = (float)(d + 16) * 1.2e-7f;
+    const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int a = a0 + 8 * ty + i;
+        const float ha = a < k ? cst[a].y : 0.0f;
+        const float sa = sqrtf(ha);
+        float m = inf;  // fminf skips NaN entries; all NaN leaves no bound
+#pragma unroll
+        for (int j = 0; j < 12; ++j) {
+            const int c = 12 * tx + j, b = b0 + c;
+            if (b < k && b != a) {
+                const float hb = hb_s[c];
+                const float d2 = ha + hb - 2.0f * acc[i][j];
+                m = fminf(m, d2 - rel * (ha + hb + 2.0f * sa * sb_s[c]));
+            }
+        }
+        for (int o = 8; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (tx == 0 && a < k) dmin[(int64_t)a * tiles + tile] = m < inf ? sqrtf(fmaxf(m, 0.0f)) * (1.0f - 1e-6f) : 0.0f;
     }
 }
 
-// Per centroid tile: (min beta, max |c^|^2, max |c|^2, non-finite flag).
-__global__ void tile_stats_kernel(int k, int tiles, int tile_cols, const float4* __restrict__ cst,
-                                  float4* __restrict__ tst, const int* __restrict__ stop) {
+// Per centroid tile: (min beta, max |c^|^2, max |c|^2, non-finite flag); one
+// block per tile, one thread per centroid.
+__global__ void __launch_bounds__(kCentroidTileRows) tile_stats_kernel(int k, int tile_cols,
+                                                                      const float4* __restrict__ cst,
+                                                                      float4* __restrict__ tst,
+                                                                      const int* __restrict__ stop) {
     if (stop && *stop) return;
-    for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
-        float4 m = make_float4(__int_as_float(0x7f800000), 0.0f, 0.0f, 0.0f);
-        const int e = min(k, (t + 1) * tile_cols);
-        for (int b = t * tile_cols; b < e; ++b) {
-            const float4 v = cst[b];
-            m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
-            if (!(fabsf(v.x) < __int_as_float(0x7f800000) && v.y < __int_as_float(0x7f800000) &&
-                  v.z < __int_as_float(0x7f800000)))
-                m.w = 1.0f;  // a non-finite centroid: no pruning against this tile
+    __shared__ float4 part[(kCentroidTileRows + 31) / 32];
+    const int t = blockIdx.x;
+    const int b = t * tile_cols + (int)threadIdx.x;
+    float4 m = make_float4(__int_as_float(0x7f800000), 0.0f, 0.0f, 0.0f);
+    if ((int)threadIdx.x < tile_cols && b < k) {
+        const float4 v = cst[b];
+        m = make_float4(v.x, v.y, v.z, 0.0f);
+        if (!(fabsf(v.x) < __int_as_float(0x7f800000) && v.y < __int_as_float(0x7f800000) &&
+              v.z < __int_as_float(0x7f800000)))
+            m.w = 1.0f;  // a non-finite centroid: no pruning against this tile
+    }
+    for (int o = 16; o; o >>= 1) {
+        m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
+        m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
+        m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
+        m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
+    }
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+            const float4 o = part[w];
+            m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
         }
         tst[t] = m;
     }
@@ -213,10 +286,8 @@ bool prune_supported(int64_t k, int d) {
     return (k + kCentroidTileRows - 1) / kCentroidTileRows <= kMaxPruneTiles && d % 128 == 0 && d <= 1024;
 }
 
-int64_t gram_scratch_floats(int k) { return (int64_t)std::min(k, kGramRows) * k; }
-
 int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
-                             float* gram, float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
+                             float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
                              cudaStream_t stream) {
     MXK_REQUIRE(prune_supported(k, d), "centroid geometry: unsupported shape");
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
@@ -228,17 +299,13 @@ int launch_centroid_geometry(int k, int d, const float* centroids, const float* 
         MXK_CUDA(cudaGetLastError());
     }
     if (prev) {  // the pairwise bounds are only used with a previous iteration
-        for (int a0 = 0; a0 < k; a0 += kGramRows) {
-            const int rows = std::min(kGramRows, k - a0);
-            MXK_CHECK(launch_gemm_fp32(rows, k, d, chat + (int64_t)a0 * d, chat, gram, stream));
-            LaunchScope scope("centroid_pairs", stream);
-            gram_pairs_kernel<<<(unsigned)rows, kGeoThreads, 0, stream>>>(a0, k, d, tiles, kCentroidTileRows, gram, cst,
-                                                                         dmin, stop);
-            MXK_CUDA(cudaGetLastError());
-        }
+        LaunchScope scope("centroid_pairs", stream);
+        pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0,
+                             stream>>>(k, d, tiles, chat, cst, dmin, stop);
+        MXK_CUDA(cudaGetLastError());
     }
     LaunchScope scope("tile_stats", stream);
-    tile_stats_kernel<<<1, 64, 0, stream>>>(k, tiles, kCentroidTileRows, cst, tst, stop);
+    tile_stats_kernel<<<(unsigned)tiles, kCentroidTileRows, 0, stream>>>(k, kCentroidTileRows, cst, tst, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
