@@ -111,15 +111,20 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
 // Exact pruning of centroid tiles (see prune.cu for the bounds).  Supported for
 // at most 64 centroid tiles and d % 128 == 0, d <= 1024.
 bool prune_supported(int64_t k, int d);
-// Centroid geometry: chat (k x d dequantized centroids), cst (k x (|c|^2 -
-// |c^|^2, |c^|^2, |c|^2 as cn, 0)), tst (per tile: min beta, max |c^|^2, max
-// |c|^2, non-finite flag) and, with prev: delta (k upper bounds of |c^ -
-// c^_prev|) and dmin (k x tiles lower bounds of quantized centroid-to-tile
-// distances, from an FP32 Gram product reduced in registers).  stop: the
-// Lloyd loop's stop word (optional).
-int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
-                             float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
-                             cudaStream_t stream);
+// Centroid preparation of an MX iteration with pruning, one pass per centroid
+// row: cn (|c|^2, compute_l2_norm's values), the MXFP8 codes qcent (k x d) and
+// scales cscales (atom layout for kCentroidTileRows-row tiles, as
+// launch_quantize writes them), chat (k x d dequantized centroids), cst (k x
+// (|c|^2 - |c^|^2, |c^|^2, |c|^2, 0)) and delta (k upper bounds of |c^ -
+// c^_prev|, +inf without prev).  stop: the Lloyd loop's stop word (optional).
+int launch_centroid_prep(int k, int d, const float* centroids, const float* prev, float* cn, float* chat,
+                         float4* cst, float* delta, uint8_t* qcent, uint8_t* cscales, const int* stop,
+                         cudaStream_t stream);
+// dmin (k x tiles lower bounds of quantized centroid-to-tile distances, from
+// an FP32 Gram product reduced in registers) and tst (per tile: min beta, max
+// |c^|^2, max |c|^2, non-finite flag) from chat and cst.
+int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
+                          cudaStream_t stream);
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
 // and the current (cst) and previous (cst_old) centroid stats; row_bound
@@ -143,9 +148,11 @@ int launch_assign_clusters(int64_t rows, int k, const float* point_norms, const 
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
                       float* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
 // centroids = counts ? sums / counts : old.  If shift_scratch is not null
-// (shift_scratch_floats() floats), its last element receives sum((old - new)^2),
+// (shift_scratch_floats() floats, zeroed once before the first use by a Lloyd
+// loop), shift_scratch[shift_total_index()] receives sum((old - new)^2),
 // reduced in a fixed order (bit-reproducible).  sums and centroids may alias.
 int64_t shift_scratch_floats();
+int64_t shift_total_index();
 //
 // loop (optional, device words, Lloyd driver): loop[0] = stopped, loop[1] =
 // completed iterations, loop[2] = stopped on a non-finite shift, loop[3] = the

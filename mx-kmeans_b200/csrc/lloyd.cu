@@ -375,6 +375,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
+    MXK_CUDA(cudaMemsetAsync(shift, 0, sizeof(float) * shift_scratch_floats(), stream));  // (the finalize ticket)
     // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
     // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
     const bool prune = forced8 && n > 0 && prune_supported(k, d);
@@ -446,18 +447,25 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             }
             ord = order;
         }
-        MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
         // Pruning needs the previous iteration's labels and distances from the
         // MX GEMM (not an FP32 iteration) and, in prev, the centroids it used.
         const bool prune_it = prune && it >= 1 && it - 1 >= options->fp32_iterations;
         float4* cst = cstats + (int64_t)(it & 1) * k;
         const float4* cst_old = cstats + (int64_t)((it + 1) & 1) * k;
-        if (prune && it >= options->fp32_iterations)  // this iteration's centroid stats (the next one's old ones)
-            MXK_CHECK(launch_centroid_geometry(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, dmin,
-                                               cdelta, cst, tstats, loop, stream));
-        if (prune_it)
+        // MX iterations with pruning: the centroid norms, the centroids' MXFP8
+        // codes and scales and their pruning stats (this iteration's, the next
+        // one's old ones) in one pass; otherwise the norms alone here.
+        const bool prep = prune && it >= options->fp32_iterations;
+        if (prep)
+            MXK_CHECK(launch_centroid_prep(k, d, centroids, prune_it ? prev : nullptr, cnorm, chat, cst, cdelta, qcent,
+                                           cscales, loop, stream));
+        else
+            MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
+        if (prune_it) {
+            MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
                                        loop, stream));
+        }
         MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         const bool traced = it < trace.max_iterations;
         if (traced && trace.centroids)
@@ -478,8 +486,9 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         } else if (forced8) {
             // Every point is in the MXFP8 group, in the visiting sequence `ord`;
             // the group's row count is loop[3] (n, or 0 once the loop stopped).
-            MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
-                                      kCentroidTileRows, "quantize_centroids"));
+            if (!prep)  // (else the centroid pass above wrote the MXFP8 centroids)
+                MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
+                                          kCentroidTileRows, "quantize_centroids"));
             // MXFP8 at d = 128: the GEMM quantizes the point tiles itself from the
             // FP32 rows (same bytes as quantize_rows), so this pass disappears.
             const bool fused_q = d == 128 && !cache;

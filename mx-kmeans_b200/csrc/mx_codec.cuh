@@ -175,4 +175,17 @@ __device__ __forceinline__ uint32_t e2m1_to_e4m3(uint32_t c) {
     return e4m3x2_encode(v, 0.0f) & 0xffu;
 }
 
+// Byte offset of the scale of (row, 32-feature block) in the tcgen05 atom layout
+// for tiles of tile_rows rows: ceil(tile_rows / 128) 512-byte atoms per (tile,
+// 128-feature chunk), tile-major, slice row r's four block scales at
+// (r % 32) * 16 + (r / 32) * 4 + block % 4.
+__device__ __forceinline__ int64_t scale_atom_offset(int64_t row, int blk, int kchunks, int tile_rows) {
+    const int64_t tile = row / tile_rows;
+    const int rr = (int)(row - tile * tile_rows);
+    const int per_tile = (tile_rows + 127) >> 7;
+    const int r = rr & 127;
+    return (((tile * kchunks + (blk >> 2)) * per_tile + (rr >> 7)) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) +
+           (blk & 3);
+}
+
 }  // namespace mxk::dev

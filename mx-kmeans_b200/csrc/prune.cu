@@ -65,21 +65,44 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// Per centroid (one warp per row): the dequantized row c^ into chat, stats
-// cst[a] = (beta = |c|^2 - |c^|^2, |c^|^2, |c|^2, 0), and delta[a] >= |c^_a -
-// c^_a_old| (the previous centroids' round trip; +inf without prev).
-__global__ void __launch_bounds__(256) centroid_quant_kernel(int k, int d, const float* __restrict__ c,
-                                                             const float* __restrict__ prev,
-                                                             const float* __restrict__ cn, float* __restrict__ chat,
-                                                             float4* __restrict__ cst, float* __restrict__ delta,
-                                                             const int* __restrict__ stop) {
+// Per centroid (one warp per row), in one pass over its row: the row's squared
+// norm |c|^2 (the reference's sequential FP32 sum, compute_l2_norm: features in
+// order, carried from lane to lane), its MXFP8 codes and UE8M0 scales (the
+// bytes quantize_rows writes, scales in the GEMM's atom layout for 192-row
+// tiles), the dequantized row c^ into chat, stats cst[a] = (beta = |c|^2 -
+// |c^|^2, |c^|^2, |c|^2, 0), and delta[a] >= |c^_a - c^_a_old| (the previous
+// centroids' round trip; +inf without prev).
+__global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const float* __restrict__ c,
+                                                            const float* __restrict__ prev, float* __restrict__ cn,
+                                                            float* __restrict__ chat, float4* __restrict__ cst,
+                                                            float* __restrict__ delta, uint8_t* __restrict__ qcent,
+                                                            uint8_t* __restrict__ cscales,
+                                                            const int* __restrict__ stop) {
     if (stop && *stop) return;
     const int lane = threadIdx.x & 31;
     const int a = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (a >= k) return;
-    float h = 0.0f, mv = 0.0f;
+    if (a >= k) return;  // warp-uniform
+    const int kchunks = d >> 7;
+    float norm = 0.0f, h = 0.0f, mv = 0.0f;
     for (int j = 4 * lane; j < d; j += 128) {
-        const float4 ch = mxfp8_round_trip4(__ldg(reinterpret_cast<const float4*>(c + (int64_t)a * d + j)), lane);
+        const float4 x = __ldg(reinterpret_cast<const float4*>(c + (int64_t)a * d + j));
+        // features j - 4 lane .. + 127 in order: lane L applies its four, then
+        // hands the running sum to lane L + 1
+#pragma unroll
+        for (int L = 0; L < 32; ++L) {
+            const float t = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, fmaf(x.x, x.x, norm))));
+            norm = __shfl_sync(0xffffffffu, t, L);
+        }
+        float amax = fmaxf(fmaxf(fmaxf(0.0f, fabsf(x.x)), fmaxf(fabsf(x.y), fabsf(x.z))), fabsf(x.w));
+        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
+        const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
+        const uint32_t lo = dev::e4m3x2_encode(x.x * rcp, x.y * rcp);
+        const uint32_t hi = dev::e4m3x2_encode(x.z * rcp, x.w * rcp);
+        *reinterpret_cast<uint32_t*>(qcent + (int64_t)a * d + j) = (lo & 0xffffu) | (hi << 16);
+        if ((lane & 7) == 0) cscales[dev::scale_atom_offset(a, j >> 5, kchunks, kCentroidTileRows)] = (uint8_t)sc;
+        const float4 ch = make_float4(dev::e4m3_decode(lo & 0xffu) * scale, dev::e4m3_decode((lo >> 8) & 0xffu) * scale,
+                                      dev::e4m3_decode(hi & 0xffu) * scale, dev::e4m3_decode((hi >> 8) & 0xffu) * scale);
         *reinterpret_cast<float4*>(chat + (int64_t)a * d + j) = ch;
         h = fmaf(ch.x, ch.x, fmaf(ch.y, ch.y, fmaf(ch.z, ch.z, fmaf(ch.w, ch.w, h))));
         if (prev) {
@@ -94,7 +117,8 @@ __global__ void __launch_bounds__(256) centroid_quant_kernel(int k, int d, const
     if (lane == 0) {
         const float rel = 1.0f + (float)(d + 8) * 1.2e-7f;  // rounding of an FP32 sum of d squares
         delta[a] = prev ? sqrtf(mv * rel) * (1.0f + 1e-6f) : __int_as_float(0x7f800000);
-        cst[a] = make_float4(cn[a] - h, h, cn[a], 0.0f);
+        cn[a] = norm;
+        cst[a] = make_float4(norm - h, h, norm, 0.0f);
     }
 }
 
@@ -104,12 +128,41 @@ __global__ void __launch_bounds__(256) centroid_quant_kernel(int k, int d, const
 // |c^_a - c^_b|^2 = h_a + h_b - 2 G_ab, less (d + 16) u' (h_a + h_b + 2 |c^_a|
 // |c^_b|) for the rounding of the product, the norms and this sum; 0 when no
 // finite bound exists.  The Gram block is reduced to its per-row minima in
-// registers, so no K x K product is stored.
+// registers, so no K x K product is stored.  The first block of each tile
+// column also writes the tile's stats tst[T] = (min beta, max |c^|^2, max
+// |c|^2, non-finite flag) over its centroids.
 __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d, int tiles, const float* __restrict__ chat,
                                                                    const float4* __restrict__ cst,
-                                                                   float* __restrict__ dmin,
+                                                                   float* __restrict__ dmin, float4* __restrict__ tst,
                                                                    const int* __restrict__ stop) {
     if (stop && *stop) return;
+    if (blockIdx.x == 0) {
+        __shared__ float4 part[kPairThreads / 32];
+        const float inf = __int_as_float(0x7f800000);
+        float4 m = make_float4(inf, 0.0f, 0.0f, 0.0f);
+        for (int j = threadIdx.x; j < kPairCols; j += kPairThreads) {
+            const int b = blockIdx.y * kPairCols + j;
+            if (b >= k) break;
+            const float4 v = cst[b];
+            m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
+            if (!(fabsf(v.x) < inf && v.y < inf && v.z < inf)) m.w = 1.0f;  // a non-finite centroid: no pruning
+        }
+        for (int o = 16; o; o >>= 1) {
+            m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
+            m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
+            m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
+            m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
+        }
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < kPairThreads / 32; ++w) {
+                const float4 o = part[w];
+                m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
+            }
+            tst[blockIdx.y] = m;
+        }
+    }
     __shared__ __align__(16) float As[kPairChunk][kPairRows];
     __shared__ __align__(16) float Bs[kPairChunk][kPairCols];
     __shared__ float hb_s[kPairCols], sb_s[kPairCols];
@@ -182,41 +235,6 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
     }
 }
 
-// Per centroid tile: (min beta, max |c^|^2, max |c|^2, non-finite flag); one
-// block per tile, one thread per centroid.
-__global__ void __launch_bounds__(kCentroidTileRows) tile_stats_kernel(int k, int tile_cols,
-                                                                      const float4* __restrict__ cst,
-                                                                      float4* __restrict__ tst,
-                                                                      const int* __restrict__ stop) {
-    if (stop && *stop) return;
-    __shared__ float4 part[(kCentroidTileRows + 31) / 32];
-    const int t = blockIdx.x;
-    const int b = t * tile_cols + (int)threadIdx.x;
-    float4 m = make_float4(__int_as_float(0x7f800000), 0.0f, 0.0f, 0.0f);
-    if ((int)threadIdx.x < tile_cols && b < k) {
-        const float4 v = cst[b];
-        m = make_float4(v.x, v.y, v.z, 0.0f);
-        if (!(fabsf(v.x) < __int_as_float(0x7f800000) && v.y < __int_as_float(0x7f800000) &&
-              v.z < __int_as_float(0x7f800000)))
-            m.w = 1.0f;  // a non-finite centroid: no pruning against this tile
-    }
-    for (int o = 16; o; o >>= 1) {
-        m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
-        m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
-        m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
-        m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
-    }
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-            const float4 o = part[w];
-            m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
-        }
-        tst[t] = m;
-    }
-}
-
 // The rounding term rho of the header comment for squared norms px, pc (of x and
 // c) and hx2, hc2 (of x^ and c^).
 __device__ __forceinline__ float rho_bound(float px, float hx2, float pc, float hc2, float kappa) {
@@ -286,26 +304,25 @@ bool prune_supported(int64_t k, int d) {
     return (k + kCentroidTileRows - 1) / kCentroidTileRows <= kMaxPruneTiles && d % 128 == 0 && d <= 1024;
 }
 
-int launch_centroid_geometry(int k, int d, const float* centroids, const float* prev, const float* cn, float* chat,
-                             float* dmin, float* delta, float4* cst, float4* tst, const int* stop,
-                             cudaStream_t stream) {
-    MXK_REQUIRE(prune_supported(k, d), "centroid geometry: unsupported shape");
+int launch_centroid_prep(int k, int d, const float* centroids, const float* prev, float* cn, float* chat,
+                         float4* cst, float* delta, uint8_t* qcent, uint8_t* cscales, const int* stop,
+                         cudaStream_t stream) {
+    MXK_REQUIRE(prune_supported(k, d), "centroid prep: unsupported shape");
+    LaunchScope scope("centroid_prep", stream);
+    centroid_prep_kernel<<<(unsigned)(((int64_t)k * 32 + 255) / 256), 256, 0, stream>>>(k, d, centroids, prev, cn, chat,
+                                                                                       cst, delta, qcent, cscales,
+                                                                                       stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
+                          cudaStream_t stream) {
+    MXK_REQUIRE(prune_supported(k, d), "centroid pairs: unsupported shape");
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
-    {
-        LaunchScope scope("centroid_quant_stats", stream);
-        centroid_quant_kernel<<<(unsigned)(((int64_t)k * 32 + 255) / 256), 256, 0, stream>>>(k, d, centroids, prev,
-                                                                                            cn, chat, cst, delta,
-                                                                                            stop);
-        MXK_CUDA(cudaGetLastError());
-    }
-    if (prev) {  // the pairwise bounds are only used with a previous iteration
-        LaunchScope scope("centroid_pairs", stream);
-        pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0,
-                             stream>>>(k, d, tiles, chat, cst, dmin, stop);
-        MXK_CUDA(cudaGetLastError());
-    }
-    LaunchScope scope("tile_stats", stream);
-    tile_stats_kernel<<<(unsigned)tiles, kCentroidTileRows, 0, stream>>>(k, kCentroidTileRows, cst, tst, stop);
+    LaunchScope scope("centroid_pairs", stream);
+    pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0, stream>>>(
+        k, d, tiles, chat, cst, dmin, tst, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }

@@ -28,19 +28,6 @@ __device__ __forceinline__ float4 ldg4(const float* p) {
 // threads of a 32-feature block combine their maxima with one shuffle, derive the
 // UE8M0 scale exactly as the reference (Scale(amax/qmax) or 1 when amax == 0),
 // and multiply by the exact reciprocal of the scale.
-// Byte offset of the scale of (row, 32-feature block) in the tcgen05 atom layout
-// for tiles of tile_rows rows: ceil(tile_rows / 128) 512-byte atoms per (tile,
-// 128-feature chunk), tile-major, slice row r's four block scales at
-// (r % 32) * 16 + (r / 32) * 4 + block % 4.
-__device__ __forceinline__ int64_t scale_atom_offset(int64_t row, int blk, int kchunks, int tile_rows) {
-    const int64_t tile = row / tile_rows;
-    const int rr = (int)(row - tile * tile_rows);
-    const int per_tile = (tile_rows + 127) >> 7;
-    const int r = rr & 127;
-    return (((tile * kchunks + (blk >> 2)) * per_tile + (rr >> 7)) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) +
-           (blk & 3);
-}
-
 template <int BITS>
 __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chunks, int d,
                                                const float* __restrict__ points, const int* __restrict__ pid,
@@ -137,7 +124,7 @@ __device__ __forceinline__ void quantize_chunk(int64_t g, int64_t total, int chu
     }
     if ((chunk & 1) == 0) {
         if (atom_rows)
-            scales[scale_atom_offset(row, chunk >> 1, d >> 7, atom_rows)] = (uint8_t)s;
+            scales[dev::scale_atom_offset(row, chunk >> 1, d >> 7, atom_rows)] = (uint8_t)s;
         else
             scales[row * (d >> 5) + (chunk >> 1)] = (uint8_t)s;
         // Squared errors are non-negative, so integer order equals float order.
@@ -591,7 +578,7 @@ __global__ void __launch_bounds__(256) gather_mxfp8_rows_kernel(int64_t rows, in
         reinterpret_cast<uint4*>(dst + row * d)[piece] = reinterpret_cast<const uint4*>(src + from * d)[piece];
         if (piece < (d >> 7)) {  // the four block scales of 128-feature chunk `piece`
             const uint32_t w = reinterpret_cast<const uint32_t*>(src_scales + from * (d >> 5))[piece];
-            *reinterpret_cast<uint32_t*>(dst_scales + scale_atom_offset(row, 4 * piece, d >> 7, kPointTileRows)) = w;
+            *reinterpret_cast<uint32_t*>(dst_scales + dev::scale_atom_offset(row, 4 * piece, d >> 7, kPointTileRows)) = w;
         }
     }
 }

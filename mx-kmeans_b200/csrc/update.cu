@@ -169,16 +169,35 @@ __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* _
     }
 }
 
+// Applies the stopping rule to the Lloyd driver's state words for shift s
+// (kmeans.cu:62-67): counts the iteration and stops on a non-finite shift or
+// one <= tolerance.
+__device__ __forceinline__ void apply_stop_rule(int* loop, float s, float tolerance) {
+    loop[1] += 1;
+    if (!isfinite(s)) {
+        loop[2] = 1;
+        loop[0] = 1;
+        loop[3] = 0;
+    } else if (s <= tolerance) {
+        loop[0] = 1;
+        loop[3] = 0;
+    }
+}
+
 // Divides, applies the empty-cluster rule, and writes this CTA's partial shift
 // (sum of (old - new)^2 over its grid-stride elements, reduced in a fixed order)
 // to partials[blockIdx.x].  The grid size is fixed by the shape, so the shift is
 // bit-identical on every GPU that runs it -- all ranks of a sharded run stop on
-// the same iteration without exchanging it.
+// the same iteration without exchanging it.  With `loop` (the Lloyd driver's
+// state words) the CTA that finishes last (a ticket on *done, which it resets
+// to 0) also sums the partials in index order into *total_out and applies the
+// stopping rule; once loop[0] is set the launch does nothing.
 __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float* __restrict__ sums,
                                                        const int* __restrict__ counts, const float* __restrict__ old,
                                                        float* __restrict__ centroids, float* __restrict__ partials,
-                                                       const int* __restrict__ stop) {
-    if (stop && *stop) return;  // converged: the centroids stay as they are
+                                                       int* __restrict__ loop, unsigned* __restrict__ done,
+                                                       float* __restrict__ total_out, float tolerance) {
+    if (loop && *(volatile int*)loop) return;  // converged: the centroids stay as they are
     __shared__ float warp_sum[8];
     const int64_t total = (int64_t)k * d;
     float local = 0.0f;
@@ -194,10 +213,31 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float
     for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(kFull, local, o);
     if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
     __syncthreads();
+    __shared__ bool last;
     if (threadIdx.x == 0) {
         float s = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
         partials[blockIdx.x] = s;
+        if (loop) {
+            __threadfence();  // the partial is visible before the ticket is taken
+            last = atomicAdd(done, 1u) == gridDim.x - 1;
+        }
+    }
+    if (!loop) return;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    local = 0.0f;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) local += __ldcg(partials + i);
+    for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(kFull, local, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
+        *total_out = s;
+        *done = 0u;
+        apply_stop_rule(loop, s, tolerance);
     }
 }
 
@@ -217,17 +257,7 @@ __global__ void sum_partials_kernel(const float* __restrict__ partials, int coun
         float s = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
         out[0] = s;
-        if (loop) {
-            loop[1] += 1;
-            if (!isfinite(s)) {
-                loop[2] = 1;
-                loop[0] = 1;
-                loop[3] = 0;
-            } else if (s <= tolerance) {
-                loop[0] = 1;
-                loop[3] = 0;
-            }
-        }
+        if (loop) apply_stop_rule(loop, s, tolerance);
     }
 }
 
@@ -312,7 +342,10 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
     return MXK_OK;
 }
 
-int64_t shift_scratch_floats() { return kShiftBlocks + 1; }
+// [0, kShiftBlocks): partials, [kShiftBlocks]: the total, [kShiftBlocks + 1]:
+// the finalize kernel's ticket counter (zero between launches)
+int64_t shift_scratch_floats() { return kShiftBlocks + 2; }
+int64_t shift_total_index() { return kShiftBlocks; }
 
 int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop, float tolerance) {
@@ -322,11 +355,13 @@ int launch_finalize(int d, int k, const float* sums, const int* counts, const fl
     if (blocks > kShiftBlocks) blocks = kShiftBlocks;
     {
         LaunchScope scope("finalize", stream);
-        finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(d, k, sums, counts, old_centroids, centroids,
-                                                              shift_scratch, loop);
+        finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+            d, k, sums, counts, old_centroids, centroids, shift_scratch, loop,
+            loop ? reinterpret_cast<unsigned*>(shift_scratch + kShiftBlocks + 1) : nullptr,
+            loop ? shift_scratch + kShiftBlocks : nullptr, tolerance);
         MXK_CUDA(cudaGetLastError());
     }
-    if (shift_scratch) {
+    if (shift_scratch && !loop) {  // (with loop the finalize kernel's last CTA sums the partials)
         LaunchScope scope("shift_total", stream);
         sum_partials_kernel<<<1, 1024, 0, stream>>>(shift_scratch, (int)blocks, shift_scratch + kShiftBlocks, loop,
                                                     tolerance);
@@ -380,7 +415,7 @@ int mxk_centroid_shift(int64_t elements, const float* previous, const float* cur
         MXK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), sizeof(float) * mxk::shift_scratch_floats(), s));
         int st = mxk::launch_shift(elements, previous, current, scratch, s);
         if (st == MXK_OK) {
-            cudaError_t e = cudaMemcpyAsync(device_sum, scratch + mxk::shift_scratch_floats() - 1, sizeof(float),
+            cudaError_t e = cudaMemcpyAsync(device_sum, scratch + mxk::shift_total_index(), sizeof(float),
                                             cudaMemcpyDeviceToDevice, s);
             if (e != cudaSuccess) st = mxk::fail_cuda("cudaMemcpyAsync", e);
         }
