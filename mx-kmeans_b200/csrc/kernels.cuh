@@ -122,11 +122,9 @@ int launch_centroid_prep(int k, int d, const float* centroids, const float* prev
                          cudaStream_t stream);
 // dmin (k x tiles lower bounds of quantized centroid-to-tile distances, from
 // an FP32 Gram product reduced in registers) and tst (per tile: min beta, max
-// |c^|^2, max |c|^2, non-finite flag) from chat and cst.  Rows of dmin: a_count
-// centroids from a_begin (a multiple of 64; a_count < 0: all k); tst always
-// covers every tile.
+// |c^|^2, max |c|^2, non-finite flag) from chat and cst.
 int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
-                          cudaStream_t stream, int a_begin = 0, int a_count = -1);
+                          cudaStream_t stream);
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
 // and the current (cst) and previous (cst_old) centroid stats; row_bound

@@ -58,7 +58,6 @@ struct NcclApi {
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
-    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -79,13 +78,12 @@ static NcclApi& nccl() {
         MXK_SYM(CommAbort, "ncclCommAbort");
         MXK_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
         MXK_SYM(AllReduce, "ncclAllReduce");
-        MXK_SYM(AllGather, "ncclAllGather");
         MXK_SYM(GroupStart, "ncclGroupStart");
         MXK_SYM(GroupEnd, "ncclGroupEnd");
         MXK_SYM(GetErrorString, "ncclGetErrorString");
 #undef MXK_SYM
-        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.AllGather &&
-                 api.GroupStart && api.GroupEnd && api.GetErrorString;
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.GroupStart &&
+                 api.GroupEnd && api.GetErrorString;
     });
     return api;
 }
@@ -380,14 +378,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CUDA(cudaMemsetAsync(shift, 0, sizeof(float) * shift_scratch_floats(), stream));  // (the finalize ticket)
     // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
     // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
-    // (the same on every rank of a sharded run, whose collectives depend on it:
-    // a rank without rows still takes part)
-    const bool sharded = comm && comm->nranks > 1;
-    const bool prune = forced8 && (n > 0 || sharded) && prune_supported(k, d);
-    // Sharded runs split the centroid-pair bounds (the one centroid-side pass
-    // that grows as K^2 D) by centroid rows: each rank computes pair_rows rows
-    // and an all-gather assembles the k x tiles bounds on every rank.
-    const int pair_rows = sharded ? (int)(((k + comm->nranks - 1) / comm->nranks + 63) / 64 * 64) : k;
+    const bool prune = forced8 && n > 0 && prune_supported(k, d);
     const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr;
     float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
@@ -397,7 +388,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (prune) {
         MXK_CHECK(ws.alloc(&pinfo, n));
         MXK_CHECK(ws.alloc(&chat, kd));
-        MXK_CHECK(ws.alloc(&dmin, (int64_t)(sharded ? pair_rows * comm->nranks : k) * ctiles));
+        MXK_CHECK(ws.alloc(&dmin, (int64_t)k * ctiles));
         MXK_CHECK(ws.alloc(&cdelta, k));
         MXK_CHECK(ws.alloc(&cstats, 2 * (int64_t)k));
         MXK_CHECK(ws.alloc(&tstats, ctiles));
@@ -429,6 +420,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (!forced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
 
+    const bool sharded = comm && comm->nranks > 1;
     if (sharded && !nccl().ok) return fail(MXK_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
     if (sharded && !comm->comm)
         return fail(MXK_ERR_COMM, "kmeans_mixed_sharded: the communicator was aborted; destroy and re-create it");
@@ -470,17 +462,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         else
             MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
         if (prune_it) {
-            if (sharded) {
-                const int a0 = comm->rank * pair_rows;
-                MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream, a0,
-                                                std::max(0, std::min(pair_rows, k - a0))));
-                const size_t count = (size_t)pair_rows * ctiles;
-                const ncclResult_t r = nccl().AllGather(dmin + (size_t)comm->rank * count, dmin, count, ncclFloat32,
-                                                        comm->comm, stream);
-                if (r != ncclSuccess) return fail_nccl("ncclAllGather", r);
-            } else {
-                MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
-            }
+            MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
                                        loop, stream));
         }

@@ -122,8 +122,7 @@ __global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const 
     }
 }
 
-// dmin[a * tiles + T], a_begin <= a < a_end: a lower bound of min over c in T,
-// c != a, of |c^ - c^_a|,
+// dmin[a * tiles + T]: a lower bound of min over c in T, c != a, of |c^ - c^_a|,
 // from the Gram entries G_ab = <c^_a, c^_b> (FP32, each accumulated by fmaf in
 // increasing feature order) and the quantized squared norms h = cst[].y:
 // |c^_a - c^_b|^2 = h_a + h_b - 2 G_ab, less (d + 16) u' (h_a + h_b + 2 |c^_a|
@@ -132,8 +131,7 @@ __global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const 
 // registers, so no K x K product is stored.  The first block of each tile
 // column also writes the tile's stats tst[T] = (min beta, max |c^|^2, max
 // |c|^2, non-finite flag) over its centroids.
-__global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d, int tiles, int a_begin, int a_end,
-                                                                   const float* __restrict__ chat,
+__global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d, int tiles, const float* __restrict__ chat,
                                                                    const float4* __restrict__ cst,
                                                                    float* __restrict__ dmin, float4* __restrict__ tst,
                                                                    const int* __restrict__ stop) {
@@ -169,7 +167,7 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
     __shared__ __align__(16) float Bs[kPairChunk][kPairCols];
     __shared__ float hb_s[kPairCols], sb_s[kPairCols];
     const int tid = threadIdx.x;
-    const int a0 = a_begin + blockIdx.x * kPairRows, tile = blockIdx.y, b0 = tile * kPairCols;
+    const int a0 = blockIdx.x * kPairRows, tile = blockIdx.y, b0 = tile * kPairCols;
     const int ty = tid >> 4, tx = tid & 15;  // rows 8 ty .. +8, columns 12 tx .. +12
     for (int j = tid; j < kPairCols; j += kPairThreads) {
         const int b = b0 + j;
@@ -189,7 +187,7 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
             const int r = idx % kPairRows, q = idx / kPairRows;
             const int a = a0 + r;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (a < a_end) v = __ldg(reinterpret_cast<const float4*>(chat + (int64_t)a * d + k0 + 4 * q));
+            if (a < k) v = __ldg(reinterpret_cast<const float4*>(chat + (int64_t)a * d + k0 + 4 * q));
             As[4 * q][r] = v.x, As[4 * q + 1][r] = v.y, As[4 * q + 2][r] = v.z, As[4 * q + 3][r] = v.w;
         }
         for (int idx = tid; idx < kPairCols * (kPairChunk / 4); idx += kPairThreads) {
@@ -220,7 +218,7 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int a = a0 + 8 * ty + i;
-        const float ha = a < a_end ? cst[a].y : 0.0f;
+        const float ha = a < k ? cst[a].y : 0.0f;
         const float sa = sqrtf(ha);
         float m = inf;  // fminf skips NaN entries; all NaN leaves no bound
 #pragma unroll
@@ -233,7 +231,7 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
             }
         }
         for (int o = 8; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (tx == 0 && a < a_end) dmin[(int64_t)a * tiles + tile] = m < inf ? sqrtf(fmaxf(m, 0.0f)) * (1.0f - 1e-6f) : 0.0f;
+        if (tx == 0 && a < k) dmin[(int64_t)a * tiles + tile] = m < inf ? sqrtf(fmaxf(m, 0.0f)) * (1.0f - 1e-6f) : 0.0f;
     }
 }
 
@@ -319,16 +317,12 @@ int launch_centroid_prep(int k, int d, const float* centroids, const float* prev
 }
 
 int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
-                          cudaStream_t stream, int a_begin, int a_count) {
+                          cudaStream_t stream) {
     MXK_REQUIRE(prune_supported(k, d), "centroid pairs: unsupported shape");
-    MXK_REQUIRE(a_begin >= 0 && a_begin % kPairRows == 0, "centroid pairs: row range must start at a multiple of 64");
-    if (a_count < 0) a_count = k - a_begin;
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
-    // (at least one row block, which also writes the tile stats)
-    const int row_blocks = std::max(1, (a_count + kPairRows - 1) / kPairRows);
     LaunchScope scope("centroid_pairs", stream);
-    pair_bounds_kernel<<<dim3((unsigned)row_blocks, (unsigned)tiles), kPairThreads, 0, stream>>>(
-        k, d, tiles, a_begin, a_begin + a_count, chat, cst, dmin, tst, stop);
+    pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0, stream>>>(
+        k, d, tiles, chat, cst, dmin, tst, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
