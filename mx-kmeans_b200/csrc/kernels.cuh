@@ -125,6 +125,10 @@ int launch_centroid_prep(int k, int d, const float* centroids, const float* prev
 // |c^|^2, max |c|^2, non-finite flag) from chat and cst.
 int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
                           cudaStream_t stream);
+// Between full computations: dmin lowered in place by the centroids' movement
+// bounds (delta, from launch_centroid_prep), and tst as above.
+int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* cst, float* dmin, float4* tst,
+                                const int* stop, cudaStream_t stream);
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
 // and the current (cst) and previous (cst_old) centroid stats; row_bound
@@ -161,10 +165,14 @@ int64_t shift_total_index();
 // sets loop[0] when the shift is <= tolerance or not finite (the reference's
 // stopping rule, kmeans.cu:62-67); once it is set the launch does nothing, so a
 // driver may enqueue iterations before it has read whether the previous one
-// converged.  Requires shift_scratch.
-int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids,
-                    float* centroids, float* shift_scratch, cudaStream_t stream, int* loop = nullptr,
-                    float tolerance = 0.0f);
+// converged.  Requires shift_scratch.  With loop, the driver's options:
+// old_centroids may be centroids itself (updated in place); prev_out receives
+// the old centroids; zero_sums leaves sums and counts zero for the next
+// accumulation; host_state (host-mapped pinned memory) receives the four state
+// words once the launch is done, also after the loop has stopped.
+int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream, int* loop = nullptr, float tolerance = 0.0f,
+                    float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr);
 // sum((previous - current)^2) into shift_scratch[shift_scratch_floats() - 1].
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,
                  cudaStream_t stream);

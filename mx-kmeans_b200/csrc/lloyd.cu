@@ -19,7 +19,11 @@
 // enqueues up to kLookahead iterations beyond the last one whose state it has
 // read and never waits on the GPU between iterations (the reference reads the
 // shift back and synchronizes every iteration).  Labels, centroids and the
-// returned iteration count are those of the iteration that met the rule.
+// returned iteration count are those of the iteration that met the rule.  The
+// update kernel also keeps the previous centroids (the reference's copy at the
+// top of the iteration), zeroes the sums for the next iteration and writes the
+// loop state into pinned host memory, so an iteration issues no copies or
+// memsets.
 //
 // The reference's precision policy ignores the two-largest distance gap
 // (include/precision.hpp:20-26), so under it the driver's fused assignment does
@@ -235,12 +239,21 @@ constexpr int kLookahead = 8;
 // is nearly as good: measured at configs[3], every second iteration saves the
 // 0.21 ms sort on half of them and costs the GEMM < 0.02 ms.
 constexpr int kResortEvery = 2;
+// Full centroid-pair bound computations: the first kPairsFullFirst pruned
+// iterations, then every kPairsFullEvery-th (drift updates in between).
+constexpr int kPairsFullFirst = 3;
+constexpr int kPairsFullEvery = 4;
+// Drift updates only below this many rows per centroid: measured at configs[3]
+// (K = 2048), the looser bounds cost the GEMM ~1.6% of its time against a
+// ~22 us saving per iteration, a gain below ~4M rows on one GPU.
+constexpr int64_t kPairsDriftRowsPerCentroid = 2048;
 
 // Pinned host copies of the loop state words (one slot per iteration in flight)
 // and the events that say when each copy has landed.  Leased per call from a
 // per-device pool (MirrorLease) and kept until exit.
 struct LoopMirror {
     int* host = nullptr;
+    int* dev = nullptr;  // the same slots as the device sees them (host-mapped)
     cudaEvent_t ev[kLookahead + 1] = {};
     ~LoopMirror() {
         // an error return can leave copies into `host` in flight
@@ -252,7 +265,8 @@ struct LoopMirror {
     }
     int init() {
         MXK_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int) * 4 * (kLookahead + 1),
-                               cudaHostAllocDefault));
+                               cudaHostAllocMapped));
+        MXK_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev), host, 0));
         for (cudaEvent_t& e : ev) MXK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         return MXK_OK;
     }
@@ -374,6 +388,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&prev, kd));
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
+    MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
+    MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
     MXK_CUDA(cudaMemsetAsync(shift, 0, sizeof(float) * shift_scratch_floats(), stream));  // (the finalize ticket)
     // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
@@ -426,6 +442,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         return fail(MXK_ERR_COMM, "kmeans_mixed_sharded: the communicator was aborted; destroy and re-create it");
     const int inject_at = sharded && comm->rank == g_inject_rank.load() ? g_inject_iteration.load() : -1;
     bool cached_stale = true;  // the gathered copy of the cached rows does not follow the current order
+    int pruned_its = 0;        // pruned iterations enqueued so far
     for (int it = 0; it < options->max_iterations; ++it) {
         if (it == inject_at) {
             // the injected failure: drain what this rank has enqueued (its peers
@@ -462,11 +479,22 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         else
             MXK_CHECK(launch_l2_norm(k, d, centroids, cnorm, stream));
         if (prune_it) {
-            MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
+            // The centroid-pair bounds are computed in full (an FP32 Gram pass,
+            // K^2 D).  With few rows per centroid (a shard of a multi-GPU run)
+            // that pass weighs more than the slightly looser bounds cost the
+            // GEMM, so there it runs only in the first pruned iterations, while
+            // the centroids move most, and every kPairsFullEvery-th after; in
+            // between the bounds are lowered by the centroids' movement bounds
+            // (K x tiles work).  Either way the labels are exact.
+            const bool drift_ok = n < (int64_t)k * kPairsDriftRowsPerCentroid;
+            if (!drift_ok || pruned_its < kPairsFullFirst || pruned_its % kPairsFullEvery == 0)
+                MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
+            else
+                MXK_CHECK(launch_centroid_pairs_drift(k, d, cdelta, cst, dmin, tstats, loop, stream));
+            ++pruned_its;
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
                                        loop, stream));
         }
-        MXK_CUDA(cudaMemcpyAsync(prev, centroids, sizeof(float) * kd, cudaMemcpyDeviceToDevice, stream));
         const bool traced = it < trace.max_iterations;
         if (traced && trace.centroids)
             MXK_CUDA(cudaMemcpyAsync(trace.centroids + (int64_t)it * kd, centroids, sizeof(float) * kd,
@@ -564,9 +592,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         if (traced && trace.labels)
             MXK_CUDA(cudaMemcpyAsync(trace.labels + (int64_t)it * n, labels, sizeof(int) * n, cudaMemcpyDeviceToDevice,
                                      stream));
-        // kmeans.cu:62-65
-        MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
-        MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
+        // kmeans.cu:62-65 (sums and counts are zero: set before the loop, and
+        // left zero by every finalize)
         MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream, loop));
         if (sharded) {
             NcclApi& api = nccl();
@@ -577,9 +604,13 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             if (r != ncclSuccess) return fail_nccl("ncclAllReduce", r);
             if (r2 != ncclSuccess) return fail_nccl("ncclGroupEnd", r2);
         }
-        MXK_CHECK(launch_finalize(d, k, sums, counts, prev, centroids, shift, stream, loop, options->tolerance));
+        // The centroids are updated in place; the finalize kernel also keeps the
+        // old ones in prev (the next iteration's pruning bounds and, there, the
+        // previous centroids of update.cu:26-29), zeroes sums and counts, and
+        // writes the loop state into this iteration's pinned host slot.
         const int slot = it % (kLookahead + 1);
-        MXK_CUDA(cudaMemcpyAsync(mirror->host + 4 * slot, loop, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream));
+        MXK_CHECK(launch_finalize(d, k, sums, counts, centroids, centroids, shift, stream, loop, options->tolerance,
+                                  prev, true, mirror->dev + 4 * slot));
         MXK_CUDA(cudaEventRecord(mirror->ev[slot], stream));
         // Read the state of iteration it - lookahead.  FP32 iterations (whose
         // kernels do not consult the stop word) and verbose runs are read at once,

@@ -122,6 +122,36 @@ __global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const 
     }
 }
 
+// tst[t] = (min beta, max |c^|^2, max |c|^2, non-finite flag) over the
+// centroids of tile t, by one whole block of kPairThreads threads.
+__device__ void tile_stats_block(int k, int t, const float4* __restrict__ cst, float4* __restrict__ tst) {
+    __shared__ float4 part[kPairThreads / 32];
+    const float inf = __int_as_float(0x7f800000);
+    float4 m = make_float4(inf, 0.0f, 0.0f, 0.0f);
+    for (int j = threadIdx.x; j < kPairCols; j += kPairThreads) {
+        const int b = t * kPairCols + j;
+        if (b >= k) break;
+        const float4 v = cst[b];
+        m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
+        if (!(fabsf(v.x) < inf && v.y < inf && v.z < inf)) m.w = 1.0f;  // a non-finite centroid: no pruning
+    }
+    for (int o = 16; o; o >>= 1) {
+        m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
+        m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
+        m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
+        m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
+    }
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kPairThreads / 32; ++w) {
+            const float4 o = part[w];
+            m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
+        }
+        tst[t] = m;
+    }
+}
+
 // dmin[a * tiles + T]: a lower bound of min over c in T, c != a, of |c^ - c^_a|,
 // from the Gram entries G_ab = <c^_a, c^_b> (FP32, each accumulated by fmaf in
 // increasing feature order) and the quantized squared norms h = cst[].y:
@@ -136,33 +166,7 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
                                                                    float* __restrict__ dmin, float4* __restrict__ tst,
                                                                    const int* __restrict__ stop) {
     if (stop && *stop) return;
-    if (blockIdx.x == 0) {
-        __shared__ float4 part[kPairThreads / 32];
-        const float inf = __int_as_float(0x7f800000);
-        float4 m = make_float4(inf, 0.0f, 0.0f, 0.0f);
-        for (int j = threadIdx.x; j < kPairCols; j += kPairThreads) {
-            const int b = blockIdx.y * kPairCols + j;
-            if (b >= k) break;
-            const float4 v = cst[b];
-            m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
-            if (!(fabsf(v.x) < inf && v.y < inf && v.z < inf)) m.w = 1.0f;  // a non-finite centroid: no pruning
-        }
-        for (int o = 16; o; o >>= 1) {
-            m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
-            m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
-            m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
-            m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
-        }
-        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int w = 1; w < kPairThreads / 32; ++w) {
-                const float4 o = part[w];
-                m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
-            }
-            tst[blockIdx.y] = m;
-        }
-    }
+    if (blockIdx.x == 0) tile_stats_block(k, blockIdx.y, cst, tst);
     __shared__ __align__(16) float As[kPairChunk][kPairRows];
     __shared__ __align__(16) float Bs[kPairChunk][kPairCols];
     __shared__ float hb_s[kPairCols], sb_s[kPairCols];
@@ -232,6 +236,41 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
         }
         for (int o = 8; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (tx == 0 && a < k) dmin[(int64_t)a * tiles + tile] = m < inf ? sqrtf(fmaxf(m, 0.0f)) * (1.0f - 1e-6f) : 0.0f;
+    }
+}
+
+// Drift update of the pair bounds between two full computations: the quantized
+// centroids moved by at most delta (|c^_new - c^_old|), so by the triangle
+// inequality min over b in T of |c^_a - c^_b| shrinks by at most delta_a +
+// max over b in T of delta_b.  dmin[a][T] is lowered by that (with a margin
+// above the rounding of the two FP32 subtractions) and clamped at 0; a
+// non-finite delta leaves no bound.  Blocks [0, tiles) write the tile stats.
+__global__ void __launch_bounds__(kPairThreads) pair_drift_kernel(int k, int tiles, const float* __restrict__ delta,
+                                                                  const float4* __restrict__ cst,
+                                                                  float* __restrict__ dmin, float4* __restrict__ tst,
+                                                                  const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    if ((int)blockIdx.x < tiles) {
+        tile_stats_block(k, blockIdx.x, cst, tst);
+        return;
+    }
+    __shared__ unsigned tmax[kMaxPruneTiles];  // per tile max delta (non-negative: integer order)
+    for (int t = threadIdx.x; t < tiles; t += blockDim.x) tmax[t] = 0u;
+    __syncthreads();
+    for (int b = threadIdx.x; b < k; b += blockDim.x) {
+        const float v = delta[b];
+        atomicMax(&tmax[b / kPairCols], v == v ? __float_as_uint(v) : 0x7f800000u);  // NaN counts as infinite
+    }
+    __syncthreads();
+    const int a = (blockIdx.x - tiles) * blockDim.x + threadIdx.x;
+    if (a >= k) return;
+    const float da = delta[a];
+    const float inf = __int_as_float(0x7f800000);
+    for (int t = 0; t < tiles; ++t) {
+        float* p = dmin + (int64_t)a * tiles + t;
+        const float x = *p, y = da, z = __uint_as_float(tmax[t]);
+        const float v = (x - y - z) - 4e-7f * (x + y + z);
+        *p = (v < inf && y < inf && z < inf) ? fmaxf(v, 0.0f) : 0.0f;  // (false for NaN: no bound)
     }
 }
 
@@ -323,6 +362,17 @@ int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, fl
     LaunchScope scope("centroid_pairs", stream);
     pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0, stream>>>(
         k, d, tiles, chat, cst, dmin, tst, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* cst, float* dmin, float4* tst,
+                                const int* stop, cudaStream_t stream) {
+    MXK_REQUIRE(prune_supported(k, d), "centroid pairs: unsupported shape");
+    const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
+    LaunchScope scope("centroid_pairs_drift", stream);
+    pair_drift_kernel<<<(unsigned)(tiles + (k + kPairThreads - 1) / kPairThreads), kPairThreads, 0, stream>>>(
+        k, tiles, delta, cst, dmin, tst, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }

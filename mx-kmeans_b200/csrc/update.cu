@@ -191,21 +191,39 @@ __device__ __forceinline__ void apply_stop_rule(int* loop, float s, float tolera
 // the same iteration without exchanging it.  With `loop` (the Lloyd driver's
 // state words) the CTA that finishes last (a ticket on *done, which it resets
 // to 0) also sums the partials in index order into *total_out and applies the
-// stopping rule; once loop[0] is set the launch does nothing.
-__global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float* __restrict__ sums,
-                                                       const int* __restrict__ counts, const float* __restrict__ old,
-                                                       float* __restrict__ centroids, float* __restrict__ partials,
-                                                       int* __restrict__ loop, unsigned* __restrict__ done,
-                                                       float* __restrict__ total_out, float tolerance) {
-    if (loop && *(volatile int*)loop) return;  // converged: the centroids stay as they are
+// stopping rule; once loop[0] is set the launch does nothing except publish
+// the state.  Driver options: old may be centroids itself (each element is
+// read, then written, by one thread); prev_out receives the old centroids;
+// zero_sums leaves sums and counts zeroed for the next accumulation;
+// host_state (host-mapped) receives the four state words.
+__device__ __forceinline__ void publish_state(const int* loop, int* host_state) {
+    if (!host_state) return;
+    volatile const int* src = loop;
+    volatile int* dst = host_state;
+    for (int i = 0; i < 4; ++i) dst[i] = src[i];
+    __threadfence_system();
+}
+
+__global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __restrict__ sums, int* __restrict__ counts,
+                                                       const float* old, float* centroids, float* __restrict__ prev_out,
+                                                       float* __restrict__ partials, int* __restrict__ loop,
+                                                       unsigned* __restrict__ done, float* __restrict__ total_out,
+                                                       float tolerance, int zero_sums, int* __restrict__ host_state) {
+    if (loop && *(volatile int*)loop) {  // converged: the centroids stay as they are
+        if (blockIdx.x == 0 && threadIdx.x == 0) publish_state(loop, host_state);
+        return;
+    }
     __shared__ float warp_sum[8];
     const int64_t total = (int64_t)k * d;
     float local = 0.0f;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int cnt = counts[i / d];
+        const float o = old[i];
         // An empty cluster keeps its previous center (update.cu:26-29).
-        const float v = cnt ? sums[i] / (float)cnt : old[i];
-        const float diff = old[i] - v;
+        const float v = cnt ? sums[i] / (float)cnt : o;
+        const float diff = o - v;
+        if (prev_out) prev_out[i] = o;
+        if (zero_sums) sums[i] = 0.0f;
         centroids[i] = v;
         local += diff * diff;
     }
@@ -238,6 +256,12 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, const float
         *total_out = s;
         *done = 0u;
         apply_stop_rule(loop, s, tolerance);
+        __threadfence();
+        publish_state(loop, host_state);
+    }
+    if (zero_sums) {  // every CTA has read its counts (it took a ticket after its loop)
+        __syncthreads();
+        for (int c = threadIdx.x; c < k; c += blockDim.x) counts[c] = 0;
     }
 }
 
@@ -347,8 +371,10 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
 int64_t shift_scratch_floats() { return kShiftBlocks + 2; }
 int64_t shift_total_index() { return kShiftBlocks; }
 
-int launch_finalize(int d, int k, const float* sums, const int* counts, const float* old_centroids, float* centroids,
-                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance) {
+int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
+                    bool zero_sums, int* host_state) {
+    MXK_REQUIRE(!(zero_sums || host_state) || loop, "finalize: zeroing and the host state need the loop words");
     MXK_REQUIRE(!loop || shift_scratch, "finalize: the loop state needs the shift scratch");
     const int64_t total = (int64_t)k * d;
     int64_t blocks = (total + 255) / 256;
@@ -356,9 +382,9 @@ int launch_finalize(int d, int k, const float* sums, const int* counts, const fl
     {
         LaunchScope scope("finalize", stream);
         finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-            d, k, sums, counts, old_centroids, centroids, shift_scratch, loop,
+            d, k, sums, counts, old_centroids, centroids, prev_out, shift_scratch, loop,
             loop ? reinterpret_cast<unsigned*>(shift_scratch + kShiftBlocks + 1) : nullptr,
-            loop ? shift_scratch + kShiftBlocks : nullptr, tolerance);
+            loop ? shift_scratch + kShiftBlocks : nullptr, tolerance, zero_sums ? 1 : 0, host_state);
         MXK_CUDA(cudaGetLastError());
     }
     if (shift_scratch && !loop) {  // (with loop the finalize kernel's last CTA sums the partials)
