@@ -505,6 +505,7 @@ def main():
     mxk.profile_enable(True)
     launches0 = mxk.launch_count()
     mxk.gemm_tiles_multiplied(reset=True)
+    mxk.gemm_rows_processed(reset=True)
     barrier()
     t_wall0 = time.monotonic()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -517,6 +518,7 @@ def main():
     t_wall1 = time.monotonic()
     launches = mxk.launch_count() - launches0
     tiles_done = mxk.gemm_tiles_multiplied(reset=True)
+    rows_done = mxk.gemm_rows_processed(reset=True)
     stats = mxk.profile_read()
     mxk.profile_enable(False)
     clocks = sampler.stop(window=(t_wall0, t_wall1))
@@ -570,14 +572,16 @@ def main():
         unpruned = iters * ((rows + 127) // 128) * ((k + 191) // 192) * tile_flops
         seconds = gemm[1] / 1e3
         tflops = executed / seconds / 1e12
-        # algorithmic DRAM bytes per launch: each point's row (FP32, quantized in
-        # the kernel, at D = 128; else its MXFP8 bytes and scales), its id, norm,
-        # previous label, new label and distance, and in the pruned iterations
-        # (all but the first) its 8-byte bound record
+        # algorithmic DRAM bytes: for each point row the GEMM processed (rows
+        # whose labels the bounds proved beforehand leave it), the row (FP32,
+        # quantized in the kernel, at D = 128; else its MXFP8 bytes and scales),
+        # its id, norm, previous label, new label and distance, and in the
+        # pruned iterations (all but each call's first) its 8-byte bound record
         per_row = 4.0 * d_pad if d_pad == 128 else d_pad + d_pad / 32.0
-        it_per_step = max(iters / max(args.steps, 1), 1.0)
-        alg_bytes = rows * (per_row + 20.0 + 8.0 * (it_per_step - 1) / it_per_step)
-        gbs = alg_bytes * iters / seconds / 1e9
+        first_rows = rows * args.steps  # the first iteration of each call is unpruned
+        bytes_total = rows_done * (per_row + 20.0) + max(rows_done - first_rows, 0) * 8.0
+        alg_bytes = bytes_total / max(iters, 1)
+        gbs = bytes_total / seconds / 1e9
         # the binding roofline is the one whose ideal time is longer
         hbm_bound = alg_bytes / (peak_gbs * 1e9) > (executed / max(iters, 1)) / (peak_tf * 1e12)
         traffic = measured_traffic(rows, cfg)
@@ -594,13 +598,15 @@ def main():
                     "executed_flops_per_iteration": executed / max(iters, 1),
                     "nominal_flops_per_iteration": flops_per_iter,
                     "tiles_multiplied_fraction": executed / unpruned if unpruned else None,
+                    "rows_processed_fraction": rows_done / (rows * iters) if iters else None,
                     "nominal_tflops": flops_per_iter * iters / (gemm[1] / 1e3) / 1e12,
                     "peak_source": f"hbm_gbs, 2 x bf16_tflops_sustained of {pk_kind} MEASURED_PEAKS.json "
                                    "(dense MXFP8 tensor rate is twice BF16)"}
     kernel_ms = {kk: {"launches": v[0], "total_ms": round(v[1], 3)}
                  for kk, v in sorted(stats.items(), key=lambda kv: -kv[1][1])}
     update = update_roofline(stats, rows, d_pad, peak_gbs)
-    quant = quantize_roofline(stats, rows, d_pad, peak_gbs)
+    # (the point quantize encodes the rows the GEMM processes)
+    quant = quantize_roofline(stats, rows_done / max(iters, 1), d_pad, peak_gbs)
 
     cpu = None
     if rank == 0 and world == 1 and not args.quick:

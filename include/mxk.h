@@ -54,6 +54,11 @@ int mxk_release_workspace(void);
  * current device's MX GEMM launches have multiplied since the last reset
  * (synchronizes the device); pruned tiles are not counted. */
 int mxk_gemm_tiles_multiplied(unsigned long long* count, int reset);
+/* Measurement aid, no reference counterpart: the number of point rows the
+ * current device's MX GEMM launches have processed since the last reset
+ * (synchronizes the device); rows whose labels the Lloyd loop's bounds proved
+ * beforehand are not counted. */
+int mxk_gemm_rows_processed(unsigned long long* count, int reset);
 
 /* ---- ops (include/kmeans.cuh:23-47) ------------------------------------ */
 

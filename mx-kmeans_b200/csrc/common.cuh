@@ -67,6 +67,8 @@ unsigned* device_error_word();
 // Per-device count of 128 x 192 tiles the MX GEMM has multiplied (all K chunks),
 // for reporting the tensor work actually executed when tiles are pruned.
 unsigned long long* device_tile_counter();
+// Per-device count of the point rows the MX GEMM has processed.
+unsigned long long* device_row_counter();
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved through the runtime,
 // so the library has no link-time dependency on libcuda).

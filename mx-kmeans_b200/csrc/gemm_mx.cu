@@ -117,6 +117,7 @@ struct GemmParams {
     // multiplied nor scanned).  Every bit set when null.  Needs tiles_n <= 64.
     const uint64_t* tile_mask;
     unsigned long long* tiles_done;  // count of multiplied 128 x 192 tiles (all K chunks)
+    unsigned long long* rows_done;   // count of processed point rows
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
     int best_dist_stride;  // best_dist[point * best_dist_stride]
     const float2* row_bound;  // optional (argmin): MxArgmin::row_bound
@@ -416,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t tiles_m = (mrows + kBM - 1) / kBM;
     const int tiles_n = (int)((p.n + kBN - 1) / kBN);
 
+    if (threadIdx.x == 0 && blockIdx.x == 0 && p.rows_done) atomicAdd(p.rows_done, (unsigned long long)mrows);
     if (threadIdx.x == 0) {
         // fused quantize: the two quantizer warps arrive
         for (int i = 0; i < kMaxAStages; ++i)
@@ -1178,6 +1180,7 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
     }
     p.err = device_error_word();
     p.tiles_done = device_tile_counter();
+    p.rows_done = device_row_counter();
     if (!p.err) return fail(MXK_ERR_CUDA, "gemm_mx: cannot allocate the device error word");
 
     int max_smem = 0, dev = 0;

@@ -129,13 +129,30 @@ int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, fl
 // bounds (delta, from launch_centroid_prep), and tst as above.
 int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* cst, float* dmin, float4* tst,
                                 const int* stop, cudaStream_t stream);
+// Row compaction of the pruned fused iteration (launch_tile_mask's `work`):
+// device buffers for the rows that stay in the GEMM, in visiting order.
+struct WorkRows {
+    int* pid = nullptr;            // [rows] their point ids
+    float2* rb = nullptr;          // [rows] their MxArgmin::row_bound records
+    unsigned long long* cmask = nullptr;  // [row tiles] centroid-tile masks of the compacted 128-row tiles
+    uint4* need_bits = nullptr;    // [row tiles] scratch: which rows of each tile stay
+    int* counts = nullptr;         // [row tiles] scratch
+    int* offsets = nullptr;        // [row tiles] scratch
+    int* rows = nullptr;           // [1] how many rows stay (0 once the loop has stopped)
+};
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
 // and the current (cst) and previous (cst_old) centroid stats; row_bound
-// (optional, one per row) receives MxArgmin::row_bound's records.
-int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
+// (optional, one per row) receives MxArgmin::row_bound's records.  With work:
+// a row whose bounds prove that every other centroid is strictly farther than
+// its previous label's keeps that label and leaves the GEMM (its pinfo
+// distance becomes its upper bound); the other rows are compacted into work
+// (ids, records, masks of the compacted tiles, count), for a GEMM launched on
+// work->pid with rows_dev = work->rows.
+int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream);
+                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream,
+                     WorkRows* work = nullptr);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

@@ -411,6 +411,21 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&tmask, (n + kPointTileRows - 1) / kPointTileRows));
         MXK_CHECK(ws.alloc(&rbound, n));
     }
+    // Row compaction in pruned iterations (not with the point cache, whose GEMM
+    // reads contiguous pre-gathered point tiles): rows whose label the bounds
+    // prove leave the GEMM.
+    const bool compact = prune && !cache;
+    WorkRows work;
+    if (compact) {
+        const int64_t row_tiles = (n + kPointTileRows - 1) / kPointTileRows;
+        MXK_CHECK(ws.alloc(&work.pid, n));
+        MXK_CHECK(ws.alloc(&work.rb, n));
+        MXK_CHECK(ws.alloc(&work.cmask, row_tiles));
+        MXK_CHECK(ws.alloc(&work.need_bits, row_tiles));
+        MXK_CHECK(ws.alloc(&work.counts, row_tiles));
+        MXK_CHECK(ws.alloc(&work.offsets, row_tiles));
+        MXK_CHECK(ws.alloc(&work.rows, 1));
+    }
     int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)
     MXK_CHECK(ws.alloc(&loop, 4));
     MirrorLease mirror;
@@ -493,7 +508,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 MXK_CHECK(launch_centroid_pairs_drift(k, d, cdelta, cst, dmin, tstats, loop, stream));
             ++pruned_its;
             MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
-                                       loop, stream));
+                                       loop, stream, compact ? &work : nullptr));
         }
         const bool traced = it < trace.max_iterations;
         if (traced && trace.centroids)
@@ -514,6 +529,11 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         } else if (forced8) {
             // Every point is in the MXFP8 group, in the visiting sequence `ord`;
             // the group's row count is loop[3] (n, or 0 once the loop stopped).
+            // In compacted iterations the quantize and GEMM take only the rows
+            // whose labels the bounds left open (work.pid, count work.rows).
+            const bool compacted = compact && prune_it;
+            const int* gemm_pid = compacted ? work.pid : ord;
+            const int* gemm_rows = compacted ? work.rows : loop + 3;
             if (!prep)  // (else the centroid pass above wrote the MXFP8 centroids)
                 MXK_CHECK(launch_quantize(8, k, d, centroids, nullptr, qcent, cscales, nullptr, nullptr, stream,
                                           kCentroidTileRows, "quantize_centroids"));
@@ -526,21 +546,21 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                     MXK_CHECK(launch_gather_mxfp8_rows(n, d, qnat, snat, ord, qpoints, pscales, loop, stream));
                 cached_stale = false;
             } else if (!fused_q) {
-                MXK_CHECK(launch_quantize(8, n, d, points, ord, qpoints, pscales, nullptr, loop + 3, stream,
+                MXK_CHECK(launch_quantize(8, n, d, points, gemm_pid, qpoints, pscales, nullptr, gemm_rows, stream,
                                           kPointTileRows, "quantize_points"));
             }
             MxArgmin am;
             am.point_norms = pnorm;
             am.centroid_norms = cnorm;
-            am.pid = ord;
+            am.pid = gemm_pid;
             am.labels = labels;
             am.gaps = nullptr;
             am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
-            am.tile_mask = prune_it ? tmask : nullptr;
-            am.row_bound = prune_it ? rbound : nullptr;
+            am.tile_mask = prune_it ? (compacted ? reinterpret_cast<const uint64_t*>(work.cmask) : tmask) : nullptr;
+            am.row_bound = prune_it ? (compacted ? work.rb : rbound) : nullptr;
             am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
-            MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, loop + 3, stream,
+            MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows, stream,
                                      true, fused_q ? points : nullptr, n));
             if (traced && trace.group_sizes)  // (0, 0, rows of the MXFP8 group)
                 MXK_CUDA(cudaMemcpyAsync(trace.group_sizes + 3 * it + 2, loop + 3, sizeof(int),

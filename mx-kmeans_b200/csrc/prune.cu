@@ -281,19 +281,27 @@ __device__ __forceinline__ float rho_bound(float px, float hx2, float pc, float 
 }
 
 // One block per 128-row point tile: the union over its rows of the centroid
-// tiles the bounds cannot exclude.
+// tiles the bounds cannot exclude.  With `compact` (the fused path's row
+// compaction) a row whose every other centroid -- its own tile's included,
+// through dmin[a][own], which leaves a out -- lies strictly beyond its upper
+// bound keeps its label: it is left out of the GEMM (need_bits, counts), its
+// distance for the next iteration's bounds becomes that upper bound, and the
+// tile's mask is the union over the rows that remain; cmask[blockIdx.x] is
+// zeroed for the compacted masks of work_scatter_kernel.
 __global__ void __launch_bounds__(128) tile_mask_kernel(
     int64_t rows, int k, int d, int tiles, int tile_cols, const int* __restrict__ pid,
-    const int* __restrict__ prev_label, const float4* __restrict__ pinfo, const float4* __restrict__ cst,
+    const int* __restrict__ prev_label, float4* __restrict__ pinfo, const float4* __restrict__ cst,
     const float4* __restrict__ cst_old,
     const float4* __restrict__ tst, const float* __restrict__ delta, const float* __restrict__ dmin,
-    uint64_t* __restrict__ mask, float2* __restrict__ row_bound, const int* __restrict__ stop) {
+    uint64_t* __restrict__ mask, float2* __restrict__ row_bound, int compact, uint4* __restrict__ need_bits,
+    int* __restrict__ tile_count, uint64_t* __restrict__ cmask, const int* __restrict__ stop) {
     if (stop && *stop) return;
     const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
     const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
     const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
     const float inf = __int_as_float(0x7f800000);
     uint64_t m = 0;
+    bool need = false;
     // (bound on the row's nearest distance, its previous label) for the GEMM's
     // screen; (inf, -1) when no finite bound holds
     float2 rb = make_float2(inf, __int_as_float(-1));
@@ -301,6 +309,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
         const int64_t x = pid ? pid[row] : row;
         const int a = prev_label[x];
         m = all;
+        need = true;
         if ((unsigned)a < (unsigned)k) {
             const float4 pi = pinfo[x];  // (previous distance, alpha_x, |x^|^2, |x|^2)
             const float dp = pi.x, px = pi.w;
@@ -312,6 +321,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
             const float um = u + 1e-4f * (fabsf(u) + fabsf(ps.x) + fabsf(now.x)) + 1e-30f;
             if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(ps.x) < inf) {  // false for NaN too: keep every tile
                 m = 1ull << (a / tile_cols);  // its own tile
+                need = false;
                 // The screen only needs some upper bound: a wider margin costs
                 // nothing measurable and keeps it far from the rounding terms.
                 const float us = um + 1e-3f * (fabsf(um) + fabsf(ps.x) + fabsf(now.x));
@@ -322,19 +332,109 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
                     const float g = fmaxf(dm[t] - r, 0.0f);
                     const float lb = g * g * (1.0f - 1e-6f) + ps.x + ts.x - rho_bound(px, ps.y, ts.z, ts.y, kappa);
                     const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(ps.x) + fabsf(ts.x));
-                    if (!(lbm > um) || ts.w != 0.0f) m |= 1ull << t;
+                    if (!(lbm > um) || ts.w != 0.0f) {
+                        m |= 1ull << t;
+                        need = true;
+                    }
                 }
+                if (compact && !need) pinfo[x].x = um;  // the label stands; its distance bound for next time
             }
         }
     }
+    if (compact && !need) m = 0;
     if (row_bound && row < rows) row_bound[row] = rb;
     // union over the 128 rows
     m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
         ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
+    const unsigned nb = __ballot_sync(0xffffffffu, need);
     __shared__ uint64_t part[4];
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    __shared__ unsigned bits[4];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m, bits[threadIdx.x >> 5] = nb;
     __syncthreads();
-    if (threadIdx.x == 0) mask[blockIdx.x] = part[0] | part[1] | part[2] | part[3];
+    if (threadIdx.x == 0) {
+        mask[blockIdx.x] = part[0] | part[1] | part[2] | part[3];
+        if (compact) {
+            need_bits[blockIdx.x] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+            tile_count[blockIdx.x] = __popc(bits[0]) + __popc(bits[1]) + __popc(bits[2]) + __popc(bits[3]);
+            cmask[blockIdx.x] = 0ull;
+        }
+    }
+}
+
+// Exclusive prefix sum of the per-tile counts of rows that stay in the GEMM
+// (one block): offsets[i], and *work_rows = the total (0 once the loop has
+// stopped, so the GEMM launches of later iterations do nothing).
+__global__ void __launch_bounds__(1024) work_scan_kernel(int ntiles, const int* __restrict__ counts,
+                                                         int* __restrict__ offsets, int* __restrict__ work_rows,
+                                                         const int* __restrict__ stop) {
+    if (stop && *(volatile const int*)stop) {
+        if (threadIdx.x == 0) *work_rows = 0;
+        return;
+    }
+    __shared__ int warp_tot[32];
+    const int per = (ntiles + blockDim.x - 1) / blockDim.x;
+    const int b = threadIdx.x * per, e = min(ntiles, b + per);
+    int sum = 0;
+    for (int i = b; i < e; ++i) sum += counts[i];
+    // block-wide exclusive scan of the per-thread sums
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int incl = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += v;
+        }
+        warp_tot[lane] = t;  // inclusive over warps
+    }
+    __syncthreads();
+    int run = incl - sum + (w > 0 ? warp_tot[w - 1] : 0);
+    for (int i = b; i < e; ++i) {
+        offsets[i] = run;
+        run += counts[i];
+    }
+    if (threadIdx.x == blockDim.x - 1) *work_rows = run;
+}
+
+// One block per 128-row point tile: the rows that stay in the GEMM, in order,
+// to work_pid / work_rb at the tile's offset; the tile's mask ORed into the
+// (at most two) compacted 128-row tiles its rows land in.
+__global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const int* __restrict__ pid,
+                                                           const float2* __restrict__ row_bound,
+                                                           const uint4* __restrict__ need_bits,
+                                                           const int* __restrict__ offsets,
+                                                           const int* __restrict__ counts,
+                                                           const uint64_t* __restrict__ mask,
+                                                           int* __restrict__ work_pid, float2* __restrict__ work_rb,
+                                                           unsigned long long* __restrict__ cmask,
+                                                           const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    const int cnt = counts[blockIdx.x];
+    if (cnt == 0) return;
+    const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
+    const uint4 nb = need_bits[blockIdx.x];
+    const unsigned words[4] = {nb.x, nb.y, nb.z, nb.w};
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int off = offsets[blockIdx.x];
+    if ((words[w] >> lane) & 1u) {
+        int before = __popc(words[w] & ((1u << lane) - 1u));
+        for (int v = 0; v < w; ++v) before += __popc(words[v]);
+        const int pos = off + before;
+        work_pid[pos] = pid ? pid[row] : (int)row;
+        work_rb[pos] = row_bound[row];
+    }
+    if (threadIdx.x == 0) {
+        const uint64_t m = mask[blockIdx.x];
+        const int j0 = off >> 7, j1 = (off + cnt - 1) >> 7;
+        atomicOr(cmask + j0, (unsigned long long)m);
+        if (j1 != j0) atomicOr(cmask + j1, (unsigned long long)m);
+    }
 }
 
 }  // namespace
@@ -377,18 +477,39 @@ int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* 
     return MXK_OK;
 }
 
-int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, const float4* pinfo,
+int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream) {
-    if (rows <= 0) return MXK_OK;
+                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream,
+                     WorkRows* work) {
+    if (rows <= 0 && !work) return MXK_OK;
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
+    MXK_REQUIRE(!work || (row_bound && work->pid && work->rb && work->need_bits && work->counts && work->offsets &&
+                          work->cmask && work->rows),
+                "tile mask: incomplete row-compaction buffers");
     const int64_t blocks = (rows + kPointTileRows - 1) / kPointTileRows;
-    LaunchScope scope("tile_mask", stream);
-    tile_mask_kernel<<<(unsigned)blocks, 128, 0, stream>>>(rows, k, d, tiles, kCentroidTileRows, pid, prev_label,
-                                                           pinfo, cst, cst_old, tst, delta, dmin, mask, row_bound,
-                                                           stop);
-    MXK_CUDA(cudaGetLastError());
+    MXK_REQUIRE(blocks < (1ll << 31), "tile mask: too many rows");
+    if (blocks > 0) {
+        LaunchScope scope("tile_mask", stream);
+        tile_mask_kernel<<<(unsigned)blocks, 128, 0, stream>>>(
+            rows, k, d, tiles, kCentroidTileRows, pid, prev_label, pinfo, cst, cst_old, tst, delta, dmin, mask,
+            row_bound, work ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
+            work ? reinterpret_cast<uint64_t*>(work->cmask) : nullptr, stop);
+        MXK_CUDA(cudaGetLastError());
+    }
+    if (!work) return MXK_OK;
+    {
+        LaunchScope scope("work_scan", stream);
+        work_scan_kernel<<<1, 1024, 0, stream>>>((int)blocks, work->counts, work->offsets, work->rows, stop);
+        MXK_CUDA(cudaGetLastError());
+    }
+    if (blocks > 0) {
+        LaunchScope scope("work_scatter", stream);
+        work_scatter_kernel<<<(unsigned)blocks, 128, 0, stream>>>(rows, pid, row_bound, work->need_bits,
+                                                                   work->offsets, work->counts, mask, work->pid,
+                                                                   work->rb, work->cmask, stop);
+        MXK_CUDA(cudaGetLastError());
+    }
     return MXK_OK;
 }
 

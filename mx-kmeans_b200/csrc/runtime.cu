@@ -169,6 +169,20 @@ unsigned long long* device_tile_counter() {
     return counters[dev];
 }
 
+unsigned long long* device_row_counter() {
+    static unsigned long long* counters[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!counters[dev]) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+        counters[dev] = static_cast<unsigned long long*>(p);
+    }
+    return counters[dev];
+}
+
 int check_device_error(cudaStream_t stream) {
     unsigned* w = device_error_word();
     if (!w) return fail(MXK_ERR_CUDA, "cannot allocate the device error word");
@@ -302,6 +316,15 @@ uint64_t mxk_launch_count(void) { return mxk::g_launches.load(); }
 int mxk_gemm_tiles_multiplied(unsigned long long* count, int reset) {
     unsigned long long* c = mxk::device_tile_counter();
     if (!c) return mxk::fail(MXK_ERR_CUDA, "gemm_tiles_multiplied: no counter on the current device");
+    MXK_CUDA(cudaDeviceSynchronize());
+    MXK_CUDA(cudaMemcpy(count, c, sizeof(*count), cudaMemcpyDeviceToHost));
+    if (reset) MXK_CUDA(cudaMemset(c, 0, sizeof(*c)));
+    return MXK_OK;
+}
+
+int mxk_gemm_rows_processed(unsigned long long* count, int reset) {
+    unsigned long long* c = mxk::device_row_counter();
+    if (!c) return mxk::fail(MXK_ERR_CUDA, "gemm_rows_processed: no counter on the current device");
     MXK_CUDA(cudaDeviceSynchronize());
     MXK_CUDA(cudaMemcpy(count, c, sizeof(*count), cudaMemcpyDeviceToHost));
     if (reset) MXK_CUDA(cudaMemset(c, 0, sizeof(*c)));

@@ -63,6 +63,7 @@ SIGNATURES = {
     "mxk_check_wait_timeout": ([ctypes.c_longlong, _P, _P], _I),
     "mxk_release_workspace": ([], _I),
     "mxk_gemm_tiles_multiplied": ([ctypes.POINTER(ctypes.c_ulonglong), _I], _I),
+    "mxk_gemm_rows_processed": ([ctypes.POINTER(ctypes.c_ulonglong), _I], _I),
     "mxk_init_farthest": ([_I64, _I, _I, _P, _P, _P], _I),
     "mxk_init_kmeanspp": ([_I64, _I, _I, _P, _P, ctypes.c_uint32, _P], _I),
     "mxk_gemm_mx": ([_I, _I64, _I64, _I, _P, _P, _P, _P, _P, _P], _I),
@@ -173,6 +174,14 @@ def gemm_tiles_multiplied(reset=False):
     last reset (pruned tiles excluded)."""
     v = ctypes.c_ulonglong(0)
     check(load().mxk_gemm_tiles_multiplied(ctypes.byref(v), 1 if reset else 0))
+    return v.value
+
+
+def gemm_rows_processed(reset=False):
+    """Point rows processed by the MX GEMM on the current device since the last
+    reset (rows whose labels the loop's bounds proved are not counted)."""
+    v = ctypes.c_ulonglong(0)
+    check(load().mxk_gemm_rows_processed(ctypes.byref(v), 1 if reset else 0))
     return v.value
 
 
