@@ -138,6 +138,7 @@ struct WorkRows {
     uint4* need_bits = nullptr;    // [row tiles] scratch: which rows of each tile stay
     int* counts = nullptr;         // [row tiles] scratch
     int* offsets = nullptr;        // [row tiles] scratch
+    int* seg_total = nullptr;      // [row tiles / 1024 + 1] scratch
     int* rows = nullptr;           // [1] how many rows stay (0 once the loop has stopped)
 };
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that

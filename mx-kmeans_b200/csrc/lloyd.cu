@@ -424,6 +424,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&work.need_bits, row_tiles));
         MXK_CHECK(ws.alloc(&work.counts, row_tiles));
         MXK_CHECK(ws.alloc(&work.offsets, row_tiles));
+        MXK_CHECK(ws.alloc(&work.seg_total, row_tiles / 1024 + 1));
         MXK_CHECK(ws.alloc(&work.rows, 1));
     }
     int* loop = nullptr;  // [0] stopped, [1] completed iterations, [2] non-finite shift, [3] rows (0 once stopped)

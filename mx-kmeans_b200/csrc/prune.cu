@@ -361,24 +361,20 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     }
 }
 
-// Exclusive prefix sum of the per-tile counts of rows that stay in the GEMM
-// (one block): offsets[i], and *work_rows = the total (0 once the loop has
-// stopped, so the GEMM launches of later iterations do nothing).
-__global__ void __launch_bounds__(1024) work_scan_kernel(int ntiles, const int* __restrict__ counts,
-                                                         int* __restrict__ offsets, int* __restrict__ work_rows,
-                                                         const int* __restrict__ stop) {
-    if (stop && *(volatile const int*)stop) {
-        if (threadIdx.x == 0) *work_rows = 0;
-        return;
-    }
+// Segmented exclusive prefix sum of the per-tile counts of rows that stay in
+// the GEMM: block s scans tiles [1024 s, 1024 s + 1024) into offsets[] (local
+// to the segment) and writes the segment's total to seg_total[s];
+// work_scatter_kernel adds the totals of the segments before its own.
+constexpr int kScanSeg = 1024;
+__global__ void __launch_bounds__(kScanSeg) work_scan_kernel(int ntiles, const int* __restrict__ counts,
+                                                             int* __restrict__ offsets, int* __restrict__ seg_total,
+                                                             const int* __restrict__ stop) {
+    if (stop && *stop) return;
     __shared__ int warp_tot[32];
-    const int per = (ntiles + blockDim.x - 1) / blockDim.x;
-    const int b = threadIdx.x * per, e = min(ntiles, b + per);
-    int sum = 0;
-    for (int i = b; i < e; ++i) sum += counts[i];
-    // block-wide exclusive scan of the per-thread sums
+    const int i = blockIdx.x * kScanSeg + threadIdx.x;
+    const int c = i < ntiles ? counts[i] : 0;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int incl = sum;
+    int incl = c;
     for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
@@ -386,7 +382,7 @@ __global__ void __launch_bounds__(1024) work_scan_kernel(int ntiles, const int* 
     if (lane == 31) warp_tot[w] = incl;
     __syncthreads();
     if (w == 0) {
-        int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+        int t = warp_tot[lane];
         for (int o = 1; o < 32; o <<= 1) {
             const int v = __shfl_up_sync(0xffffffffu, t, o);
             if (lane >= o) t += v;
@@ -394,34 +390,55 @@ __global__ void __launch_bounds__(1024) work_scan_kernel(int ntiles, const int* 
         warp_tot[lane] = t;  // inclusive over warps
     }
     __syncthreads();
-    int run = incl - sum + (w > 0 ? warp_tot[w - 1] : 0);
-    for (int i = b; i < e; ++i) {
-        offsets[i] = run;
-        run += counts[i];
-    }
-    if (threadIdx.x == blockDim.x - 1) *work_rows = run;
+    if (i < ntiles) offsets[i] = incl - c + (w > 0 ? warp_tot[w - 1] : 0);
+    if (threadIdx.x == 0) seg_total[blockIdx.x] = warp_tot[31];
 }
 
 // One block per 128-row point tile: the rows that stay in the GEMM, in order,
 // to work_pid / work_rb at the tile's offset; the tile's mask ORed into the
 // (at most two) compacted 128-row tiles its rows land in.
+// Block 0 also writes *work_rows, the number of rows that stay (0 once the loop
+// has stopped, so that the GEMM launches of later iterations do nothing).
 __global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const int* __restrict__ pid,
                                                            const float2* __restrict__ row_bound,
                                                            const uint4* __restrict__ need_bits,
                                                            const int* __restrict__ offsets,
                                                            const int* __restrict__ counts,
+                                                           const int* __restrict__ seg_total, int nseg,
                                                            const uint64_t* __restrict__ mask,
                                                            int* __restrict__ work_pid, float2* __restrict__ work_rb,
                                                            unsigned long long* __restrict__ cmask,
-                                                           const int* __restrict__ stop) {
-    if (stop && *stop) return;
+                                                           int* __restrict__ work_rows, const int* __restrict__ stop) {
+    const bool stopped = stop && *stop;
+    __shared__ int seg_base;
+    if (threadIdx.x < 32) {  // the totals of the segments before this tile's (all of them for block 0)
+        const int seg = blockIdx.x / kScanSeg;
+        const int upto = blockIdx.x == 0 ? nseg : seg;
+        int acc = 0, mine = 0;
+        if (!stopped)
+            for (int s2 = threadIdx.x; s2 < upto; s2 += 32) {
+                const int v = seg_total[s2];
+                acc += v;
+                if (s2 < seg) mine += v;
+            }
+        for (int o = 16; o; o >>= 1) {
+            acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            mine += __shfl_xor_sync(0xffffffffu, mine, o);
+        }
+        if (threadIdx.x == 0) {
+            seg_base = mine;
+            if (blockIdx.x == 0) *work_rows = stopped ? 0 : acc;
+        }
+    }
+    if (stopped || (int64_t)blockIdx.x * 128 >= rows) return;  // (block 0 of an empty shard: the count only)
+    __syncthreads();
     const int cnt = counts[blockIdx.x];
     if (cnt == 0) return;
     const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
     const uint4 nb = need_bits[blockIdx.x];
     const unsigned words[4] = {nb.x, nb.y, nb.z, nb.w};
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int off = offsets[blockIdx.x];
+    const int off = seg_base + offsets[blockIdx.x];
     if ((words[w] >> lane) & 1u) {
         int before = __popc(words[w] & ((1u << lane) - 1u));
         for (int v = 0; v < w; ++v) before += __popc(words[v]);
@@ -485,7 +502,7 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
     MXK_REQUIRE(!work || (row_bound && work->pid && work->rb && work->need_bits && work->counts && work->offsets &&
-                          work->cmask && work->rows),
+                          work->seg_total && work->cmask && work->rows),
                 "tile mask: incomplete row-compaction buffers");
     const int64_t blocks = (rows + kPointTileRows - 1) / kPointTileRows;
     MXK_REQUIRE(blocks < (1ll << 31), "tile mask: too many rows");
@@ -498,16 +515,18 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
         MXK_CUDA(cudaGetLastError());
     }
     if (!work) return MXK_OK;
-    {
+    const int nseg = (int)((blocks + kScanSeg - 1) / kScanSeg);
+    if (nseg > 0) {
         LaunchScope scope("work_scan", stream);
-        work_scan_kernel<<<1, 1024, 0, stream>>>((int)blocks, work->counts, work->offsets, work->rows, stop);
+        work_scan_kernel<<<(unsigned)nseg, kScanSeg, 0, stream>>>((int)blocks, work->counts, work->offsets,
+                                                                   work->seg_total, stop);
         MXK_CUDA(cudaGetLastError());
     }
-    if (blocks > 0) {
+    {  // (at least one block: it writes the row count)
         LaunchScope scope("work_scatter", stream);
-        work_scatter_kernel<<<(unsigned)blocks, 128, 0, stream>>>(rows, pid, row_bound, work->need_bits,
-                                                                   work->offsets, work->counts, mask, work->pid,
-                                                                   work->rb, work->cmask, stop);
+        work_scatter_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 128, 0, stream>>>(
+            rows, pid, row_bound, work->need_bits, work->offsets, work->counts, work->seg_total, nseg, mask,
+            work->pid, work->rb, work->cmask, work->rows, stop);
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;
