@@ -121,6 +121,8 @@ struct GemmParams {
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
     int best_dist_stride;  // best_dist[point * best_dist_stride]
     const float2* row_bound;  // optional (argmin): MxArgmin::row_bound
+    int4* changes;            // optional (argmin, with row_bound): MxArgmin::changes
+    int* change_count;
     unsigned* err;
 };
 
@@ -1091,6 +1093,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (p.best_dist) p.best_dist[point * p.best_dist_stride] = m.first;
                         if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
+                    if (p.changes) {  // label changes, one counter update per warp
+                        const bool moved = valid && forced >= 0 && m.best != forced;
+                        const unsigned bal = __ballot_sync(0xffffffffu, moved);
+                        if (bal) {
+                            const int leader = __ffs(bal) - 1;
+                            int base = 0;
+                            if (lane == leader) base = atomicAdd(p.change_count, __popc(bal));
+                            base = __shfl_sync(0xffffffffu, base, leader);
+                            if (moved)
+                                p.changes[base + __popc(bal & ((1u << lane) - 1u))] =
+                                    make_int4((int)point, forced, m.best, 0);
+                        }
+                    }
                 }
             }
             id_cur = id_nxt, lead_cur = lead_nxt, pn_cur = pn_nxt, hint_cur = hint_nxt, mask_cur = mask_nxt;
@@ -1175,6 +1190,9 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         p.best_dist = argmin->best_dist;
         p.best_dist_stride = argmin->best_dist_stride;
         p.row_bound = argmin->row_bound;
+        p.changes = argmin->changes;
+        p.change_count = argmin->change_count;
+        MXK_REQUIRE(!p.changes || (p.row_bound && p.change_count), "gemm_mx: label changes need row bounds and a count");
         MXK_REQUIRE(!(p.row_bound && p.gaps), "gemm_mx: row bounds and gaps are exclusive");
         MXK_REQUIRE(!p.tile_mask || (n + kBN - 1) / kBN <= 64, "gemm_mx: a tile mask covers at most 64 centroid tiles");
     }

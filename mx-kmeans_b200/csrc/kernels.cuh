@@ -88,11 +88,16 @@ struct MxArgmin {
     float* best_dist = nullptr;
     int best_dist_stride = 1;
     // optional, per GEMM row (the order of pid): (an upper bound on the row's
-    // distance to its nearest centroid, the row's previous label, as int bits),
-    // or (inf, -1).  The epilogue starts each row's minimum at the bound and
+    // distance to its nearest centroid or inf, the row's previous label as int
+    // bits or -1).  The epilogue starts each row's minimum at the bound and
     // always evaluates the chunk holding the previous label exactly; the
     // result is unchanged.
     const float2* row_bound = nullptr;
+    // optional (with row_bound): every row whose label differs from its
+    // previous one (row_bound's) is recorded as (point, previous, new, 0) at
+    // changes[atomicAdd(change_count, 1)]
+    int4* changes = nullptr;
+    int* change_count = nullptr;
 };
 // Dense: out[m x n] = A . B^T.  Argmin: labels of the m rows against n centroids.
 // rows_dev (optional) = device-resident m (m is then an upper bound).
@@ -187,10 +192,21 @@ int64_t shift_total_index();
 // old_centroids may be centroids itself (updated in place); prev_out receives
 // the old centroids; zero_sums leaves sums and counts zero for the next
 // accumulation; host_state (host-mapped pinned memory) receives the four state
-// words once the launch is done, also after the loop has stopped.
+// words once the launch is done, also after the loop has stopped.  acc_sums
+// (k x d FP64) and acc_counts (k): running sums and counts kept across
+// iterations, to which this iteration's sums / counts are added (full: which
+// they replace); the centroids come from the running values.  zero_word
+// (optional) is zeroed once the launch has read everything.
 int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop = nullptr, float tolerance = 0.0f,
-                    float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr);
+                    float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr,
+                    double* acc_sums = nullptr, int* acc_counts = nullptr, bool full = true,
+                    int* zero_word = nullptr);
+// The label changes recorded by the GEMM (rec[i] = (point, old label, new
+// label, 0), *count of them): each moves its point's row and count from the old
+// cluster's to the new one's in sums / counts (this iteration's additions).
+int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, float* sums,
+                              int* counts, cudaStream_t stream, const int* stop = nullptr);
 // sum((previous - current)^2) into shift_scratch[shift_scratch_floats() - 1].
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,
                  cudaStream_t stream);

@@ -390,6 +390,15 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CHECK(ws.alloc(&counts, k));
     MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
     MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
+    // Running cluster sums (FP64) and counts across iterations: a pruned
+    // iteration's GEMM records the points whose label changed and the update
+    // moves only those rows (the reference re-adds every point each iteration;
+    // the sums agree to within FP32 rounding of the moved rows).
+    double* acc_sums = nullptr;
+    int *acc_counts = nullptr, *chg_count = nullptr;
+    int4* chg = nullptr;
+    MXK_CHECK(ws.alloc(&acc_sums, kd));
+    MXK_CHECK(ws.alloc(&acc_counts, k));
     MXK_CHECK(ws.alloc(&shift, shift_scratch_floats()));
     MXK_CUDA(cudaMemsetAsync(shift, 0, sizeof(float) * shift_scratch_floats(), stream));  // (the finalize ticket)
     // Exact pruning of centroid tiles (prune.cu) from the previous iteration's
@@ -410,6 +419,9 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&tstats, ctiles));
         MXK_CHECK(ws.alloc(&tmask, (n + kPointTileRows - 1) / kPointTileRows));
         MXK_CHECK(ws.alloc(&rbound, n));
+        MXK_CHECK(ws.alloc(&chg, n));
+        MXK_CHECK(ws.alloc(&chg_count, 1));
+        MXK_CUDA(cudaMemsetAsync(chg_count, 0, sizeof(int), stream));
     }
     // Row compaction in pruned iterations (not with the point cache, whose GEMM
     // reads contiguous pre-gathered point tiles): rows whose label the bounds
@@ -559,6 +571,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.start_hint = it > 0 ? labels : nullptr;  // previous iteration's labels
             am.tile_mask = prune_it ? (compacted ? reinterpret_cast<const uint64_t*>(work.cmask) : tmask) : nullptr;
             am.row_bound = prune_it ? (compacted ? work.rb : rbound) : nullptr;
+            am.changes = prune_it ? chg : nullptr;
+            am.change_count = prune_it ? chg_count : nullptr;
             am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows, stream,
@@ -615,7 +629,14 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                                      stream));
         // kmeans.cu:62-65 (sums and counts are zero: set before the loop, and
         // left zero by every finalize)
-        MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream, loop));
+        // A pruned MX iteration (forced MXFP8: its GEMM recorded the label
+        // changes) adds only the moved rows to the running sums; any other
+        // iteration accumulates every point afresh.
+        const bool incremental = prune_it && forced8;
+        if (incremental)
+            MXK_CHECK(launch_accumulate_changes(d, k, points, chg, chg_count, sums, counts, stream, loop));
+        else
+            MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream, loop));
         if (sharded) {
             NcclApi& api = nccl();
             ncclResult_t r = api.GroupStart();
@@ -631,7 +652,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         // writes the loop state into this iteration's pinned host slot.
         const int slot = it % (kLookahead + 1);
         MXK_CHECK(launch_finalize(d, k, sums, counts, centroids, centroids, shift, stream, loop, options->tolerance,
-                                  prev, true, mirror->dev + 4 * slot));
+                                  prev, true, mirror->dev + 4 * slot, acc_sums, acc_counts, !incremental,
+                                  incremental ? chg_count : nullptr));
         MXK_CUDA(cudaEventRecord(mirror->ev[slot], stream));
         // Read the state of iteration it - lookahead.  FP32 iterations (whose
         // kernels do not consult the stop word) and verbose runs are read at once,

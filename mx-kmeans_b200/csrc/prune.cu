@@ -303,7 +303,8 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     uint64_t m = 0;
     bool need = false;
     // (bound on the row's nearest distance, its previous label) for the GEMM's
-    // screen; (inf, -1) when no finite bound holds
+    // screen: (inf, label) when no finite bound holds, (inf, -1) without a
+    // valid previous label
     float2 rb = make_float2(inf, __int_as_float(-1));
     if (row < rows) {
         const int64_t x = pid ? pid[row] : row;
@@ -311,6 +312,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
         m = all;
         need = true;
         if ((unsigned)a < (unsigned)k) {
+            rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
             const float4 pi = pinfo[x];  // (previous distance, alpha_x, |x^|^2, |x|^2)
             const float dp = pi.x, px = pi.w;
             const float2 ps = make_float2(pi.y, pi.z);
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
                 // The screen only needs some upper bound: a wider margin costs
                 // nothing measurable and keeps it far from the rounding terms.
                 const float us = um + 1e-3f * (fabsf(um) + fabsf(ps.x) + fabsf(now.x));
-                if (fabsf(us) < inf) rb = make_float2(us, __int_as_float(a));
+                if (fabsf(us) < inf) rb.x = us;
                 const float* dm = dmin + (int64_t)a * tiles;
                 for (int t = 0; t < tiles; ++t) {
                     const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)

@@ -169,6 +169,38 @@ __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* _
     }
 }
 
+// Incremental update: for each recorded label change (point, old, new) of
+// this iteration, one warp moves the point's FP32 row from cluster old's sum to
+// cluster new's (vector reductions into the iteration's delta sums) and its
+// count.  rec[i] = (point, old label, new label, 0), *count entries.
+__global__ void __launch_bounds__(256) accumulate_changes_kernel(int d, int k, const float* __restrict__ points,
+                                                                 const int4* __restrict__ rec,
+                                                                 const int* __restrict__ count,
+                                                                 float* __restrict__ sums, int* __restrict__ counts,
+                                                                 unsigned* __restrict__ err,
+                                                                 const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    const int lane = threadIdx.x & 31;
+    const int warps = (int)((gridDim.x * blockDim.x) >> 5);
+    const int nrec = *count;
+    for (int i = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); i < nrec; i += warps) {
+        const int4 c = rec[i];
+        if (bad_label(c.z, k, lane == 0 ? err : nullptr) || bad_label(c.y, k, lane == 0 ? err : nullptr)) continue;
+        const float* x = points + (int64_t)c.x * d;
+        float* to = sums + (int64_t)c.z * d;
+        float* from = sums + (int64_t)c.y * d;
+        for (int f = 4 * lane; f < d; f += 128) {
+            const float4 v = ldg_stream4(x + f);
+            red_add_v4(to + f, v);
+            red_add_v4(from + f, make_float4(-v.x, -v.y, -v.z, -v.w));
+        }
+        if (lane == 0) {
+            atomicAdd(counts + c.z, 1);
+            atomicAdd(counts + c.y, -1);
+        }
+    }
+}
+
 // Applies the stopping rule to the Lloyd driver's state words for shift s
 // (kmeans.cu:62-67): counts the iteration and stops on a non-finite shift or
 // one <= tolerance.
@@ -195,7 +227,13 @@ __device__ __forceinline__ void apply_stop_rule(int* loop, float s, float tolera
 // the state.  Driver options: old may be centroids itself (each element is
 // read, then written, by one thread); prev_out receives the old centroids;
 // zero_sums leaves sums and counts zeroed for the next accumulation;
-// host_state (host-mapped) receives the four state words.
+// host_state (host-mapped) receives the four state words.  With acc_sums /
+// acc_counts (FP64 running sums and int counts kept across iterations), sums /
+// counts are this iteration's additions: full replaces the running values with
+// them (a fresh accumulation), otherwise they are added (label changes); the
+// last CTA also zeroes *zero_word (the change list's count).  The
+// centroid is the running sum rounded to FP32, divided by the count in FP32,
+// as the reference divides its FP32 sums.
 __device__ __forceinline__ void publish_state(const int* loop, int* host_state) {
     if (!host_state) return;
     volatile const int* src = loop;
@@ -208,7 +246,9 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __re
                                                        const float* old, float* centroids, float* __restrict__ prev_out,
                                                        float* __restrict__ partials, int* __restrict__ loop,
                                                        unsigned* __restrict__ done, float* __restrict__ total_out,
-                                                       float tolerance, int zero_sums, int* __restrict__ host_state) {
+                                                       float tolerance, int zero_sums, int* __restrict__ host_state,
+                                                       double* __restrict__ acc_sums, int* __restrict__ acc_counts,
+                                                       int full, int* __restrict__ zero_word) {
     if (loop && *(volatile int*)loop) {  // converged: the centroids stay as they are
         if (blockIdx.x == 0 && threadIdx.x == 0) publish_state(loop, host_state);
         return;
@@ -217,10 +257,17 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __re
     const int64_t total = (int64_t)k * d;
     float local = 0.0f;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int cnt = counts[i / d];
+        int cnt = counts[i / d];
+        float sum = sums[i];
+        if (acc_sums) {
+            const double run = (full ? 0.0 : acc_sums[i]) + (double)sum;
+            acc_sums[i] = run;
+            sum = (float)run;
+            if (!full) cnt += acc_counts[i / d];
+        }
         const float o = old[i];
         // An empty cluster keeps its previous center (update.cu:26-29).
-        const float v = cnt ? sums[i] / (float)cnt : o;
+        const float v = cnt ? sum / (float)cnt : o;
         const float diff = o - v;
         if (prev_out) prev_out[i] = o;
         if (zero_sums) sums[i] = 0.0f;
@@ -255,13 +302,17 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __re
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += warp_sum[w];
         *total_out = s;
         *done = 0u;
+        if (zero_word) *zero_word = 0;
         apply_stop_rule(loop, s, tolerance);
         __threadfence();
         publish_state(loop, host_state);
     }
-    if (zero_sums) {  // every CTA has read its counts (it took a ticket after its loop)
+    if (zero_sums || acc_counts) {  // every CTA has read its counts (it took a ticket after its loop)
         __syncthreads();
-        for (int c = threadIdx.x; c < k; c += blockDim.x) counts[c] = 0;
+        for (int c = threadIdx.x; c < k; c += blockDim.x) {
+            if (acc_counts) acc_counts[c] = (full ? 0 : acc_counts[c]) + counts[c];
+            if (zero_sums) counts[c] = 0;
+        }
     }
 }
 
@@ -368,13 +419,29 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
 
 // [0, kShiftBlocks): partials, [kShiftBlocks]: the total, [kShiftBlocks + 1]:
 // the finalize kernel's ticket counter (zero between launches)
+int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, float* sums,
+                              int* counts, cudaStream_t stream, const int* stop) {
+    MXK_REQUIRE(d > 0 && d % 4 == 0 && points && rec && count && sums && counts, "accumulate_changes: bad arguments");
+    MXK_REQUIRE(reinterpret_cast<uintptr_t>(points) % 16 == 0 && reinterpret_cast<uintptr_t>(sums) % 16 == 0,
+                "accumulate_changes: points and sums must be 16-byte aligned");
+    unsigned* err = device_error_word();
+    if (!err) return fail(MXK_ERR_CUDA, "accumulate_changes: cannot allocate the device error word");
+    LaunchScope scope("accumulate_changes", stream);
+    accumulate_changes_kernel<<<(unsigned)(sm_count() * 8), 256, 0, stream>>>(d, k, points, rec, count, sums, counts,
+                                                                             err, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
 int64_t shift_scratch_floats() { return kShiftBlocks + 2; }
 int64_t shift_total_index() { return kShiftBlocks; }
 
 int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
-                    bool zero_sums, int* host_state) {
-    MXK_REQUIRE(!(zero_sums || host_state) || loop, "finalize: zeroing and the host state need the loop words");
+                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+    MXK_REQUIRE(!(zero_sums || host_state || acc_sums) || loop,
+                "finalize: zeroing, running sums and the host state need the loop words");
+    MXK_REQUIRE(!acc_sums == !acc_counts, "finalize: running sums and counts go together");
     MXK_REQUIRE(!loop || shift_scratch, "finalize: the loop state needs the shift scratch");
     const int64_t total = (int64_t)k * d;
     int64_t blocks = (total + 255) / 256;
@@ -384,7 +451,8 @@ int launch_finalize(int d, int k, float* sums, int* counts, const float* old_cen
         finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
             d, k, sums, counts, old_centroids, centroids, prev_out, shift_scratch, loop,
             loop ? reinterpret_cast<unsigned*>(shift_scratch + kShiftBlocks + 1) : nullptr,
-            loop ? shift_scratch + kShiftBlocks : nullptr, tolerance, zero_sums ? 1 : 0, host_state);
+            loop ? shift_scratch + kShiftBlocks : nullptr, tolerance, zero_sums ? 1 : 0, host_state, acc_sums,
+            acc_counts, full ? 1 : 0, zero_word);
         MXK_CUDA(cudaGetLastError());
     }
     if (shift_scratch && !loop) {  // (with loop the finalize kernel's last CTA sums the partials)
