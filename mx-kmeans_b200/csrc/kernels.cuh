@@ -171,9 +171,13 @@ int launch_assign_clusters(int64_t rows, int k, const float* point_norms, const 
 // ---- update.cu ---------------------------------------------------------------
 // sums (k x d) and counts (k) must be zeroed by the caller.  order (optional):
 // visit the points in this sequence (label-sorted orders make long label runs).
-// stop (optional, device word): non-zero at run time = do nothing.
+// stop (optional, device word): non-zero at run time = do nothing.  The sums
+// are FP32 (the reference-facing update, as the reference's) or FP64 (the Lloyd
+// driver, whose running sums also take label-change deltas).
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
                       float* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
+                      double* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
 // centroids = counts ? sums / counts : old.  If shift_scratch is not null
 // (shift_scratch_floats() floats, zeroed once before the first use by a Lloyd
 // loop), shift_scratch[shift_total_index()] receives sum((old - new)^2),
@@ -202,10 +206,15 @@ int launch_finalize(int d, int k, float* sums, int* counts, const float* old_cen
                     float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr,
                     double* acc_sums = nullptr, int* acc_counts = nullptr, bool full = true,
                     int* zero_word = nullptr);
+int launch_finalize(int d, int k, double* sums, int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream, int* loop = nullptr, float tolerance = 0.0f,
+                    float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr,
+                    double* acc_sums = nullptr, int* acc_counts = nullptr, bool full = true,
+                    int* zero_word = nullptr);
 // The label changes recorded by the GEMM (rec[i] = (point, old label, new
 // label, 0), *count of them): each moves its point's row and count from the old
 // cluster's to the new one's in sums / counts (this iteration's additions).
-int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, float* sums,
+int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, double* sums,
                               int* counts, cudaStream_t stream, const int* stop = nullptr);
 // sum((previous - current)^2) into shift_scratch[shift_scratch_floats() - 1].
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,

@@ -233,8 +233,8 @@ constexpr int64_t kFp32ChunkBytes = 512ll << 20;  // dense product chunk of the 
 // held in the driver for that long does not leave the GPU idle.
 constexpr int kLookahead = 8;
 // The label-sorted visiting order is rebuilt every kResortEvery iterations.  It
-// only shapes performance (assignments are per point; the update's FP32 sums
-// are order-dependent in their last bits, as the reference's atomics are), and
+// only shapes performance (assignments are per point; the update's FP64 sums
+// are order-dependent in their last bits, as the reference's FP32 atomics are), and
 // after the first iterations few labels change, so an order one iteration old
 // is nearly as good: measured at configs[3], every second iteration saves the
 // 0.21 ms sort on half of them and costs the GEMM < 0.02 ms.
@@ -335,7 +335,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     const int64_t kd = (int64_t)k * d;
     Arena ws(stream);
     float *pnorm = nullptr, *upper = nullptr, *gaps = nullptr, *cnorm = nullptr, *cerr = nullptr, *stats = nullptr,
-          *prev = nullptr, *sums = nullptr, *shift = nullptr;
+          *prev = nullptr, *shift = nullptr;
     int *precision = nullptr, *ids = nullptr, *gcount = nullptr, *cscratch = nullptr, *counts = nullptr;
     uint8_t *qpoints = nullptr, *pscales = nullptr, *qcent = nullptr, *cscales = nullptr;
     // With the forced-MXFP8 policy the precision inputs and groups are not
@@ -386,14 +386,18 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     if (need_qpoints) MXK_CUDA(cudaMemsetAsync(pscales, 0, (size_t)scale_atom_bytes(n, d), stream));
     MXK_CUDA(cudaMemsetAsync(cscales, 0, (size_t)scale_atom_bytes(k, d, kCentroidTileRows), stream));
     MXK_CHECK(ws.alloc(&prev, kd));
+    // This iteration's cluster sums in FP64 (every point, or the moved rows'
+    // deltas), and the running sums and counts kept across iterations: a pruned
+    // iteration's GEMM records the points whose label changed and the update
+    // moves only those rows (the reference re-adds every point each iteration
+    // in FP32; FP64 keeps the running sums of clusters that lose most of their
+    // points clear of cancellation, so both round to the same FP32 sums up to
+    // the reference's own summation error).
+    double* sums = nullptr;
     MXK_CHECK(ws.alloc(&sums, kd));
     MXK_CHECK(ws.alloc(&counts, k));
-    MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(float) * kd, stream));
+    MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(double) * kd, stream));
     MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
-    // Running cluster sums (FP64) and counts across iterations: a pruned
-    // iteration's GEMM records the points whose label changed and the update
-    // moves only those rows (the reference re-adds every point each iteration;
-    // the sums agree to within FP32 rounding of the moved rows).
     double* acc_sums = nullptr;
     int *acc_counts = nullptr, *chg_count = nullptr;
     int4* chg = nullptr;
@@ -483,15 +487,9 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         PhaseRange iteration_range("lloyd_iteration");
         // From the second iteration on, visit points grouped by their label of
         // the previous (or, every other iteration, the one before) iteration
-        // (order.cu); the first iteration keeps ascending point order.
-        const int* ord = nullptr;
-        if (it > 0 && n > 0) {
-            if ((it - 1) % kResortEvery == 0) {
-                MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
-                cached_stale = true;
-            }
-            ord = order;
-        }
+        // (order.cu, rebuilt below after the assignment); the first iteration
+        // keeps ascending point order.
+        const int* ord = it > 0 && n > 0 ? order : nullptr;
         // Pruning needs the previous iteration's labels and distances from the
         // MX GEMM (not an FP32 iteration) and, in prev, the centroids it used.
         const bool prune_it = prune && it >= 1 && it - 1 >= options->fp32_iterations;
@@ -627,12 +625,20 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         if (traced && trace.labels)
             MXK_CUDA(cudaMemcpyAsync(trace.labels + (int64_t)it * n, labels, sizeof(int) * n, cudaMemcpyDeviceToDevice,
                                      stream));
-        // kmeans.cu:62-65 (sums and counts are zero: set before the loop, and
-        // left zero by every finalize)
         // A pruned MX iteration (forced MXFP8: its GEMM recorded the label
         // changes) adds only the moved rows to the running sums; any other
         // iteration accumulates every point afresh.
         const bool incremental = prune_it && forced8;
+        // Every kResortEvery-th iteration sorts the points by the labels just
+        // assigned: the next iteration visits them in that order, and a fresh
+        // accumulation below sees one run per cluster.
+        if (n > 0 && it % kResortEvery == 0 && (!incremental || it + 1 < options->max_iterations)) {
+            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
+            cached_stale = true;
+            ord = order;
+        }
+        // kmeans.cu:62-65 (sums and counts are zero: set before the loop, and
+        // left zero by every finalize)
         if (incremental)
             MXK_CHECK(launch_accumulate_changes(d, k, points, chg, chg_count, sums, counts, stream, loop));
         else
@@ -640,7 +646,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         if (sharded) {
             NcclApi& api = nccl();
             ncclResult_t r = api.GroupStart();
-            if (r == ncclSuccess) r = api.AllReduce(sums, sums, (size_t)kd, ncclFloat32, ncclSum, comm->comm, stream);
+            if (r == ncclSuccess) r = api.AllReduce(sums, sums, (size_t)kd, ncclFloat64, ncclSum, comm->comm, stream);
             if (r == ncclSuccess) r = api.AllReduce(counts, counts, (size_t)k, ncclInt32, ncclSum, comm->comm, stream);
             ncclResult_t r2 = api.GroupEnd();
             if (r != ncclSuccess) return fail_nccl("ncclAllReduce", r);

@@ -25,6 +25,27 @@ __device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
                  : "memory");
 }
 
+// Sums of the update are kept in float (the reference-facing update_centroids)
+// or double (the Lloyd driver's running sums, which must survive clusters that
+// lose most of their points without FP32 cancellation).  Acc4 is four of them.
+template <class T>
+struct Acc4 {
+    T x, y, z, w;
+};
+template <class T>
+__device__ __forceinline__ void acc_zero(Acc4<T>& a) { a.x = a.y = a.z = a.w = T(0); }
+template <class T>
+__device__ __forceinline__ void acc_add(Acc4<T>& a, float4 v) {
+    a.x += (T)v.x, a.y += (T)v.y, a.z += (T)v.z, a.w += (T)v.w;
+}
+// *dst += a (four consecutive sums), one vector reduction for float
+__device__ __forceinline__ void flush4(float* dst, const Acc4<float>& a) {
+    red_add_v4(dst, make_float4(a.x, a.y, a.z, a.w));
+}
+__device__ __forceinline__ void flush4(double* dst, const Acc4<double>& a) {
+    atomicAdd(dst, a.x), atomicAdd(dst + 1, a.y), atomicAdd(dst + 2, a.z), atomicAdd(dst + 3, a.w);
+}
+
 __device__ __forceinline__ float4 ldg_stream4(const float* p) {
     float4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
@@ -43,10 +64,10 @@ __device__ __forceinline__ bool bad_label(int lab, int k, unsigned* err) {
     return true;
 }
 
-template <int NJ>
+template <int NJ, class T>
 __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, int k, const float* __restrict__ points,
                                                               const int* __restrict__ labels,
-                                                              const int* __restrict__ order, float* __restrict__ sums,
+                                                              const int* __restrict__ order, T* __restrict__ sums,
                                                               int* __restrict__ counts, int64_t per_warp,
                                                               unsigned* __restrict__ err, const int* __restrict__ stop) {
     if (stop && *stop) return;  // the Lloyd loop has already converged
@@ -55,11 +76,11 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
     const int64_t begin = warp * per_warp;
     if (begin >= n) return;
     const int64_t end = begin + per_warp < n ? begin + per_warp : n;
-    float4 acc[NJ];
+    Acc4<T> acc[NJ];
     int cur = -1;  // no open run
     int run = 0;
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < NJ; ++j) acc_zero(acc[j]);
     // Rows are taken kBatch at a time: their ids, labels and feature vectors
     // are all requested before the first is added, so each warp keeps several
     // rows in flight; the additions stay in row order.
@@ -87,43 +108,42 @@ __global__ void __launch_bounds__(256) accumulate_runs_kernel(int64_t n, int d, 
             if (bad_label(lab[u], k, lane == 0 ? err : nullptr)) continue;
             if (lab[u] != cur) {
                 if (cur >= 0) {
-                    float* dst = sums + (int64_t)cur * d + 4 * lane;
+                    T* dst = sums + (int64_t)cur * d + 4 * lane;
 #pragma unroll
-                    for (int j = 0; j < NJ; ++j)
-                        red_add_v4(dst + 128 * j, acc[j]), acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j = 0; j < NJ; ++j) flush4(dst + 128 * j, acc[j]), acc_zero(acc[j]);
                     if (lane == 0) atomicAdd(counts + cur, run);
                 }
                 cur = lab[u];
                 run = 0;
             }
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) {
-                const float4 x = xb[u][j];
-                acc[j].x += x.x, acc[j].y += x.y, acc[j].z += x.z, acc[j].w += x.w;
-            }
+            for (int j = 0; j < NJ; ++j) acc_add(acc[j], xb[u][j]);
             ++run;
         }
     }
     if (cur < 0) return;
-    float* dst = sums + (int64_t)cur * d + 4 * lane;
+    T* dst = sums + (int64_t)cur * d + 4 * lane;
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) red_add_v4(dst + 128 * j, acc[j]);
+    for (int j = 0; j < NJ; ++j) flush4(dst + 128 * j, acc[j]);
     if (lane == 0) atomicAdd(counts + cur, run);
 }
 
 // (a) privatized path: the CTA's copy of all K x D sums and K counts lives in
 // shared memory; one warp per point, float4 per lane.
+template <class T>
 __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int d, int k,
                                                                  const float* __restrict__ points,
                                                                  const int* __restrict__ labels,
-                                                                 const int* __restrict__ order, float* __restrict__ sums,
+                                                                 const int* __restrict__ order, T* __restrict__ sums,
                                                                  int* __restrict__ counts, unsigned* __restrict__ err,
                                                                  const int* __restrict__ stop) {
     if (stop && *stop) return;
-    extern __shared__ float priv[];  // k*d sums, then k counts
+    extern __shared__ __align__(16) unsigned char priv_raw[];
+    T* priv = reinterpret_cast<T*>(priv_raw);  // k*d sums, then k counts
     int* pcount = reinterpret_cast<int*>(priv + (int64_t)k * d);
     const int kd = k * d;
-    for (int i = threadIdx.x; i < kd + k; i += blockDim.x) priv[i] = 0.0f;  // int 0 has the same bits
+    for (int i = threadIdx.x; i < kd; i += blockDim.x) priv[i] = T(0);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) pcount[i] = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
@@ -133,28 +153,29 @@ __global__ void __launch_bounds__(512) accumulate_private_kernel(int64_t n, int 
         const int lab = labels[pnt];
         if (bad_label(lab, k, lane == 0 ? err : nullptr)) continue;
         const float* src = points + pnt * d;
-        float* dst = priv + (int64_t)lab * d;
+        T* dst = priv + (int64_t)lab * d;
         for (int v = lane; v < vec_per_row; v += 32) {
             const float4 x = ldg_stream4(src + 4 * v);
-            atomicAdd(dst + 4 * v, x.x);
-            atomicAdd(dst + 4 * v + 1, x.y);
-            atomicAdd(dst + 4 * v + 2, x.z);
-            atomicAdd(dst + 4 * v + 3, x.w);
+            atomicAdd(dst + 4 * v, (T)x.x);
+            atomicAdd(dst + 4 * v + 1, (T)x.y);
+            atomicAdd(dst + 4 * v + 2, (T)x.z);
+            atomicAdd(dst + 4 * v + 3, (T)x.w);
         }
         if (lane == 0) atomicAdd(pcount + lab, 1);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < (kd >> 2); i += blockDim.x) {
-        const float4 v = reinterpret_cast<const float4*>(priv)[i];
-        if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f) red_add_v4(sums + 4 * i, v);
+        const Acc4<T> v{priv[4 * i], priv[4 * i + 1], priv[4 * i + 2], priv[4 * i + 3]};
+        if (v.x != T(0) || v.y != T(0) || v.z != T(0) || v.w != T(0)) flush4(sums + 4 * i, v);
     }
     for (int i = threadIdx.x; i < k; i += blockDim.x)
         if (pcount[i]) atomicAdd(counts + i, pcount[i]);
 }
 
 // Generic fallback for d % 128 != 0 (API use with unpadded d).
+template <class T>
 __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* __restrict__ points,
-                                         const int* __restrict__ labels, float* __restrict__ sums,
+                                         const int* __restrict__ labels, T* __restrict__ sums,
                                          int* __restrict__ counts, unsigned* __restrict__ err,
                                          const int* __restrict__ stop) {
     if (stop && *stop) return;
@@ -165,38 +186,62 @@ __global__ void accumulate_scalar_kernel(int64_t n, int d, int k, const float* _
         const int lab = labels[row];
         if (bad_label(lab, k, f == 0 ? err : nullptr)) continue;
         if (f == 0) atomicAdd(counts + lab, 1);
-        atomicAdd(sums + (int64_t)lab * d + f, points[i]);
+        atomicAdd(sums + (int64_t)lab * d + f, (T)points[i]);
     }
 }
 
-// Incremental update: for each recorded label change (point, old, new) of
-// this iteration, one warp moves the point's FP32 row from cluster old's sum to
-// cluster new's (vector reductions into the iteration's delta sums) and its
-// count.  rec[i] = (point, old label, new label, 0), *count entries.
+// Incremental update: each recorded label change (point, old, new) moves the
+// point's row from cluster old's sum to cluster new's and its count.  A warp
+// takes 32 consecutive records (one per lane), groups them by new label and by
+// old label (the GEMM visits rows sorted by their previous label, so the old
+// labels of neighbouring records mostly agree), sums each group's rows in FP64
+// registers and flushes one FP64 reduction per group and feature, instead of
+// one per record.  rec[i] = (point, old label, new label, 0), *count entries.
 __global__ void __launch_bounds__(256) accumulate_changes_kernel(int d, int k, const float* __restrict__ points,
                                                                  const int4* __restrict__ rec,
                                                                  const int* __restrict__ count,
-                                                                 float* __restrict__ sums, int* __restrict__ counts,
+                                                                 double* __restrict__ sums, int* __restrict__ counts,
                                                                  unsigned* __restrict__ err,
                                                                  const int* __restrict__ stop) {
     if (stop && *stop) return;
     const int lane = threadIdx.x & 31;
     const int warps = (int)((gridDim.x * blockDim.x) >> 5);
     const int nrec = *count;
-    for (int i = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); i < nrec; i += warps) {
-        const int4 c = rec[i];
-        if (bad_label(c.z, k, lane == 0 ? err : nullptr) || bad_label(c.y, k, lane == 0 ? err : nullptr)) continue;
-        const float* x = points + (int64_t)c.x * d;
-        float* to = sums + (int64_t)c.z * d;
-        float* from = sums + (int64_t)c.y * d;
-        for (int f = 4 * lane; f < d; f += 128) {
-            const float4 v = ldg_stream4(x + f);
-            red_add_v4(to + f, v);
-            red_add_v4(from + f, make_float4(-v.x, -v.y, -v.z, -v.w));
-        }
-        if (lane == 0) {
-            atomicAdd(counts + c.z, 1);
-            atomicAdd(counts + c.y, -1);
+    for (int base = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; base < nrec; base += warps * 32) {
+        int4 c = base + lane < nrec ? rec[base + lane] : make_int4(0, -1, -1, 0);
+        bool valid = base + lane < nrec;
+        if (valid && (bad_label(c.z, k, err) || bad_label(c.y, k, err))) valid = false;
+        const unsigned live = __ballot_sync(kFull, valid);
+        if (!valid) c.y = c.z = -1;
+        const int point = c.x;
+#pragma unroll 1
+        for (int side = 0; side < 2; ++side) {
+            const int key = side ? c.y : c.z;
+            const unsigned peers = __match_any_sync(kFull, key);
+            if (valid && lane == __ffs(peers) - 1) atomicAdd(counts + key, side ? -__popc(peers) : __popc(peers));
+            unsigned leads = __ballot_sync(kFull, valid && lane == __ffs(peers) - 1) & live;
+            while (leads) {
+                const int l = __ffs(leads) - 1;
+                leads &= leads - 1;
+                const unsigned members = __shfl_sync(kFull, peers, l);
+                const int label = __shfl_sync(kFull, key, l);
+                double* dst = sums + (int64_t)label * d;
+                for (int f0 = 0; f0 < d; f0 += 128) {  // (warp-uniform trip count: the shuffles below)
+                    const int f = f0 + 4 * lane;
+                    Acc4<double> acc;
+                    acc_zero(acc);
+                    unsigned m = members;
+                    while (m) {
+                        const int j = __ffs(m) - 1;
+                        m &= m - 1;
+                        const int64_t row = __shfl_sync(kFull, point, j);
+                        // (cached in L1: the other side's group reads the row again)
+                        if (f < d) acc_add(acc, __ldg(reinterpret_cast<const float4*>(points + row * d + f)));
+                    }
+                    if (side) acc.x = -acc.x, acc.y = -acc.y, acc.z = -acc.z, acc.w = -acc.w;
+                    if (f < d) flush4(dst + f, acc);
+                }
+            }
         }
     }
 }
@@ -242,7 +287,8 @@ __device__ __forceinline__ void publish_state(const int* loop, int* host_state) 
     __threadfence_system();
 }
 
-__global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __restrict__ sums, int* __restrict__ counts,
+template <class T>
+__global__ void __launch_bounds__(256) finalize_kernel(int d, int k, T* __restrict__ sums, int* __restrict__ counts,
                                                        const float* old, float* centroids, float* __restrict__ prev_out,
                                                        float* __restrict__ partials, int* __restrict__ loop,
                                                        unsigned* __restrict__ done, float* __restrict__ total_out,
@@ -258,9 +304,9 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __re
     float local = 0.0f;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int cnt = counts[i / d];
-        float sum = sums[i];
+        float sum = (float)sums[i];
         if (acc_sums) {
-            const double run = (full ? 0.0 : acc_sums[i]) + (double)sum;
+            const double run = (full ? 0.0 : acc_sums[i]) + (double)sums[i];
             acc_sums[i] = run;
             sum = (float)run;
             if (!full) cnt += acc_counts[i / d];
@@ -270,7 +316,7 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, float* __re
         const float v = cnt ? sum / (float)cnt : o;
         const float diff = o - v;
         if (prev_out) prev_out[i] = o;
-        if (zero_sums) sums[i] = 0.0f;
+        if (zero_sums) sums[i] = T(0);
         centroids[i] = v;
         local += diff * diff;
     }
@@ -356,17 +402,16 @@ __global__ void __launch_bounds__(256) shift_kernel(int64_t elements, const floa
 
 constexpr int kShiftBlocks = 256;  // fixed grid of the shift reduction (<= partial slots)
 
-}  // namespace
-
-int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, float* sums,
-                      int* counts, cudaStream_t stream, const int* stop) {
+template <class T>
+int accumulate_impl(int64_t n, int d, int k, const float* points, const int* labels, const int* order, T* sums,
+                    int* counts, cudaStream_t stream, const int* stop) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && k > 0 && points && labels && sums && counts, "update_centroids: bad arguments");
     const int sms = sm_count();
     unsigned* err = device_error_word();
     if (!err) return fail(MXK_ERR_CUDA, "update_centroids: cannot allocate the device error word");
     const bool aligned = (reinterpret_cast<uintptr_t>(points) % 16 == 0) && (reinterpret_cast<uintptr_t>(sums) % 16 == 0);
-    const int64_t priv_bytes = ((int64_t)k * d + k) * 4;
+    const int64_t priv_bytes = (int64_t)k * d * (int64_t)sizeof(T) + (int64_t)k * 4;
     int max_smem = 0, dev = 0;
     MXK_CUDA(cudaGetDevice(&dev));
     MXK_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -374,11 +419,11 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
     // beats per-element shared-memory atomics; without one, privatize when the
     // sums fit in shared memory.
     if (!order && aligned && d % 4 == 0 && priv_bytes <= max_smem && priv_bytes <= 200 * 1024 && n >= (int64_t)k * 64) {
-        MXK_CUDA(cudaFuncSetAttribute(accumulate_private_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        MXK_CUDA(cudaFuncSetAttribute(accumulate_private_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)priv_bytes));
         LaunchScope scope("accumulate_private", stream);
-        accumulate_private_kernel<<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, order, sums, counts,
-                                                                             err, stop);
+        accumulate_private_kernel<T><<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, order, sums,
+                                                                                counts, err, stop);
         MXK_CUDA(cudaGetLastError());
         return MXK_OK;
     }
@@ -401,44 +446,26 @@ int launch_accumulate(int64_t n, int d, int k, const float* points, const int* l
             return MXK_OK;
         };
         switch (d / 128) {
-            case 1: return launch(accumulate_runs_kernel<1>);
-            case 2: return launch(accumulate_runs_kernel<2>);
-            case 3: return launch(accumulate_runs_kernel<3>);
-            case 4: return launch(accumulate_runs_kernel<4>);
-            case 5: return launch(accumulate_runs_kernel<5>);
-            case 6: return launch(accumulate_runs_kernel<6>);
-            case 7: return launch(accumulate_runs_kernel<7>);
-            default: return launch(accumulate_runs_kernel<8>);
+            case 1: return launch(accumulate_runs_kernel<1, T>);
+            case 2: return launch(accumulate_runs_kernel<2, T>);
+            case 3: return launch(accumulate_runs_kernel<3, T>);
+            case 4: return launch(accumulate_runs_kernel<4, T>);
+            case 5: return launch(accumulate_runs_kernel<5, T>);
+            case 6: return launch(accumulate_runs_kernel<6, T>);
+            case 7: return launch(accumulate_runs_kernel<7, T>);
+            default: return launch(accumulate_runs_kernel<8, T>);
         }
     }
     LaunchScope scope("accumulate_scalar", stream);
-    accumulate_scalar_kernel<<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err, stop);
+    accumulate_scalar_kernel<T><<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
 
-// [0, kShiftBlocks): partials, [kShiftBlocks]: the total, [kShiftBlocks + 1]:
-// the finalize kernel's ticket counter (zero between launches)
-int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, float* sums,
-                              int* counts, cudaStream_t stream, const int* stop) {
-    MXK_REQUIRE(d > 0 && d % 4 == 0 && points && rec && count && sums && counts, "accumulate_changes: bad arguments");
-    MXK_REQUIRE(reinterpret_cast<uintptr_t>(points) % 16 == 0 && reinterpret_cast<uintptr_t>(sums) % 16 == 0,
-                "accumulate_changes: points and sums must be 16-byte aligned");
-    unsigned* err = device_error_word();
-    if (!err) return fail(MXK_ERR_CUDA, "accumulate_changes: cannot allocate the device error word");
-    LaunchScope scope("accumulate_changes", stream);
-    accumulate_changes_kernel<<<(unsigned)(sm_count() * 8), 256, 0, stream>>>(d, k, points, rec, count, sums, counts,
-                                                                             err, stop);
-    MXK_CUDA(cudaGetLastError());
-    return MXK_OK;
-}
-
-int64_t shift_scratch_floats() { return kShiftBlocks + 2; }
-int64_t shift_total_index() { return kShiftBlocks; }
-
-int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
-                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
-                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+template <class T>
+int finalize_impl(int d, int k, T* sums, int* counts, const float* old_centroids, float* centroids,
+                  float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
+                  bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
     MXK_REQUIRE(!(zero_sums || host_state || acc_sums) || loop,
                 "finalize: zeroing, running sums and the host state need the loop words");
     MXK_REQUIRE(!acc_sums == !acc_counts, "finalize: running sums and counts go together");
@@ -448,7 +475,7 @@ int launch_finalize(int d, int k, float* sums, int* counts, const float* old_cen
     if (blocks > kShiftBlocks) blocks = kShiftBlocks;
     {
         LaunchScope scope("finalize", stream);
-        finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+        finalize_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(
             d, k, sums, counts, old_centroids, centroids, prev_out, shift_scratch, loop,
             loop ? reinterpret_cast<unsigned*>(shift_scratch + kShiftBlocks + 1) : nullptr,
             loop ? shift_scratch + kShiftBlocks : nullptr, tolerance, zero_sums ? 1 : 0, host_state, acc_sums,
@@ -462,6 +489,49 @@ int launch_finalize(int d, int k, float* sums, int* counts, const float* old_cen
         MXK_CUDA(cudaGetLastError());
     }
     return MXK_OK;
+}
+
+}  // namespace
+
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, float* sums,
+                      int* counts, cudaStream_t stream, const int* stop) {
+    return accumulate_impl(n, d, k, points, labels, order, sums, counts, stream, stop);
+}
+int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, double* sums,
+                      int* counts, cudaStream_t stream, const int* stop) {
+    return accumulate_impl(n, d, k, points, labels, order, sums, counts, stream, stop);
+}
+
+int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, double* sums,
+                              int* counts, cudaStream_t stream, const int* stop) {
+    MXK_REQUIRE(d > 0 && d % 4 == 0 && points && rec && count && sums && counts, "accumulate_changes: bad arguments");
+    MXK_REQUIRE(reinterpret_cast<uintptr_t>(points) % 16 == 0 && reinterpret_cast<uintptr_t>(sums) % 16 == 0,
+                "accumulate_changes: points and sums must be 16-byte aligned");
+    unsigned* err = device_error_word();
+    if (!err) return fail(MXK_ERR_CUDA, "accumulate_changes: cannot allocate the device error word");
+    LaunchScope scope("accumulate_changes", stream);
+    accumulate_changes_kernel<<<(unsigned)(sm_count() * 8), 256, 0, stream>>>(d, k, points, rec, count, sums, counts,
+                                                                             err, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
+// [0, kShiftBlocks): partials, [kShiftBlocks]: the total, [kShiftBlocks + 1]:
+// the finalize kernel's ticket counter (zero between launches)
+int64_t shift_scratch_floats() { return kShiftBlocks + 2; }
+int64_t shift_total_index() { return kShiftBlocks; }
+
+int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
+                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+    return finalize_impl(d, k, sums, counts, old_centroids, centroids, shift_scratch, stream, loop, tolerance, prev_out,
+                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word);
+}
+int launch_finalize(int d, int k, double* sums, int* counts, const float* old_centroids, float* centroids,
+                    float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
+                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+    return finalize_impl(d, k, sums, counts, old_centroids, centroids, shift_scratch, stream, loop, tolerance, prev_out,
+                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word);
 }
 
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,
