@@ -119,8 +119,9 @@ struct GemmParams {
     unsigned long long* tiles_done;  // count of multiplied 128 x 192 tiles (all K chunks)
     unsigned long long* rows_done;   // count of processed point rows
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
-    int best_dist_stride;  // best_dist[point * best_dist_stride]
-    const float2* row_bound;  // optional (argmin): MxArgmin::row_bound
+    int best_dist_stride;  // best_dist[point * best_dist_stride] (and MxArgmin::second_bound's at + 1)
+    const float4* row_bound;  // optional (argmin): MxArgmin::row_bound
+    const float* bmax32;      // MxArgmin::beta_max32 (kSec kernels)
     int4* changes;            // optional (argmin, with row_bound): MxArgmin::changes
     int* change_count;
     unsigned* err;
@@ -250,10 +251,14 @@ struct NormSrc {
 // bound rather than a candidate's).
 constexpr int kNoLabel = 0x7fffffff;
 
-// Running (distance, index) minimum and two largest distances of one row.
+// Running (distance, index) minimum and two largest distances of one row;
+// sec (kSec kernels): the smallest key seen, in the units of the screen's keys
+// fmaf(-2, dot, cn) -- a screened chunk's k_min, an exact distance less pn --
+// over every centroid other than the current minimum's.
 struct RowMin {
     float first, largest, next;
     int best;
+    float sec;
 };
 
 // Folds 32 consecutive columns c0..c0+31 (all < n) of one row into `m`:
@@ -263,10 +268,11 @@ struct RowMin {
 // or equal, resolved by the lower index as insert_distance does).  NaN
 // distances never compare, as in the reference.
 // force: evaluate the chunk even when its minimum exceeds m.first, taking it if
-// m holds no centroid yet (m.first is then only a bound).
-template <bool kGaps, class Norms>
+// m holds no centroid yet (m.first is then only a bound).  kSec: the columns
+// that are not (or no longer) the minimum lower m.sec.
+template <bool kGaps, bool kSec, class Norms>
 __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, int c0,
-                                               RowMin& m, bool force = false) {
+                                               RowMin& m, bool force = false, float pn = 0.0f) {
     float dist[32];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -295,10 +301,21 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const No
         for (int j = 30; j >= 0; --j) idx = dist[j] == cm ? j : idx;
         const int cand = c0 + idx;
         if (cm < m.first || (cm == m.first && cand < m.best) || m.best == kNoLabel) {
+            if constexpr (kSec) {  // the chunk's other columns and the previous minimum
+                const float inf = __int_as_float(0x7f800000);
+                float s2 = inf;
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                    s2 = dev::min3f(s2, j == idx ? inf : dist[j], j + 1 == idx ? inf : dist[j + 1]);
+                if (m.best != kNoLabel) s2 = fminf(s2, m.first);
+                m.sec = fminf(m.sec, s2 - pn);
+            }
             m.first = cm;
             m.best = cand;
+            return;
         }
     }
+    if constexpr (kSec) m.sec = fminf(m.sec, cm - pn);  // no column of the chunk is the minimum
 }
 
 // argmin_chunk32 behind a cheap screen.  Keys k_j = fmaf(-2, dot_j, cn_j) need
@@ -309,8 +326,10 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const No
 // and of its own excess over k_min, so d_j > first for every j in the chunk once
 // pn + k_min - 2^-20 * S > first.  Skipping then changes nothing: the result is
 // bit-identical to argmin_chunk32 alone.  NaN or infinite inputs fail the test
-// and take the exact path.  pc = pn + max(cn).
-template <class Norms>
+// and take the exact path.  pc = pn + max(cn).  kSec: a screened-out chunk
+// lowers m.sec to its k_min (each d_j >= pn + k_min - 2^-18 (pc + |k_min|) by
+// the same rounding argument).
+template <bool kSec, class Norms>
 __device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2,
                                                         float pn, float pc, int c0, RowMin& m, bool force) {
     // keys folded into two running 3-input minima as they are formed (few live registers)
@@ -326,13 +345,16 @@ __device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32],
     }
     const float kmin = fminf(ka, kb);
     const float scale = pc + fabsf(kmin) + fabsf(m.first);
-    if (!force && fmaf(-0x1p-20f, scale, pn + kmin) > m.first) return;
-    argmin_chunk32<false>(v, cn, pn2, c0, m, force);
+    if (!force && fmaf(-0x1p-20f, scale, pn + kmin) > m.first) {
+        if constexpr (kSec) m.sec = fminf(m.sec, kmin);
+        return;
+    }
+    argmin_chunk32<false, kSec>(v, cn, pn2, c0, m, force, pn);
 }
 
 // Columns c0.. of a 32-column chunk that runs past n: one column at a time
 // (column `forced` is taken while m holds no centroid, as in argmin_chunk32).
-template <bool kGaps, class Norms>
+template <bool kGaps, bool kSec, class Norms>
 __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms& cn, float pn, int c0, int64_t n,
                                             RowMin& m, int forced) {
 #pragma unroll
@@ -341,8 +363,12 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms
             const float dist = fmaf(-2.0f, __uint_as_float(v[j]), pn + cn.load1(c0 + j));
             if (dist < m.first || (dist == m.first && c0 + j < m.best) ||
                 (c0 + j == forced && m.best == kNoLabel && dist == dist)) {
+                if constexpr (kSec)
+                    if (m.best != kNoLabel) m.sec = fminf(m.sec, m.first - pn);
                 m.first = dist;
                 m.best = c0 + j;
+            } else if constexpr (kSec) {
+                m.sec = fminf(m.sec, dist - pn);
             }
             if constexpr (kGaps) {
                 m.next = fmaxf(m.next, fminf(m.largest, dist));
@@ -356,34 +382,47 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms
 // exact path when gaps are needed, one column at a time past n.  The chunk
 // holding column `forced` (the row's previous label, or -1) is always
 // evaluated exactly, so a row whose minimum starts at a bound finds a centroid.
-template <bool kGaps, class Norms>
+template <bool kGaps, bool kSec, class Norms>
 __device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, float pn, float pc,
                                            int cc, int64_t n, RowMin& m, int forced) {
     if (cc + 32 <= n) {
         if constexpr (kGaps)
-            argmin_chunk32<true>(v, cn, pn2, cc, m);
+            argmin_chunk32<true, false>(v, cn, pn2, cc, m);
         else
-            argmin_chunk32_screened(v, cn, pn2, pn, pc, cc, m, (unsigned)(forced - cc) < 32u);
+            argmin_chunk32_screened<kSec>(v, cn, pn2, pn, pc, cc, m, (unsigned)(forced - cc) < 32u);
     } else if (cc < n) {
-        argmin_tail<kGaps>(v, cn, pn, cc, n, m, forced);
+        argmin_tail<kGaps, kSec>(v, cn, pn, cc, n, m, forced);
     }
 }
 
 // Lexicographic (distance, index) minimum and two-largest merge of a partial
 // result (d, b, l, nx) into m; a partial without a centroid never displaces one.
-template <bool kGaps>
-__device__ __forceinline__ void merge_rowmin(RowMin& m, float d, int b, float l, float nx) {
-    if (b != kNoLabel && (d < m.first || (d == m.first && b < m.best) || m.best == kNoLabel)) m.first = d, m.best = b;
+// kSec: the partial's key bound s and whichever candidate loses (if it is
+// another centroid; its distance less pn) lower m.sec.
+template <bool kGaps, bool kSec = false>
+__device__ __forceinline__ void merge_rowmin(RowMin& m, float d, int b, float l, float nx, float s = 0.0f,
+                                             float pn = 0.0f) {
+    const bool take = b != kNoLabel && (d < m.first || (d == m.first && b < m.best) || m.best == kNoLabel);
+    if constexpr (kSec) {
+        if (take) {
+            if (m.best != kNoLabel && m.best != b) m.sec = fminf(m.sec, m.first - pn);
+        } else if (b != kNoLabel && b != m.best) {
+            m.sec = fminf(m.sec, d - pn);
+        }
+        m.sec = fminf(m.sec, s);
+    }
+    if (take) m.first = d, m.best = b;
     if constexpr (kGaps) {
         m.next = fmaxf(fminf(m.largest, l), fmaxf(m.next, nx));
         m.largest = fmaxf(m.largest, l);
     }
 }
 
-template <bool kArgmin, bool kGaps>
+template <bool kArgmin, bool kGaps, bool kSec = false>
 __global__ void __launch_bounds__(kThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
+    static_assert(!kSec || (kArgmin && !kGaps), "the second-nearest bound is an argmin-only, gap-free output");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const SmemLayout L = smem_layout(p.kchunks, p.a_stages, p.cn_smem, p.b_stages, p.sfb_atoms, p.fuse_x);
@@ -947,6 +986,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float c = warp_cmax[w];
             cmax = c > cmax || c != c ? c : cmax;
         }
+        // kSec: the largest beta of all centroids (the key bound's conversion)
+        float bmax_all = -__int_as_float(0x7f800000);
+        if constexpr (kSec) {
+            for (int c = lane; c < (int)((p.n + 31) >> 5); c += 32) bmax_all = fmaxf(bmax_all, __ldg(p.bmax32 + c));
+            for (int o = 16; o; o >>= 1) bmax_all = fmaxf(bmax_all, __shfl_xor_sync(0xffffffffu, bmax_all, o));
+        }
         RingPos rel{0, 0u, kBStages};
         uint32_t seed_ph = 0;  // phase of this quadrant's seed exchanges
         int s = 0;           // accumulator stage of the next tile
@@ -972,17 +1017,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto mask_of = [&](int64_t t) -> uint64_t {  // centroid tiles of point tile t
             return p.tile_mask && t < tiles_m ? p.tile_mask[t] : ~0ull;
         };
-        auto bound_of = [&](int64_t t) -> float2 {  // (bound, previous label) of this lane's row of tile t
+        auto bound_of = [&](int64_t t) -> float4 {  // (bound, previous label, excluded tiles' bound) of tile t's row
             const int64_t g = t * kBM + r;
+            const float inf = __int_as_float(0x7f800000);
             return kArgmin && p.row_bound && t < tiles_m && g < mrows ? p.row_bound[g]
-                                                                      : make_float2(__int_as_float(0x7f800000),
-                                                                                    __int_as_float(-1));
+                                                                      : make_float4(inf, __int_as_float(-1), inf, 0.0f);
         };
         int64_t id_cur = row_id(blockIdx.x), lead_cur = lead_id(blockIdx.x);
         float pn_cur = norm_of(id_cur);
         int hint_cur = hint_of(lead_cur);
         uint64_t mask_cur = mask_of(blockIdx.x);
-        float2 rb_cur = bound_of(blockIdx.x);
+        float4 rb_cur = bound_of(blockIdx.x);
         int64_t id_nxt = row_id(blockIdx.x + step), lead_nxt = lead_id(blockIdx.x + step);
         for (int64_t tile = blockIdx.x; tile < tiles_m && ok; tile += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -996,16 +1041,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int hint_nxt = hint_of(lead_nxt);
             const uint64_t tmask = mask_cur;
             const uint64_t mask_nxt = mask_of(tile + step);
-            const float2 rb = rb_cur;
-            const float2 rb_nxt = bound_of(tile + step);
+            const float4 rb = rb_cur;
+            const float4 rb_nxt = bound_of(tile + step);
             const int forced = __float_as_int(rb.y);
             const int64_t id_nn = row_id(tile + 2 * step), lead_nn = lead_id(tile + 2 * step);
             const uint64_t pn2 = dev::pack2(pn, pn);
             const float pc = pn + cmax;
-            RowMin m{rb.x, -1e38f, -1e38f, kNoLabel};
+            RowMin m{rb.x, -1e38f, -1e38f, kNoLabel, __int_as_float(0x7f800000)};
             for (int i = 0; i < tiles_n; ++i) {
                 const int ct = ct0 + i < tiles_n ? ct0 + i : ct0 + i - tiles_n;
                 if (!((tmask >> ct) & 1ull)) continue;  // pruned centroid tile (the first, ct0, never is)
+                const int slice0 = ct * kBN + j * kSliceCols;
                 if (!dev::mbar_wait(&acc_full[s], sph, abort_flag, p.err)) { ok = false; break; }
                 dev::tc_fence_after();
                 if (releaser) {
@@ -1023,7 +1069,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) dev::mbar_arrive(&acc_empty[s]);
                 if (++s == kAccStages) s = 0, sph ^= 1u;
-                const int slice0 = ct * kBN + j * kSliceCols;
 #pragma unroll
                 for (int sub = 0; sub < kSubChunks; ++sub) {
                     const int cc = slice0 + sub * 32;
@@ -1043,9 +1088,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                     } else if (p.cn_smem) {
-                        fold_chunk<kGaps>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m, forced);
+                        fold_chunk<kGaps, kSec>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m,
+                                                forced);
                     } else {
-                        fold_chunk<kGaps>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m, forced);
+                        fold_chunk<kGaps, kSec>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m, forced);
                     }
                 }
                 if (seeding && i == 0 && (tmask & (tmask - 1ull)) != 0) {  // (more tiles follow in this row tile)
@@ -1062,7 +1108,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int o = 0; o < kEpiPerQuad; ++o) {
                         if (o == j) continue;
                         const float2 sd = mine[o * kBM + r];
-                        merge_rowmin<false>(m, sd.x, __float_as_int(sd.y), 0.0f, 0.0f);
+                        // (the partial's bound comes with the final merge)
+                        merge_rowmin<false, kSec>(m, sd.x, __float_as_int(sd.y), 0.0f, 0.0f,
+                                                  __int_as_float(0x7f800000), pn);
                     }
                 }
             }
@@ -1075,7 +1123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4* slots = merge + (size_t)buf * (kEpiPerQuad - 1) * kBM;
                 if (j != 0) {
                     if (!dev::mbar_wait(&merge_empty[hb], hph ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                    slots[(j - 1) * kBM + r] = make_float4(m.first, __int_as_float(m.best), m.largest, m.next);
+                    slots[(j - 1) * kBM + r] =
+                        make_float4(m.first, __int_as_float(m.best), kSec ? m.sec : m.largest, m.next);
                     __syncwarp();
                     if (lane == 0) dev::mbar_arrive(&merge_full[hb]);
                 } else {
@@ -1088,9 +1137,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (valid) {
 #pragma unroll
                         for (int w = 0; w < kEpiPerQuad - 1; ++w)
-                            merge_rowmin<kGaps>(m, o[w].x, __float_as_int(o[w].y), o[w].z, o[w].w);
+                            merge_rowmin<kGaps, kSec>(m, o[w].x, __float_as_int(o[w].y), o[w].z, o[w].w, o[w].z,
+                                                      pn);
                         p.labels[point] = m.best;
-                        if (p.best_dist) p.best_dist[point * p.best_dist_stride] = m.first;
+                        if constexpr (kSec) {
+                            // keys -> a bound on d - beta_c (less the largest beta), with the
+                            // excluded tiles' bound from the row record
+                            const float sec = fminf(rb.z, fmaf(-0x1p-18f, pc + fabsf(m.sec), pn + m.sec) - bmax_all);
+                            *reinterpret_cast<float2*>(p.best_dist + point * p.best_dist_stride) =
+                                make_float2(m.first, sec);
+                        }
+                        else if (p.best_dist)
+                            p.best_dist[point * p.best_dist_stride] = m.first;
                         if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
                     if (p.changes) {  // label changes, one counter update per warp
@@ -1190,6 +1248,12 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         p.best_dist = argmin->best_dist;
         p.best_dist_stride = argmin->best_dist_stride;
         p.row_bound = argmin->row_bound;
+        p.bmax32 = argmin->beta_max32;
+        MXK_REQUIRE(!argmin->second_bound ||
+                        (p.best_dist && p.bmax32 && !p.gaps && p.best_dist_stride >= 2 &&
+                         p.best_dist_stride % 2 == 0 && aligned(p.best_dist, 8)),
+                    "gemm_mx: the second-nearest bound needs best_dist (even stride, 8-byte aligned), beta_max32 "
+                    "and no gaps");
         p.changes = argmin->changes;
         p.change_count = argmin->change_count;
         MXK_REQUIRE(!p.changes || (p.row_bound && p.change_count), "gemm_mx: label changes need row bounds and a count");
@@ -1290,6 +1354,8 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         st = launch(mx_gemm_kernel<false, false>, "mx_gemm_dense");
     else if (argmin->gaps)
         st = launch(mx_gemm_kernel<true, true>, "mx_gemm_argmin_gap");
+    else if (argmin->second_bound)
+        st = launch(mx_gemm_kernel<true, false, true>, "mx_gemm_argmin");
     else
         st = launch(mx_gemm_kernel<true, false>, "mx_gemm_argmin");
     if (tmp_atoms) cudaFreeAsync(tmp_atoms, stream);

@@ -30,9 +30,9 @@ inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileR
 }
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
 // launch_l2_norm's norms (bit-identical) and, per point, the pruning pass's
-// pinfo = (+inf: the slot the GEMM writes the point's distance into,
-// |x|^2 - |x^|^2, |x^|^2, |x|^2) for its MXFP8 round trip x^, in one pass over
-// the points.  d % 128 == 0, points 16-byte aligned.
+// pinfo = (+inf and 0: the slots the GEMM writes the point's distance and its
+// second-nearest bound into, |x|^2 - |x^|^2, |x^|^2) for its MXFP8 round trip
+// x^, in one pass over the points.  d % 128 == 0, points 16-byte aligned.
 int launch_point_norm_stats(int64_t n, int d, const float* points, float* norms, float4* pinfo,
                             cudaStream_t stream);
 // Rows of an MXFP8 matrix (d bytes per row, d / 32 row-major scale bytes)
@@ -67,6 +67,13 @@ int64_t label_sort_scratch_ints(int k);
 // stop (optional, device word): non-zero at run time = do nothing.
 int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream,
                       const int* stop = nullptr);
+// Rebuild gate for the label sort: ctl = (label changes since the last
+// rebuild, skip word), zero at the start of a run.  Adds *changes (this
+// iteration's label changes) and sets the skip word -- the stop word to pass to
+// launch_label_sort -- unless at least `threshold` labels have changed since
+// the last rebuild (then clears it and restarts the count); also set while
+// *stop is.
+int launch_sort_gate(const int* stop, const int* changes, int* ctl, int threshold, cudaStream_t stream);
 
 // ---- gemm_mx.cu ---------------------------------------------------------------
 struct MxArgmin {
@@ -87,12 +94,21 @@ struct MxArgmin {
     // best_dist[point * best_dist_stride]
     float* best_dist = nullptr;
     int best_dist_stride = 1;
+    // with best_dist (stride >= 2, 8-byte aligned rows) and beta_max32: also a
+    // lower bound on d(x, c) - beta_c for every centroid c other than the
+    // point's nearest, at best_dist[point * best_dist_stride + 1] (from the
+    // screened chunk minima and the exact chunks, each less the largest beta of
+    // its 32 centroids, and, with row_bound, the bound of the tiles the row's
+    // own mask excludes); beta_c = |c|^2 - |c^|^2 of the MXFP8 round trip c^
+    bool second_bound = false;
+    const float* beta_max32 = nullptr;  // [ceil(n / 32)] the largest beta of each 32 consecutive centroids
     // optional, per GEMM row (the order of pid): (an upper bound on the row's
     // distance to its nearest centroid or inf, the row's previous label as int
-    // bits or -1).  The epilogue starts each row's minimum at the bound and
-    // always evaluates the chunk holding the previous label exactly; the
-    // result is unchanged.
-    const float2* row_bound = nullptr;
+    // bits or -1, a lower bound on d(x, c) - beta_c for every centroid c of the
+    // tiles its own mask excludes or +inf, unused).  The epilogue starts each row's
+    // minimum at the bound and always evaluates the chunk holding the previous
+    // label exactly; the result is unchanged.
+    const float4* row_bound = nullptr;
     // optional (with row_bound): every row whose label differs from its
     // previous one (row_bound's) is recorded as (point, previous, new, 0) at
     // changes[atomicAdd(change_count, 1)]
@@ -126,19 +142,21 @@ int launch_centroid_prep(int k, int d, const float* centroids, const float* prev
                          float4* cst, float* delta, uint8_t* qcent, uint8_t* cscales, const int* stop,
                          cudaStream_t stream);
 // dmin (k x tiles lower bounds of quantized centroid-to-tile distances, from
-// an FP32 Gram product reduced in registers) and tst (per tile: min beta, max
-// |c^|^2, max |c|^2, non-finite flag) from chat and cst.
-int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
-                          cudaStream_t stream);
+// an FP32 Gram product reduced in registers), the tile stats tst (2 x tiles:
+// per tile t, tst[t] = (min beta, max |c^|^2, max |c|^2, non-finite flag) and
+// tst[tiles + t] = (max beta, max delta, 0, 0)) and bmax32 (ceil(k / 32): the
+// largest beta of each 32 consecutive centroids) from chat, cst and delta.
+int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, const float* delta, float* dmin,
+                          float4* tst, float* bmax32, const int* stop, cudaStream_t stream);
 // Between full computations: dmin lowered in place by the centroids' movement
-// bounds (delta, from launch_centroid_prep), and tst as above.
+// bounds (delta, from launch_centroid_prep), and tst and bmax32 as above.
 int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* cst, float* dmin, float4* tst,
-                                const int* stop, cudaStream_t stream);
+                                float* bmax32, const int* stop, cudaStream_t stream);
 // Row compaction of the pruned fused iteration (launch_tile_mask's `work`):
 // device buffers for the rows that stay in the GEMM, in visiting order.
 struct WorkRows {
     int* pid = nullptr;            // [rows] their point ids
-    float2* rb = nullptr;          // [rows] their MxArgmin::row_bound records
+    float4* rb = nullptr;          // [rows] their MxArgmin::row_bound records
     unsigned long long* cmask = nullptr;  // [row tiles] centroid-tile masks of the compacted 128-row tiles
     uint4* need_bits = nullptr;    // [row tiles] scratch: which rows of each tile stay
     int* counts = nullptr;         // [row tiles] scratch
@@ -149,16 +167,19 @@ struct WorkRows {
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
 // may hold a row's nearest centroid, from the previous labels and distances
 // and the current (cst) and previous (cst_old) centroid stats; row_bound
-// (optional, one per row) receives MxArgmin::row_bound's records.  With work:
-// a row whose bounds prove that every other centroid is strictly farther than
-// its previous label's keeps that label and leaves the GEMM (its pinfo
-// distance becomes its upper bound); the other rows are compacted into work
-// (ids, records, masks of the compacted tiles, count), for a GEMM launched on
-// work->pid with rows_dev = work->rows.
+// (optional, one per row) receives MxArgmin::row_bound's records.  tst_old
+// (optional): the tile stats of the previous iteration's centroids, when that
+// iteration's GEMM wrote its points' second-nearest bounds into pinfo (the
+// row test then also uses them).  With work: a row whose bounds prove that
+// every other centroid is strictly farther than its previous label's keeps
+// that label and leaves the GEMM (its pinfo distance becomes its upper bound,
+// its second-nearest bound the lower one); the other rows are compacted into
+// work (ids, records, masks of the compacted tiles, count), for a GEMM launched
+// on work->pid with rows_dev = work->rows.
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
-                     const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream,
-                     WorkRows* work = nullptr);
+                     const float4* cst, const float4* cst_old, const float4* tst, const float4* tst_old,
+                     const float* delta, const float* dmin, uint64_t* mask, float4* row_bound, const int* stop,
+                     cudaStream_t stream, WorkRows* work = nullptr);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

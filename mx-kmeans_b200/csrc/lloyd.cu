@@ -239,6 +239,9 @@ constexpr int kLookahead = 8;
 // is nearly as good: measured at configs[3], every second iteration saves the
 // 0.21 ms sort on half of them and costs the GEMM < 0.02 ms.
 constexpr int kResortEvery = 2;
+// Pruned fused iterations rebuild the order once n / kResortChangeDiv labels
+// have changed since the last rebuild.
+constexpr int64_t kResortChangeDiv = 32;
 // Full centroid-pair bound computations: the first kPairsFullFirst pruned
 // iterations, then every kPairsFullEvery-th (drift updates in between).
 constexpr int kPairsFullFirst = 3;
@@ -356,9 +359,11 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&gcount, 4));
         MXK_CHECK(ws.alloc(&cscratch, compaction_scratch_ints(n)));
     }
-    int *order = nullptr, *sort_scratch = nullptr;
+    int *order = nullptr, *sort_scratch = nullptr, *sort_ctl = nullptr;
     MXK_CHECK(ws.alloc(&order, n));
     MXK_CHECK(ws.alloc(&sort_scratch, label_sort_scratch_ints(k)));
+    MXK_CHECK(ws.alloc(&sort_ctl, 2));
+    MXK_CUDA(cudaMemsetAsync(sort_ctl, 0, sizeof(int) * 2, stream));
     // Opt-in point cache: under the forced-MXFP8 policy the points' MXFP8 bytes
     // never change, so they are quantized once per call and only regathered
     // when the visiting order changes (the reference re-quantizes every
@@ -409,18 +414,21 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     // labels and distances: forced-MXFP8 path, at most 64 centroid tiles.
     const bool prune = forced8 && n > 0 && prune_supported(k, d);
     const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
-    float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr;
-    float4* pinfo = nullptr;  // per point: (distance from the last GEMM, alpha, |x^|^2, |x|^2)
-    float4 *cstats = nullptr, *tstats = nullptr;  // [2][k] per-centroid stats by iteration parity; [ctiles]
+    float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *bmax32 = nullptr;
+    // per point: (distance from the last GEMM, its bound on every other centroid's distance, alpha, |x^|^2)
+    float4* pinfo = nullptr;
+    // per-centroid stats [2][k] and per-tile stats [2][2][ctiles], by iteration parity
+    float4 *cstats = nullptr, *tstats = nullptr;
     uint64_t* tmask = nullptr;
-    float2* rbound = nullptr;  // per row in visiting order: (distance bound, previous label)
+    float4* rbound = nullptr;  // per row in visiting order: (distance bound, previous label, excluded tiles' bound)
     if (prune) {
         MXK_CHECK(ws.alloc(&pinfo, n));
         MXK_CHECK(ws.alloc(&chat, kd));
         MXK_CHECK(ws.alloc(&dmin, (int64_t)k * ctiles));
         MXK_CHECK(ws.alloc(&cdelta, k));
         MXK_CHECK(ws.alloc(&cstats, 2 * (int64_t)k));
-        MXK_CHECK(ws.alloc(&tstats, ctiles));
+        MXK_CHECK(ws.alloc(&tstats, 4 * (int64_t)ctiles));
+        MXK_CHECK(ws.alloc(&bmax32, (k + 31) / 32));
         MXK_CHECK(ws.alloc(&tmask, (n + kPointTileRows - 1) / kPointTileRows));
         MXK_CHECK(ws.alloc(&rbound, n));
         MXK_CHECK(ws.alloc(&chg, n));
@@ -495,6 +503,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         const bool prune_it = prune && it >= 1 && it - 1 >= options->fp32_iterations;
         float4* cst = cstats + (int64_t)(it & 1) * k;
         const float4* cst_old = cstats + (int64_t)((it + 1) & 1) * k;
+        float4* tst = tstats + (int64_t)(it & 1) * 2 * ctiles;
+        const float4* tst_old = tstats + (int64_t)((it + 1) & 1) * 2 * ctiles;
         // MX iterations with pruning: the centroid norms, the centroids' MXFP8
         // codes and scales and their pruning stats (this iteration's, the next
         // one's old ones) in one pass; otherwise the norms alone here.
@@ -514,12 +524,15 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             // (K x tiles work).  Either way the labels are exact.
             const bool drift_ok = n < (int64_t)k * kPairsDriftRowsPerCentroid;
             if (!drift_ok || pruned_its < kPairsFullFirst || pruned_its % kPairsFullEvery == 0)
-                MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, dmin, tstats, loop, stream));
+                MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, cdelta, dmin, tst, bmax32, loop, stream));
             else
-                MXK_CHECK(launch_centroid_pairs_drift(k, d, cdelta, cst, dmin, tstats, loop, stream));
+                MXK_CHECK(launch_centroid_pairs_drift(k, d, cdelta, cst, dmin, tst, bmax32, loop, stream));
+            // The second-nearest bounds in pinfo come from the previous
+            // iteration's GEMM when that iteration was pruned too (its tile
+            // stats, tst_old, describe the centroids it used).
+            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tst, pruned_its > 0 ? tst_old : nullptr,
+                                       cdelta, dmin, tmask, rbound, loop, stream, compact ? &work : nullptr));
             ++pruned_its;
-            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tstats, cdelta, dmin, tmask, rbound,
-                                       loop, stream, compact ? &work : nullptr));
         }
         const bool traced = it < trace.max_iterations;
         if (traced && trace.centroids)
@@ -573,6 +586,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.change_count = prune_it ? chg_count : nullptr;
             am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
+            am.second_bound = prune_it;  // (pinfo's second slot)
+            am.beta_max32 = bmax32;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows, stream,
                                      true, fused_q ? points : nullptr, n));
             if (traced && trace.group_sizes)  // (0, 0, rows of the MXFP8 group)
@@ -629,11 +644,20 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         // changes) adds only the moved rows to the running sums; any other
         // iteration accumulates every point afresh.
         const bool incremental = prune_it && forced8;
-        // Every kResortEvery-th iteration sorts the points by the labels just
-        // assigned: the next iteration visits them in that order, and a fresh
-        // accumulation below sees one run per cluster.
-        if (n > 0 && it % kResortEvery == 0 && (!incremental || it + 1 < options->max_iterations)) {
-            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, loop));
+        // The points are sorted by the labels just assigned: the next iteration
+        // visits them in that order, and a fresh accumulation below sees one
+        // run per cluster.  Every kResortEvery-th iteration, or, in pruned
+        // iterations of the fused path (which record their label changes), once
+        // at least n / kResortChangeDiv labels have changed since the last sort
+        // (decided on the device; the order stays a valid permutation either
+        // way).  The last iteration of an incremental run needs no new order.
+        const bool gated = incremental && !cache;
+        if (n > 0 && (gated ? it + 1 < options->max_iterations
+                            : it % kResortEvery == 0 && (!incremental || it + 1 < options->max_iterations))) {
+            if (gated)
+                MXK_CHECK(launch_sort_gate(loop, chg_count, sort_ctl,
+                                           (int)std::max<int64_t>(1, n / kResortChangeDiv), stream));
+            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, gated ? sort_ctl + 1 : loop));
             cached_stale = true;
             ord = order;
         }

@@ -140,7 +140,33 @@ __global__ void __launch_bounds__(512) label_scatter_kernel(int64_t n, int k, co
     }
 }
 
+// ctl = (label changes since the visiting order was last rebuilt, skip word).
+// The skip word is set (the label sort that follows does nothing) while the
+// loop has stopped or fewer than `threshold` labels have changed since the last
+// rebuild, counting this iteration's *changes; otherwise it is cleared and the
+// count starts over.
+__global__ void sort_gate_kernel(const int* __restrict__ stop, const int* __restrict__ changes, int* __restrict__ ctl,
+                                 int threshold) {
+    if (threadIdx.x != 0) return;
+    if (stop && *stop) {
+        ctl[1] = 1;
+        return;
+    }
+    const int since = ctl[0] + *changes;
+    const bool sort = since >= threshold;
+    ctl[0] = sort ? 0 : since;
+    ctl[1] = sort ? 0 : 1;
+}
+
 }  // namespace
+
+int launch_sort_gate(const int* stop, const int* changes, int* ctl, int threshold, cudaStream_t stream) {
+    MXK_REQUIRE(changes && ctl, "sort_gate: bad arguments");
+    LaunchScope scope("sort_gate", stream);
+    sort_gate_kernel<<<1, 32, 0, stream>>>(stop, changes, ctl, threshold);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
 
 int64_t label_sort_scratch_ints(int k) { return k; }
 

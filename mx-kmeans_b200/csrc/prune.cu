@@ -23,6 +23,18 @@
 //   max(0, dmin(a, T) - r)^2 + alpha_x + min_T beta - rho_T.  When that exceeds
 //   U, no centroid of T can be x's nearest (nor tie with it): T is skipped.
 //
+// * Second-nearest bound (Hamerly's bound, in the same space).  The GEMM also
+//   writes, per point, sec <= d(x, c_old) - beta_c_old for every centroid c
+//   other than the label it chose (from its screened chunk minima, the exact
+//   chunks, each less the largest beta of its 32 centroids, and the bounds of
+//   the tiles the row's mask excluded).  So |x^ - c^_old|^2 >= sec - alpha_x -
+//   rho_old, |x^ - c^| >= that root - max delta, and d(x, c) >= (that)^2 +
+//   alpha_x + min beta - rho for every c != a: when that exceeds U the row
+//   keeps its label without the per-tile test.  A row that leaves the GEMM gets
+//   the smallest of its tiles' lower bounds (less beta) as its next sec.  Kept
+//   free of beta, the bound loses only the centroids' movement and rounding
+//   margins from one iteration to the next.
+//
 // A point tile computes the union of its rows' tiles (each row's own tile
 // always among them).  Every bound is evaluated with outward margins well above
 // the FP32 rounding of its own arithmetic, and any non-finite input keeps every
@@ -70,7 +82,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // order, carried from lane to lane), its MXFP8 codes and UE8M0 scales (the
 // bytes quantize_rows writes, scales in the GEMM's atom layout for 192-row
 // tiles), the dequantized row c^ into chat, stats cst[a] = (beta = |c|^2 -
-// |c^|^2, |c^|^2, |c|^2, 0), and delta[a] >= |c^_a - c^_a_old| (the previous
+// |c^|^2, |c^|^2, |c|^2, |c^|), and delta[a] >= |c^_a - c^_a_old| (the previous
 // centroids' round trip; +inf without prev).
 __global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const float* __restrict__ c,
                                                             const float* __restrict__ prev, float* __restrict__ cn,
@@ -118,37 +130,60 @@ __global__ void __launch_bounds__(256) centroid_prep_kernel(int k, int d, const 
         const float rel = 1.0f + (float)(d + 8) * 1.2e-7f;  // rounding of an FP32 sum of d squares
         delta[a] = prev ? sqrtf(mv * rel) * (1.0f + 1e-6f) : __int_as_float(0x7f800000);
         cn[a] = norm;
-        cst[a] = make_float4(norm - h, h, norm, 0.0f);
+        cst[a] = make_float4(norm - h, h, norm, sqrtf(h));
     }
 }
 
-// tst[t] = (min beta, max |c^|^2, max |c|^2, non-finite flag) over the
-// centroids of tile t, by one whole block of kPairThreads threads.
-__device__ void tile_stats_block(int k, int t, const float4* __restrict__ cst, float4* __restrict__ tst) {
+// The stats of tile t over its centroids, by one whole block of kPairThreads
+// threads: tst[t] = (min beta, max |c^|^2, max |c|^2, non-finite flag),
+// tst[tiles + t] = (max beta, max delta (+inf for a non-finite one), the root of
+// max |c^|^2, 0) and
+// bmax32[c / 32] = the largest beta of each 32 consecutive centroids.
+__device__ void tile_stats_block(int k, int t, int tiles, const float4* __restrict__ cst,
+                                 const float* __restrict__ delta, float4* __restrict__ tst,
+                                 float* __restrict__ bmax32) {
+    static_assert(kPairCols % 32 == 0 && kPairThreads % 32 == 0, "32-centroid groups inside one warp");
     __shared__ float4 part[kPairThreads / 32];
+    __shared__ float2 part2[kPairThreads / 32];
     const float inf = __int_as_float(0x7f800000);
     float4 m = make_float4(inf, 0.0f, 0.0f, 0.0f);
-    for (int j = threadIdx.x; j < kPairCols; j += kPairThreads) {
+    float bmax = -inf, dmax = 0.0f;
+    for (int j0 = 0; j0 < kPairCols; j0 += kPairThreads) {
+        const int j = j0 + (int)threadIdx.x;
         const int b = t * kPairCols + j;
-        if (b >= k) break;
-        const float4 v = cst[b];
-        m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
-        if (!(fabsf(v.x) < inf && v.y < inf && v.z < inf)) m.w = 1.0f;  // a non-finite centroid: no pruning
+        const bool valid = j < kPairCols && b < k;
+        float b32 = -inf;
+        if (valid) {
+            const float4 v = cst[b];
+            m.x = fminf(m.x, v.x), m.y = fmaxf(m.y, v.y), m.z = fmaxf(m.z, v.z);
+            if (!(fabsf(v.x) < inf && v.y < inf && v.z < inf)) m.w = 1.0f;  // a non-finite centroid: no pruning
+            bmax = fmaxf(bmax, v.x);
+            b32 = v.x;
+            const float dv = delta[b];
+            dmax = dv < inf ? fmaxf(dmax, dv) : inf;  // (NaN counts as infinite)
+        }
+        for (int o = 16; o; o >>= 1) b32 = fmaxf(b32, __shfl_xor_sync(0xffffffffu, b32, o));
+        const int b0 = b - (int)(threadIdx.x & 31);  // the warp's first centroid
+        if ((threadIdx.x & 31) == 0 && j < kPairCols && b0 < k) bmax32[b0 >> 5] = b32;
     }
     for (int o = 16; o; o >>= 1) {
         m.x = fminf(m.x, __shfl_xor_sync(0xffffffffu, m.x, o));
         m.y = fmaxf(m.y, __shfl_xor_sync(0xffffffffu, m.y, o));
         m.z = fmaxf(m.z, __shfl_xor_sync(0xffffffffu, m.z, o));
         m.w = fmaxf(m.w, __shfl_xor_sync(0xffffffffu, m.w, o));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+        dmax = fmaxf(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
     }
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m, part2[threadIdx.x >> 5] = make_float2(bmax, dmax);
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < kPairThreads / 32; ++w) {
             const float4 o = part[w];
             m.x = fminf(m.x, o.x), m.y = fmaxf(m.y, o.y), m.z = fmaxf(m.z, o.z), m.w = fmaxf(m.w, o.w);
+            bmax = fmaxf(bmax, part2[w].x), dmax = fmaxf(dmax, part2[w].y);
         }
         tst[t] = m;
+        tst[tiles + t] = make_float4(bmax, dmax, sqrtf(m.y), 0.0f);
     }
 }
 
@@ -159,14 +194,15 @@ __device__ void tile_stats_block(int k, int t, const float4* __restrict__ cst, f
 // |c^_b|) for the rounding of the product, the norms and this sum; 0 when no
 // finite bound exists.  The Gram block is reduced to its per-row minima in
 // registers, so no K x K product is stored.  The first block of each tile
-// column also writes the tile's stats tst[T] = (min beta, max |c^|^2, max
-// |c|^2, non-finite flag) over its centroids.
+// column also writes the tile's stats (tile_stats_block).
 __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d, int tiles, const float* __restrict__ chat,
                                                                    const float4* __restrict__ cst,
+                                                                   const float* __restrict__ delta,
                                                                    float* __restrict__ dmin, float4* __restrict__ tst,
+                                                                   float* __restrict__ bmax32,
                                                                    const int* __restrict__ stop) {
     if (stop && *stop) return;
-    if (blockIdx.x == 0) tile_stats_block(k, blockIdx.y, cst, tst);
+    if (blockIdx.x == 0) tile_stats_block(k, blockIdx.y, tiles, cst, delta, tst, bmax32);
     __shared__ __align__(16) float As[kPairChunk][kPairRows];
     __shared__ __align__(16) float Bs[kPairChunk][kPairCols];
     __shared__ float hb_s[kPairCols], sb_s[kPairCols];
@@ -248,10 +284,11 @@ __global__ void __launch_bounds__(kPairThreads) pair_bounds_kernel(int k, int d,
 __global__ void __launch_bounds__(kPairThreads) pair_drift_kernel(int k, int tiles, const float* __restrict__ delta,
                                                                   const float4* __restrict__ cst,
                                                                   float* __restrict__ dmin, float4* __restrict__ tst,
+                                                                  float* __restrict__ bmax32,
                                                                   const int* __restrict__ stop) {
     if (stop && *stop) return;
     if ((int)blockIdx.x < tiles) {
-        tile_stats_block(k, blockIdx.x, cst, tst);
+        tile_stats_block(k, blockIdx.x, tiles, cst, delta, tst, bmax32);
         return;
     }
     __shared__ unsigned tmax[kMaxPruneTiles];  // per tile max delta (non-negative: integer order)
@@ -275,9 +312,10 @@ __global__ void __launch_bounds__(kPairThreads) pair_drift_kernel(int k, int til
 }
 
 // The rounding term rho of the header comment for squared norms px, pc (of x and
-// c) and hx2, hc2 (of x^ and c^).
-__device__ __forceinline__ float rho_bound(float px, float hx2, float pc, float hc2, float kappa) {
-    return kappa * (px + pc + hx2 + hc2 + 2.0f * sqrtf(hx2) * sqrtf(hc2));
+// c) and hx2, hc2 (of x^ and c^), from pxh = px + hx2 and the roots shx =
+// |x^|, shc = |c^|.
+__device__ __forceinline__ float rho_bound(float pxh, float shx, float pc, float hc2, float shc, float kappa) {
+    return kappa * (pxh + pc + hc2 + 2.0f * shx * shc);
 }
 
 // One block per 128-row point tile: the union over its rows of the centroid
@@ -285,81 +323,152 @@ __device__ __forceinline__ float rho_bound(float px, float hx2, float pc, float 
 // compaction) a row whose every other centroid -- its own tile's included,
 // through dmin[a][own], which leaves a out -- lies strictly beyond its upper
 // bound keeps its label: it is left out of the GEMM (need_bits, counts), its
-// distance for the next iteration's bounds becomes that upper bound, and the
-// tile's mask is the union over the rows that remain; cmask[blockIdx.x] is
-// zeroed for the compacted masks of work_scatter_kernel.
+// distance for the next iteration's bounds becomes that upper bound and its
+// second-nearest bound the smallest lower bound of its tiles, and the tile's
+// mask is the union over the rows that remain; cmask[blockIdx.x] is zeroed
+// for the compacted masks of work_scatter_kernel.  tst / tst_old: 2 x tiles
+// stats of the current and (optional) previous centroids; without tst_old or
+// with a non-finite centroid the second-nearest bounds are not used.  Blocks
+// loop over point tiles (blockIdx.x, + gridDim.x, ...).
 __global__ void __launch_bounds__(128) tile_mask_kernel(
     int64_t rows, int k, int d, int tiles, int tile_cols, const int* __restrict__ pid,
     const int* __restrict__ prev_label, float4* __restrict__ pinfo, const float4* __restrict__ cst,
-    const float4* __restrict__ cst_old,
-    const float4* __restrict__ tst, const float* __restrict__ delta, const float* __restrict__ dmin,
-    uint64_t* __restrict__ mask, float2* __restrict__ row_bound, int compact, uint4* __restrict__ need_bits,
-    int* __restrict__ tile_count, uint64_t* __restrict__ cmask, const int* __restrict__ stop) {
+    const float4* __restrict__ cst_old, const float4* __restrict__ tst, const float4* __restrict__ tst_old,
+    const float* __restrict__ delta, const float* __restrict__ dmin, uint64_t* __restrict__ mask,
+    float4* __restrict__ row_bound, int compact, uint4* __restrict__ need_bits, int* __restrict__ tile_count,
+    uint64_t* __restrict__ cmask, const int* __restrict__ stop) {
     if (stop && *stop) return;
-    const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
-    const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
-    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
     const float inf = __int_as_float(0x7f800000);
-    uint64_t m = 0;
-    bool need = false;
-    // (bound on the row's nearest distance, its previous label) for the GEMM's
-    // screen: (inf, label) when no finite bound holds, (inf, -1) without a
-    // valid previous label
-    float2 rb = make_float2(inf, __int_as_float(-1));
-    if (row < rows) {
-        const int64_t x = pid ? pid[row] : row;
-        const int a = prev_label[x];
-        m = all;
-        need = true;
-        if ((unsigned)a < (unsigned)k) {
-            rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
-            const float4 pi = pinfo[x];  // (previous distance, alpha_x, |x^|^2, |x|^2)
-            const float dp = pi.x, px = pi.w;
-            const float2 ps = make_float2(pi.y, pi.z);
-            const float4 now = cst[a], old = cst_old[a];
-            const float r0 = dp - ps.x - old.x + rho_bound(px, ps.y, old.z, old.y, kappa);
-            const float r = (sqrtf(fmaxf(r0, 0.0f)) * (1.0f + 1e-6f) + delta[a]) * (1.0f + 1e-6f);
-            const float u = r * r * (1.0f + 1e-6f) + ps.x + now.x + rho_bound(px, ps.y, now.z, now.y, kappa);
-            const float um = u + 1e-4f * (fabsf(u) + fabsf(ps.x) + fabsf(now.x)) + 1e-30f;
-            if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(ps.x) < inf) {  // false for NaN too: keep every tile
-                m = 1ull << (a / tile_cols);  // its own tile
-                need = false;
-                // The screen only needs some upper bound: a wider margin costs
-                // nothing measurable and keeps it far from the rounding terms.
-                const float us = um + 1e-3f * (fabsf(um) + fabsf(ps.x) + fabsf(now.x));
-                if (fabsf(us) < inf) rb.x = us;
-                const float* dm = dmin + (int64_t)a * tiles;
-                for (int t = 0; t < tiles; ++t) {
-                    const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
-                    const float g = fmaxf(dm[t] - r, 0.0f);
-                    const float lb = g * g * (1.0f - 1e-6f) + ps.x + ts.x - rho_bound(px, ps.y, ts.z, ts.y, kappa);
-                    const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(ps.x) + fabsf(ts.x));
-                    if (!(lbm > um) || ts.w != 0.0f) {
-                        m |= 1ull << t;
-                        need = true;
-                    }
-                }
-                if (compact && !need) pinfo[x].x = um;  // the label stands; its distance bound for next time
+    // Whole-centroid-set terms of the second-nearest test (gs, below); usable
+    // when every tile is finite.
+    __shared__ float gs[8];
+    __shared__ int g_ok;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        // v = (min beta, max |c^|^2, max |c|^2, max delta; previous: max |c^|^2, max |c|^2)
+        float v[6] = {inf, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        float bad = tst_old ? 0.0f : 1.0f;
+        if (tst_old) {
+            for (int t = lane; t < tiles; t += 32) {
+                const float4 a = tst[t], b = tst[tiles + t], c = tst_old[t];
+                v[0] = fminf(v[0], a.x), v[1] = fmaxf(v[1], a.y), v[2] = fmaxf(v[2], a.z), v[3] = fmaxf(v[3], b.y);
+                v[4] = fmaxf(v[4], c.y), v[5] = fmaxf(v[5], c.z);
+                bad = fmaxf(bad, fmaxf(a.w, c.w));
             }
         }
+        for (int o = 16; o; o >>= 1) {
+            v[0] = fminf(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+#pragma unroll
+            for (int i = 1; i < 6; ++i) v[i] = fmaxf(v[i], __shfl_xor_sync(0xffffffffu, v[i], o));
+            bad = fmaxf(bad, __shfl_xor_sync(0xffffffffu, bad, o));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < 6; ++i) gs[i] = v[i];
+            gs[6] = sqrtf(v[1]), gs[7] = sqrtf(v[4]);  // roots of the max |c^|^2, current and previous
+            g_ok = bad == 0.0f;
+        }
     }
-    if (compact && !need) m = 0;
-    if (row_bound && row < rows) row_bound[row] = rb;
-    // union over the 128 rows
-    m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
-        ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
-    const unsigned nb = __ballot_sync(0xffffffffu, need);
+    __syncthreads();
+    const bool second = g_ok != 0;
+    const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
+    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
+    const int64_t ntiles = (rows + 127) / 128;
     __shared__ uint64_t part[4];
     __shared__ unsigned bits[4];
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m, bits[threadIdx.x >> 5] = nb;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        mask[blockIdx.x] = part[0] | part[1] | part[2] | part[3];
-        if (compact) {
-            need_bits[blockIdx.x] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
-            tile_count[blockIdx.x] = __popc(bits[0]) + __popc(bits[1]) + __popc(bits[2]) + __popc(bits[3]);
-            cmask[blockIdx.x] = 0ull;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t row = tile * 128 + threadIdx.x;
+        uint64_t m = 0;
+        bool need = false;
+        // (bound on the row's nearest distance, its previous label, beta-free lower
+        // bound of the tiles its mask excludes) for the GEMM's screen: (inf, label, inf)
+        // when no finite bound holds, (inf, -1, inf) without a valid previous label
+        float4 rb = make_float4(inf, __int_as_float(-1), inf, 0.0f);
+        if (row < rows) {
+            const int64_t x = pid ? pid[row] : row;
+            const int a = prev_label[x];
+            m = all;
+            need = true;
+            if ((unsigned)a < (unsigned)k) {
+                rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
+                const float4 pi = pinfo[x];  // (previous distance, second-nearest bound, alpha_x, |x^|^2)
+                const float dp = pi.x, sec = pi.y, al = pi.z, hx2 = pi.w;
+                // px + hx2 with px = |x|^2 >= fl(alpha + hx2) (1 - 1e-6) (alpha = |x|^2 - |x^|^2 in FP32)
+                const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
+                const float shx = sqrtf(hx2);
+                const float4 now = cst[a], old = cst_old[a];  // (beta, |c^|^2, |c|^2, |c^|)
+                const float r0 = dp - al - old.x + rho_bound(pxh, shx, old.z, old.y, old.w, kappa);
+                const float r = (sqrtf(fmaxf(r0, 0.0f)) * (1.0f + 1e-6f) + delta[a]) * (1.0f + 1e-6f);
+                const float u = r * r * (1.0f + 1e-6f) + al + now.x + rho_bound(pxh, shx, now.z, now.y, now.w, kappa);
+                const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(now.x)) + 1e-30f;
+                if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(al) < inf) {  // false for NaN too: keep every tile
+                    m = 1ull << (a / tile_cols);  // its own tile
+                    need = false;
+                    // The screen only needs some upper bound: a wider margin costs
+                    // nothing measurable and keeps it far from the rounding terms.
+                    const float us = um + 1e-3f * (fabsf(um) + fabsf(al) + fabsf(now.x));
+                    if (fabsf(us) < inf) rb.x = us;
+                    // second-nearest bound: every centroid other than a, from the
+                    // previous GEMM's sec (free of beta) moved by at most max delta;
+                    // hl bounds d(x, c), hf the beta-free d(x, c) - beta_c
+                    float hl = -inf, hf = -inf;
+                    if (second) {
+                        const float g = sec - al - rho_bound(pxh, shx, gs[5], gs[4], gs[7], kappa) -
+                                        1e-4f * (fabsf(sec) + fabsf(al));
+                        const float sx =
+                            fmaxf(sqrtf(fmaxf(g, 0.0f)) * (1.0f - 1e-6f) - gs[3] * (1.0f + 1e-6f), 0.0f);
+                        const float s2 = sx * sx * (1.0f - 1e-6f);
+                        const float rn = rho_bound(pxh, shx, gs[2], gs[1], gs[6], kappa);
+                        const float lb = s2 + al + gs[0] - rn;
+                        const float l = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(gs[0]));
+                        const float f = s2 + al - rn;
+                        const float lf = f - 1e-4f * (fabsf(f) + fabsf(al));
+                        if (l == l && lf == lf) hl = l, hf = lf;
+                    }
+                    float excl = inf;  // min over the tiles this row excludes of their beta-free lower bounds
+                    if (hl > um) {
+                        excl = hf;  // every other centroid strictly farther: no per-tile test
+                    } else {
+                        const float* dm = dmin + (int64_t)a * tiles;
+                        for (int t = 0; t < tiles; ++t) {
+                            const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
+                            const float gt = fmaxf(dm[t] - r, 0.0f);
+                            const float g2 = gt * gt * (1.0f - 1e-6f);
+                            const float rt = rho_bound(pxh, shx, ts.z, ts.y, tst[tiles + t].z, kappa);
+                            const float lb = g2 + al + ts.x - rt;
+                            const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(ts.x));
+                            if (!(lbm > um) || ts.w != 0.0f) {
+                                m |= 1ull << t;
+                                need = true;
+                            } else {
+                                const float f = g2 + al - rt;
+                                excl = fminf(excl, fmaxf(f - 1e-4f * (fabsf(f) + fabsf(al)), hf));
+                            }
+                        }
+                    }
+                    rb.z = excl;
+                    if (compact && !need)  // the label stands; its distance bounds for next time
+                        *reinterpret_cast<float2*>(pinfo + x) = make_float2(um, excl);
+                }
+            }
         }
+        if (compact && !need) m = 0;
+        if (row_bound && row < rows) row_bound[row] = rb;
+        // union over the 128 rows
+        m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
+            ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
+        const unsigned nb = __ballot_sync(0xffffffffu, need);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m, bits[threadIdx.x >> 5] = nb;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            mask[tile] = part[0] | part[1] | part[2] | part[3];
+            if (compact) {
+                need_bits[tile] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+                tile_count[tile] = __popc(bits[0]) + __popc(bits[1]) + __popc(bits[2]) + __popc(bits[3]);
+                cmask[tile] = 0ull;
+            }
+        }
+        __syncthreads();  // (part and bits are reused by the next tile)
     }
 }
 
@@ -402,13 +511,13 @@ __global__ void __launch_bounds__(kScanSeg) work_scan_kernel(int ntiles, const i
 // Block 0 also writes *work_rows, the number of rows that stay (0 once the loop
 // has stopped, so that the GEMM launches of later iterations do nothing).
 __global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const int* __restrict__ pid,
-                                                           const float2* __restrict__ row_bound,
+                                                           const float4* __restrict__ row_bound,
                                                            const uint4* __restrict__ need_bits,
                                                            const int* __restrict__ offsets,
                                                            const int* __restrict__ counts,
                                                            const int* __restrict__ seg_total, int nseg,
                                                            const uint64_t* __restrict__ mask,
-                                                           int* __restrict__ work_pid, float2* __restrict__ work_rb,
+                                                           int* __restrict__ work_pid, float4* __restrict__ work_rb,
                                                            unsigned long long* __restrict__ cmask,
                                                            int* __restrict__ work_rows, const int* __restrict__ stop) {
     const bool stopped = stop && *stop;
@@ -474,32 +583,32 @@ int launch_centroid_prep(int k, int d, const float* centroids, const float* prev
     return MXK_OK;
 }
 
-int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, float* dmin, float4* tst, const int* stop,
-                          cudaStream_t stream) {
+int launch_centroid_pairs(int k, int d, const float* chat, const float4* cst, const float* delta, float* dmin,
+                          float4* tst, float* bmax32, const int* stop, cudaStream_t stream) {
     MXK_REQUIRE(prune_supported(k, d), "centroid pairs: unsupported shape");
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     LaunchScope scope("centroid_pairs", stream);
     pair_bounds_kernel<<<dim3((unsigned)((k + kPairRows - 1) / kPairRows), (unsigned)tiles), kPairThreads, 0, stream>>>(
-        k, d, tiles, chat, cst, dmin, tst, stop);
+        k, d, tiles, chat, cst, delta, dmin, tst, bmax32, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
 
 int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* cst, float* dmin, float4* tst,
-                                const int* stop, cudaStream_t stream) {
+                                float* bmax32, const int* stop, cudaStream_t stream) {
     MXK_REQUIRE(prune_supported(k, d), "centroid pairs: unsupported shape");
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     LaunchScope scope("centroid_pairs_drift", stream);
     pair_drift_kernel<<<(unsigned)(tiles + (k + kPairThreads - 1) / kPairThreads), kPairThreads, 0, stream>>>(
-        k, tiles, delta, cst, dmin, tst, stop);
+        k, tiles, delta, cst, dmin, tst, bmax32, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
 
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
-                     const float4* cst, const float4* cst_old, const float4* tst, const float* delta,
-                     const float* dmin, uint64_t* mask, float2* row_bound, const int* stop, cudaStream_t stream,
-                     WorkRows* work) {
+                     const float4* cst, const float4* cst_old, const float4* tst, const float4* tst_old,
+                     const float* delta, const float* dmin, uint64_t* mask, float4* row_bound, const int* stop,
+                     cudaStream_t stream, WorkRows* work) {
     if (rows <= 0 && !work) return MXK_OK;
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
@@ -510,8 +619,14 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
     MXK_REQUIRE(blocks < (1ll << 31), "tile mask: too many rows");
     if (blocks > 0) {
         LaunchScope scope("tile_mask", stream);
-        tile_mask_kernel<<<(unsigned)blocks, 128, 0, stream>>>(
-            rows, k, d, tiles, kCentroidTileRows, pid, prev_label, pinfo, cst, cst_old, tst, delta, dmin, mask,
+        // one resident wave of blocks, each looping over point tiles
+        static int per_sm = 0;
+        if (per_sm <= 0) {
+            MXK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tile_mask_kernel, 128, 0));
+            per_sm = std::max(per_sm, 1);
+        }
+        tile_mask_kernel<<<(unsigned)std::min<int64_t>(blocks, (int64_t)sm_count() * per_sm), 128, 0, stream>>>(
+            rows, k, d, tiles, kCentroidTileRows, pid, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
             row_bound, work ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
             work ? reinterpret_cast<uint64_t*>(work->cmask) : nullptr, stop);
         MXK_CUDA(cudaGetLastError());
