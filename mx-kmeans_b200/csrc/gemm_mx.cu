@@ -121,6 +121,8 @@ struct GemmParams {
     float* best_dist;  // optional (argmin): each point's distance to its nearest centroid, at
     int best_dist_stride;  // best_dist[point * best_dist_stride] (and MxArgmin::second_bound's at + 1)
     const float4* row_bound;  // optional (argmin): MxArgmin::row_bound
+    int by_row;               // MxArgmin::by_row
+    int* row_labels;          // MxArgmin::row_labels
     const float* bmax32;      // MxArgmin::beta_max32 (kSec kernels)
     int4* changes;            // optional (argmin, with row_bound): MxArgmin::changes
     int* change_count;
@@ -1140,15 +1142,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                             merge_rowmin<kGaps, kSec>(m, o[w].x, __float_as_int(o[w].y), o[w].z, o[w].w, o[w].z,
                                                       pn);
                         p.labels[point] = m.best;
+                        // the row's position in the visiting order (by_row outputs)
+                        const int64_t at = !p.by_row ? point : p.row_bound ? (int64_t)__float_as_int(rb.w) : grow;
+                        if (p.row_labels) p.row_labels[at] = m.best;
                         if constexpr (kSec) {
                             // keys -> a bound on d - beta_c (less the largest beta), with the
                             // excluded tiles' bound from the row record
                             const float sec = fminf(rb.z, fmaf(-0x1p-18f, pc + fabsf(m.sec), pn + m.sec) - bmax_all);
-                            *reinterpret_cast<float2*>(p.best_dist + point * p.best_dist_stride) =
+                            *reinterpret_cast<float2*>(p.best_dist + at * p.best_dist_stride) =
                                 make_float2(m.first, sec);
                         }
                         else if (p.best_dist)
-                            p.best_dist[point * p.best_dist_stride] = m.first;
+                            p.best_dist[at * p.best_dist_stride] = m.first;
                         if constexpr (kGaps) p.gaps[point] = m.largest - m.next;
                     }
                     if (p.changes) {  // label changes, one counter update per warp
@@ -1248,6 +1253,9 @@ int launch_gemm_mx(int bits, int64_t m, int64_t n, int k, const void* a, const u
         p.best_dist = argmin->best_dist;
         p.best_dist_stride = argmin->best_dist_stride;
         p.row_bound = argmin->row_bound;
+        p.by_row = argmin->by_row;
+        p.row_labels = argmin->row_labels;
+        MXK_REQUIRE(!p.row_labels || p.by_row, "gemm_mx: row labels are indexed by row");
         p.bmax32 = argmin->beta_max32;
         MXK_REQUIRE(!argmin->second_bound ||
                         (p.best_dist && p.bmax32 && !p.gaps && p.best_dist_stride >= 2 &&

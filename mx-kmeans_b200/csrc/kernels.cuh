@@ -64,9 +64,25 @@ int launch_group_compaction(int64_t n, const int* precision, const int* order, i
 // order = point indices 0..n-1 sorted by labels[] (counting sort over k keys;
 // order within a key is unspecified).  scratch: label_sort_scratch_ints(k) ints.
 int64_t label_sort_scratch_ints(int k);
+// Per-row state kept in the visiting order (the pruning pass's records and
+// the rows' labels), moved along when the order is rebuilt: state[g] is the
+// record and label[g] the current label of the point at position g; tmp_* are
+// n-entry scratch.  With it the sort reorders the current visiting order (the
+// order buffer must hold a permutation, e.g. launch_identity_order's) by
+// label[] instead of the points 0..n-1 by labels[]; k <= 16384.
+struct RowState {
+    float4* state = nullptr;
+    int* label = nullptr;
+    float4* tmp_state = nullptr;
+    int* tmp_label = nullptr;
+    int* tmp_order = nullptr;
+};
+// order = 0, 1, ..., n - 1 (the identity order).
+int launch_identity_order(int64_t n, int* order, cudaStream_t stream);
 // stop (optional, device word): non-zero at run time = do nothing.
+// row_state (optional): moved into the new order.
 int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream,
-                      const int* stop = nullptr);
+                      const int* stop = nullptr, const RowState* row_state = nullptr);
 // Rebuild gate for the label sort: ctl = (label changes since the last
 // rebuild, skip word), zero at the start of a run.  Adds *changes (this
 // iteration's label changes) and sets the skip word -- the stop word to pass to
@@ -105,10 +121,16 @@ struct MxArgmin {
     // optional, per GEMM row (the order of pid): (an upper bound on the row's
     // distance to its nearest centroid or inf, the row's previous label as int
     // bits or -1, a lower bound on d(x, c) - beta_c for every centroid c of the
-    // tiles its own mask excludes or +inf, unused).  The epilogue starts each row's
-    // minimum at the bound and always evaluates the chunk holding the previous
-    // label exactly; the result is unchanged.
+    // tiles its own mask excludes or +inf, the row's position in the visiting
+    // order as int bits).  The epilogue starts each row's minimum at the bound
+    // and always evaluates the chunk holding the previous label exactly; the
+    // result is unchanged.
     const float4* row_bound = nullptr;
+    // best_dist (and its second bound) and row_labels (optional: the label
+    // again) are indexed by the row's position in the visiting order -- the GEMM
+    // row, or row_bound's fourth field -- instead of by point
+    bool by_row = false;
+    int* row_labels = nullptr;
     // optional (with row_bound): every row whose label differs from its
     // previous one (row_bound's) is recorded as (point, previous, new, 0) at
     // changes[atomicAdd(change_count, 1)]
@@ -165,8 +187,9 @@ struct WorkRows {
     int* rows = nullptr;           // [1] how many rows stay (0 once the loop has stopped)
 };
 // Per 128-row point tile (rows in pid order), the mask of centroid tiles that
-// may hold a row's nearest centroid, from the previous labels and distances
-// and the current (cst) and previous (cst_old) centroid stats; row_bound
+// may hold a row's nearest centroid, from the rows' previous labels and pinfo
+// records (both per row, in pid order: RowState's label and state) and the
+// current (cst) and previous (cst_old) centroid stats; row_bound
 // (optional, one per row) receives MxArgmin::row_bound's records.  tst_old
 // (optional): the tile stats of the previous iteration's centroids, when that
 // iteration's GEMM wrote its points' second-nearest bounds into pinfo (the

@@ -242,6 +242,11 @@ constexpr int kResortEvery = 2;
 // Pruned fused iterations rebuild the order once n / kResortChangeDiv labels
 // have changed since the last rebuild.
 constexpr int64_t kResortChangeDiv = 32;
+// Pruned iterations from the (kSecondBoundFrom + 1)-th on have their GEMM record
+// the second-nearest bounds: in the first ones the centroids still move too far
+// for those bounds to prove a row (measured at configs[3]: no effect on the
+// third and fourth iterations), and the record costs the GEMM ~10%.
+constexpr int kSecondBoundFrom = 2;
 // Full centroid-pair bound computations: the first kPairsFullFirst pruned
 // iterations, then every kPairsFullEvery-th (drift updates in between).
 constexpr int kPairsFullFirst = 3;
@@ -415,14 +420,22 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     const bool prune = forced8 && n > 0 && prune_supported(k, d);
     const int ctiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *bmax32 = nullptr;
-    // per point: (distance from the last GEMM, its bound on every other centroid's distance, alpha, |x^|^2)
+    // per row of the visiting order (RowState: moved along when the order is
+    // rebuilt): (distance from the last GEMM, its bound on every other
+    // centroid's distance, alpha, |x^|^2) and the row's label
     float4* pinfo = nullptr;
+    RowState rows_state;
     // per-centroid stats [2][k] and per-tile stats [2][2][ctiles], by iteration parity
     float4 *cstats = nullptr, *tstats = nullptr;
     uint64_t* tmask = nullptr;
     float4* rbound = nullptr;  // per row in visiting order: (distance bound, previous label, excluded tiles' bound)
     if (prune) {
         MXK_CHECK(ws.alloc(&pinfo, n));
+        MXK_CHECK(ws.alloc(&rows_state.label, n));
+        MXK_CHECK(ws.alloc(&rows_state.tmp_state, n));
+        MXK_CHECK(ws.alloc(&rows_state.tmp_label, n));
+        MXK_CHECK(ws.alloc(&rows_state.tmp_order, n));
+        rows_state.state = pinfo;
         MXK_CHECK(ws.alloc(&chat, kd));
         MXK_CHECK(ws.alloc(&dmin, (int64_t)k * ctiles));
         MXK_CHECK(ws.alloc(&cdelta, k));
@@ -468,10 +481,12 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     }
 
     // Once per run (kmeans.cu:24-27).
-    if (prune)  // the points' norms and their pruning terms in one pass
+    if (prune) {  // the points' norms and their pruning terms in one pass, in point order (the first visiting order)
         MXK_CHECK(launch_point_norm_stats(n, d, points, pnorm, pinfo, stream));
-    else
+        MXK_CHECK(launch_identity_order(n, order, stream));  // (the sort reorders the visiting order)
+    } else {
         MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
+    }
     if (cache) MXK_CHECK(launch_quantize(8, n, d, points, nullptr, qnat, snat, nullptr, nullptr, stream, 0));
     if (!forced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
@@ -527,11 +542,13 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
                 MXK_CHECK(launch_centroid_pairs(k, d, chat, cst, cdelta, dmin, tst, bmax32, loop, stream));
             else
                 MXK_CHECK(launch_centroid_pairs_drift(k, d, cdelta, cst, dmin, tst, bmax32, loop, stream));
-            // The second-nearest bounds in pinfo come from the previous
-            // iteration's GEMM when that iteration was pruned too (its tile
-            // stats, tst_old, describe the centroids it used).
-            MXK_CHECK(launch_tile_mask(n, k, d, ord, labels, pinfo, cst, cst_old, tst, pruned_its > 0 ? tst_old : nullptr,
-                                       cdelta, dmin, tmask, rbound, loop, stream, compact ? &work : nullptr));
+            // The second-nearest bounds in pinfo are used when the previous
+            // iteration's GEMM recorded them (its tile stats, tst_old, describe
+            // the centroids it used).
+            const bool second_in = pruned_its > kSecondBoundFrom;
+            MXK_CHECK(launch_tile_mask(n, k, d, ord, rows_state.label, pinfo, cst, cst_old, tst,
+                                       second_in ? tst_old : nullptr, cdelta, dmin, tmask, rbound, loop, stream,
+                                       compact ? &work : nullptr));
             ++pruned_its;
         }
         const bool traced = it < trace.max_iterations;
@@ -586,7 +603,10 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.change_count = prune_it ? chg_count : nullptr;
             am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
-            am.second_bound = prune_it;  // (pinfo's second slot)
+            am.by_row = prune;  // (the rows' state follows the visiting order)
+            am.row_labels = prune ? rows_state.label : nullptr;
+            // (pinfo's second slot; pruned_its counts this iteration already)
+            am.second_bound = prune_it && pruned_its > kSecondBoundFrom;
             am.beta_max32 = bmax32;
             MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows, stream,
                                      true, fused_q ? points : nullptr, n));
@@ -651,13 +671,18 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         // at least n / kResortChangeDiv labels have changed since the last sort
         // (decided on the device; the order stays a valid permutation either
         // way).  The last iteration of an incremental run needs no new order.
+        // (With pruning the rows' state follows the order, and the FP32
+        // iterations, which write no row labels, keep the point order.)
         const bool gated = incremental && !cache;
-        if (n > 0 && (gated ? it + 1 < options->max_iterations
-                            : it % kResortEvery == 0 && (!incremental || it + 1 < options->max_iterations))) {
+        const bool may_sort = !(prune && it < options->fp32_iterations);
+        if (n > 0 && may_sort &&
+            (gated ? it + 1 < options->max_iterations
+                   : it % kResortEvery == 0 && (!incremental || it + 1 < options->max_iterations))) {
             if (gated)
                 MXK_CHECK(launch_sort_gate(loop, chg_count, sort_ctl,
                                            (int)std::max<int64_t>(1, n / kResortChangeDiv), stream));
-            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, gated ? sort_ctl + 1 : loop));
+            MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, gated ? sort_ctl + 1 : loop,
+                                        prune ? &rows_state : nullptr));
             cached_stale = true;
             ord = order;
         }

@@ -120,6 +120,51 @@ __global__ void __launch_bounds__(512) label_scatter_block_kernel(int64_t n, int
     }
 }
 
+// The same scatter over the current visiting order when per-row state follows
+// it (RowState): CTA slices of positions g, key = rs.label[g]; the point id
+// order[g], its record and label go to the new position in rs.tmp_*, which
+// row_state_copy_kernel copies back.  Points keep their relative order within
+// a CTA's slice, so records move in short runs.
+__global__ void __launch_bounds__(512) label_scatter_rows_kernel(int64_t n, int k, const int* __restrict__ order,
+                                                                 int* __restrict__ offsets, int64_t per_block,
+                                                                 RowState rs, const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    extern __shared__ int cursor[];
+    const int64_t begin = (int64_t)blockIdx.x * per_block;
+    const int64_t end = begin + per_block < n ? begin + per_block : n;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) cursor[i] = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    for (int64_t b = begin; b < end; b += blockDim.x) {
+        const int64_t g = b + threadIdx.x;
+        const int key = g < end ? clamp_key(rs.label[g], k) : -1;
+        const unsigned peers = __match_any_sync(kFull, key);
+        if (key >= 0 && lane == __ffs(peers) - 1) atomicAdd(&cursor[key], __popc(peers));
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const int c = cursor[i];
+        cursor[i] = c ? atomicAdd(&offsets[i], c) : 0;
+    }
+    __syncthreads();
+    for (int64_t b = begin; b < end; b += blockDim.x) {
+        const int64_t g = b + threadIdx.x;
+        const int label = g < end ? rs.label[g] : -1;
+        const int key = g < end ? clamp_key(label, k) : -1;
+        const unsigned peers = __match_any_sync(kFull, key);
+        const int leader = __ffs(peers) - 1;
+        int pos = 0;
+        if (key >= 0 && lane == leader) pos = atomicAdd(&cursor[key], __popc(peers));
+        pos = __shfl_sync(kFull, pos, leader);
+        if (key >= 0) {
+            const int dst = pos + __popc(peers & ((1u << lane) - 1u));
+            rs.tmp_order[dst] = order[g];
+            rs.tmp_state[dst] = rs.state[g];
+            rs.tmp_label[dst] = label;
+        }
+    }
+}
+
 // order[offset[key]++] = p, one atomic per group of equal keys within a warp
 // (used when k is too large for the shared-memory cursors).
 __global__ void __launch_bounds__(512) label_scatter_kernel(int64_t n, int k, const int* __restrict__ labels,
@@ -138,6 +183,22 @@ __global__ void __launch_bounds__(512) label_scatter_kernel(int64_t n, int k, co
         pos = __shfl_sync(kFull, pos, leader);
         if (valid) order[pos + __popc(peers & ((1u << lane) - 1u))] = (int)p;
     }
+}
+
+// The new order, records and labels copied back from RowState's scratch.
+__global__ void __launch_bounds__(256) row_state_copy_kernel(int64_t n, RowState rs, int* __restrict__ order,
+                                                             const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (int64_t)gridDim.x * blockDim.x) {
+        order[g] = rs.tmp_order[g];
+        rs.state[g] = rs.tmp_state[g];
+        rs.label[g] = rs.tmp_label[g];
+    }
+}
+
+__global__ void __launch_bounds__(256) iota_kernel(int64_t n, int* __restrict__ v) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        v[i] = (int)i;
 }
 
 // ctl = (label changes since the visiting order was last rebuilt, skip word).
@@ -170,10 +231,21 @@ int launch_sort_gate(const int* stop, const int* changes, int* ctl, int threshol
 
 int64_t label_sort_scratch_ints(int k) { return k; }
 
+int launch_identity_order(int64_t n, int* order, cudaStream_t stream) {
+    if (n <= 0) return MXK_OK;
+    LaunchScope scope("identity_order", stream);
+    iota_kernel<<<sm_count() * 4, 256, 0, stream>>>(n, order);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
 int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scratch, cudaStream_t stream,
-                      const int* stop) {
+                      const int* stop, const RowState* row_state) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(k > 0 && labels && order && scratch, "label_sort: bad arguments");
+    const RowState rs = row_state ? *row_state : RowState{};
+    MXK_REQUIRE(!row_state || (rs.state && rs.label && rs.tmp_state && rs.tmp_label && rs.tmp_order && k <= kSmemBins),
+                "label_sort: incomplete row state, or k above the shared-memory cursors");
     MXK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int) * (size_t)k, stream));
     const int sms = sm_count();
     const size_t smem = k <= kSmemBins ? sizeof(int) * (size_t)k : 0;
@@ -189,7 +261,22 @@ int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scra
         label_scan_kernel<<<1, 1024, 0, stream>>>(k, scratch, stop);
         MXK_CUDA(cudaGetLastError());
     }
-    if (k <= kSmemBins) {
+    if (row_state) {
+        const int64_t blocks = std::min<int64_t>((int64_t)sms * 2, (n + 4095) / 4096);
+        const int64_t per_block = (n + blocks - 1) / blocks;
+        if (smem > 48 * 1024)
+            MXK_CUDA(cudaFuncSetAttribute(label_scatter_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        {
+            LaunchScope scope("label_scatter", stream);
+            label_scatter_rows_kernel<<<(unsigned)blocks, 512, smem, stream>>>(n, k, order, scratch, per_block, rs,
+                                                                               stop);
+            MXK_CUDA(cudaGetLastError());
+        }
+        LaunchScope scope("row_state_copy", stream);
+        row_state_copy_kernel<<<sms * 8, 256, 0, stream>>>(n, rs, order, stop);
+        MXK_CUDA(cudaGetLastError());
+    } else if (k <= kSmemBins) {
         const int64_t blocks = std::min<int64_t>((int64_t)sms * 2, (n + 4095) / 4096);
         const int64_t per_block = (n + blocks - 1) / blocks;
         if (smem > 48 * 1024)

@@ -329,9 +329,10 @@ __device__ __forceinline__ float rho_bound(float pxh, float shx, float pc, float
 // for the compacted masks of work_scatter_kernel.  tst / tst_old: 2 x tiles
 // stats of the current and (optional) previous centroids; without tst_old or
 // with a non-finite centroid the second-nearest bounds are not used.  Blocks
-// loop over point tiles (blockIdx.x, + gridDim.x, ...).
+// loop over point tiles (blockIdx.x, + gridDim.x, ...).  prev_label and pinfo
+// are per row, in the visiting order.
 __global__ void __launch_bounds__(128) tile_mask_kernel(
-    int64_t rows, int k, int d, int tiles, int tile_cols, const int* __restrict__ pid,
+    int64_t rows, int k, int d, int tiles, int tile_cols,
     const int* __restrict__ prev_label, float4* __restrict__ pinfo, const float4* __restrict__ cst,
     const float4* __restrict__ cst_old, const float4* __restrict__ tst, const float4* __restrict__ tst_old,
     const float* __restrict__ delta, const float* __restrict__ dmin, uint64_t* __restrict__ mask,
@@ -381,17 +382,17 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
         uint64_t m = 0;
         bool need = false;
         // (bound on the row's nearest distance, its previous label, beta-free lower
-        // bound of the tiles its mask excludes) for the GEMM's screen: (inf, label, inf)
-        // when no finite bound holds, (inf, -1, inf) without a valid previous label
-        float4 rb = make_float4(inf, __int_as_float(-1), inf, 0.0f);
+        // bound of the tiles its mask excludes, the row's position as int bits) for
+        // the GEMM's screen: (inf, label, inf, row) when no finite bound holds,
+        // (inf, -1, inf, row) without a valid previous label
+        float4 rb = make_float4(inf, __int_as_float(-1), inf, __int_as_float((int)row));
         if (row < rows) {
-            const int64_t x = pid ? pid[row] : row;
-            const int a = prev_label[x];
+            const int a = prev_label[row];
             m = all;
             need = true;
             if ((unsigned)a < (unsigned)k) {
                 rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
-                const float4 pi = pinfo[x];  // (previous distance, second-nearest bound, alpha_x, |x^|^2)
+                const float4 pi = pinfo[row];  // (previous distance, second-nearest bound, alpha_x, |x^|^2)
                 const float dp = pi.x, sec = pi.y, al = pi.z, hx2 = pi.w;
                 // px + hx2 with px = |x|^2 >= fl(alpha + hx2) (1 - 1e-6) (alpha = |x|^2 - |x^|^2 in FP32)
                 const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
@@ -430,7 +431,8 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
                         excl = hf;  // every other centroid strictly farther: no per-tile test
                     } else {
                         const float* dm = dmin + (int64_t)a * tiles;
-                        for (int t = 0; t < tiles; ++t) {
+#pragma unroll 8
+                        for (int t = 0; t < tiles; ++t) {  // (unrolled: the tiles' loads issue together)
                             const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
                             const float gt = fmaxf(dm[t] - r, 0.0f);
                             const float g2 = gt * gt * (1.0f - 1e-6f);
@@ -448,7 +450,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
                     }
                     rb.z = excl;
                     if (compact && !need)  // the label stands; its distance bounds for next time
-                        *reinterpret_cast<float2*>(pinfo + x) = make_float2(um, excl);
+                        *reinterpret_cast<float2*>(pinfo + row) = make_float2(um, excl);
                 }
             }
         }
@@ -626,7 +628,7 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
             per_sm = std::max(per_sm, 1);
         }
         tile_mask_kernel<<<(unsigned)std::min<int64_t>(blocks, (int64_t)sm_count() * per_sm), 128, 0, stream>>>(
-            rows, k, d, tiles, kCentroidTileRows, pid, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
+            rows, k, d, tiles, kCentroidTileRows, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
             row_bound, work ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
             work ? reinterpret_cast<uint64_t*>(work->cmask) : nullptr, stop);
         MXK_CUDA(cudaGetLastError());
