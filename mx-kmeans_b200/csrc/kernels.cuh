@@ -31,7 +31,7 @@ inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileR
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
 // launch_l2_norm's norms (bit-identical) and, per point, the pruning pass's
 // pinfo = (+inf and 0: the slots the GEMM writes the point's distance and its
-// second-nearest bound into, |x|^2 - |x^|^2, |x^|^2) for its MXFP8 round trip
+// second-nearest bound into, |x|^2 - |x^|^2, |x^|) for its MXFP8 round trip
 // x^, in one pass over the points.  d % 128 == 0, points 16-byte aligned.
 int launch_point_norm_stats(int64_t n, int d, const float* points, float* norms, float4* pinfo,
                             cudaStream_t stream);

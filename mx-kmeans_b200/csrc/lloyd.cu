@@ -422,7 +422,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *bmax32 = nullptr;
     // per row of the visiting order (RowState: moved along when the order is
     // rebuilt): (distance from the last GEMM, its bound on every other
-    // centroid's distance, alpha, |x^|^2) and the row's label
+    // centroid's distance, alpha, |x^|) and the row's label
     float4* pinfo = nullptr;
     RowState rows_state;
     // per-centroid stats [2][k] and per-tile stats [2][2][ctiles], by iteration parity

@@ -318,21 +318,125 @@ __device__ __forceinline__ float rho_bound(float pxh, float shx, float pc, float
     return kappa * (pxh + pc + hc2 + 2.0f * shx * shc);
 }
 
-// One block per 128-row point tile: the union over its rows of the centroid
-// tiles the bounds cannot exclude.  With `compact` (the fused path's row
-// compaction) a row whose every other centroid -- its own tile's included,
-// through dmin[a][own], which leaves a out -- lies strictly beyond its upper
-// bound keeps its label: it is left out of the GEMM (need_bits, counts), its
-// distance for the next iteration's bounds becomes that upper bound and its
-// second-nearest bound the smallest lower bound of its tiles, and the tile's
-// mask is the union over the rows that remain; cmask[blockIdx.x] is zeroed
-// for the compacted masks of work_scatter_kernel.  tst / tst_old: 2 x tiles
-// stats of the current and (optional) previous centroids; without tst_old or
-// with a non-finite centroid the second-nearest bounds are not used.  Blocks
-// loop over point tiles (blockIdx.x, + gridDim.x, ...).  prev_label and pinfo
-// are per row, in the visiting order.
+// Square root by the hardware approximation (PTX sqrt.approx.f32, relative
+// error a few units of 2^-23); every use below widens it by 4e-6, outward.
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Whole-centroid-set terms of the second-nearest test, gathered from the tile
+// stats: min beta, max |c^|^2, max |c|^2, max delta of the current centroids,
+// max |c^|^2 and max |c|^2 of the previous ones, and the roots of the two
+// max |c^|^2.
+struct SetTerms {
+    float bmin, hc2, pc, dmax, hc2_old, pc_old, shc, shc_old;
+};
+
+// One row of tile_mask_kernel: its centroid-tile mask m, whether it must stay
+// in the GEMM (need), its GEMM record rb, and (compact, proven rows) its pinfo
+// bounds for the next iteration.
+__device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, int tiles, uint64_t all, float kappa,
+                                              bool second, const SetTerms& gs, const int* __restrict__ prev_label,
+                                              float4* __restrict__ pinfo, const float4* __restrict__ cst,
+                                              const float4* __restrict__ cst_old, const float4* __restrict__ tst,
+                                              const float* __restrict__ delta, const float* __restrict__ dmin,
+                                              float4* __restrict__ row_bound, int compact, uint64_t& m, bool& need) {
+    const float inf = __int_as_float(0x7f800000);
+    m = 0;
+    need = false;
+    if (row >= rows) return;
+    // (bound on the row's nearest distance, its previous label, beta-free lower
+    // bound of the tiles its mask excludes, the row's position as int bits) for
+    // the GEMM's screen: (inf, label, inf, row) when no finite bound holds,
+    // (inf, -1, inf, row) without a valid previous label
+    float4 rb = make_float4(inf, __int_as_float(-1), inf, __int_as_float((int)row));
+    const int a = prev_label[row];
+    m = all;
+    need = true;
+    if ((unsigned)a < (unsigned)k) {
+        rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
+        const float4 pi = pinfo[row];  // (previous distance, second-nearest bound, alpha_x, |x^|)
+        const float dp = pi.x, sec = pi.y, al = pi.z, shx = pi.w;
+        const float hx2 = shx * shx * (1.0f + 1e-6f);  // >= |x^|^2
+        // px + hx2 with px = |x|^2 <= fl(alpha + hx2) (1 + 1e-6) (alpha = |x|^2 - |x^|^2 in FP32)
+        const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
+        const float4 now = cst[a], old = cst_old[a];  // (beta, |c^|^2, |c|^2, |c^|)
+        const float r0 = dp - al - old.x + rho_bound(pxh, shx, old.z, old.y, old.w, kappa);
+        const float r = (sqrt_approx(fmaxf(r0, 0.0f)) * (1.0f + 4e-6f) + delta[a]) * (1.0f + 1e-6f);
+        const float u = r * r * (1.0f + 1e-6f) + al + now.x + rho_bound(pxh, shx, now.z, now.y, now.w, kappa);
+        const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(now.x)) + 1e-30f;
+        if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(al) < inf) {  // false for NaN too: keep every tile
+            m = 1ull << (a / kCentroidTileRows);  // its own tile
+            need = false;
+            // The screen only needs some upper bound: a wider margin costs
+            // nothing measurable and keeps it far from the rounding terms.
+            const float us = um + 1e-3f * (fabsf(um) + fabsf(al) + fabsf(now.x));
+            if (fabsf(us) < inf) rb.x = us;
+            // second-nearest bound: every centroid other than a, from the
+            // previous GEMM's sec (free of beta) moved by at most max delta;
+            // hl bounds d(x, c), hf the beta-free d(x, c) - beta_c
+            float hl = -inf, hf = -inf;
+            if (second) {
+                const float g = sec - al - rho_bound(pxh, shx, gs.pc_old, gs.hc2_old, gs.shc_old, kappa) -
+                                1e-4f * (fabsf(sec) + fabsf(al));
+                const float sx =
+                    fmaxf(sqrt_approx(fmaxf(g, 0.0f)) * (1.0f - 4e-6f) - gs.dmax * (1.0f + 1e-6f), 0.0f);
+                const float s2 = sx * sx * (1.0f - 1e-6f);
+                const float rn = rho_bound(pxh, shx, gs.pc, gs.hc2, gs.shc, kappa);
+                const float lb = s2 + al + gs.bmin - rn;
+                const float l = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(gs.bmin));
+                const float f = s2 + al - rn;
+                const float lf = f - 1e-4f * (fabsf(f) + fabsf(al));
+                if (l == l && lf == lf) hl = l, hf = lf;
+            }
+            float excl = inf;  // min over the tiles this row excludes of their beta-free lower bounds
+            if (hl > um) {
+                excl = hf;  // every other centroid strictly farther: no per-tile test
+            } else {
+                const float* dm = dmin + (int64_t)a * tiles;
+#pragma unroll 8
+                for (int t = 0; t < tiles; ++t) {  // (unrolled: the tiles' loads issue together)
+                    const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
+                    const float gt = fmaxf(dm[t] - r, 0.0f);
+                    const float g2 = gt * gt * (1.0f - 1e-6f);
+                    const float rt = rho_bound(pxh, shx, ts.z, ts.y, tst[tiles + t].z, kappa);
+                    const float lb = g2 + al + ts.x - rt;
+                    const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(ts.x));
+                    if (!(lbm > um) || ts.w != 0.0f) {
+                        m |= 1ull << t;
+                        need = true;
+                    } else {
+                        const float f = g2 + al - rt;
+                        excl = fminf(excl, fmaxf(f - 1e-4f * (fabsf(f) + fabsf(al)), hf));
+                    }
+                }
+            }
+            rb.z = excl;
+            if (compact && !need)  // the label stands; its distance bounds for next time
+                *reinterpret_cast<float2*>(pinfo + row) = make_float2(um, excl);
+        }
+    }
+    if (compact && !need) m = 0;
+    if (row_bound) row_bound[row] = rb;
+}
+
+// Per 128-row point tile (one warp; lane l takes rows l, l + 32, l + 64 and
+// l + 96): the union over its rows of the centroid tiles the bounds cannot
+// exclude.  With `compact` (the fused path's row compaction) a row whose every
+// other centroid -- its own tile's included, through dmin[a][own], which
+// leaves a out -- lies strictly beyond its upper bound keeps its label: it is
+// left out of the GEMM (need_bits, counts), its distance for the next
+// iteration's bounds becomes that upper bound and its second-nearest bound the
+// smallest lower bound of its tiles, and the tile's mask is the union over the
+// rows that remain; cmask[tile] is zeroed for the compacted masks of
+// work_scatter_kernel.  tst / tst_old: 2 x tiles stats of the current and
+// (optional) previous centroids; without tst_old or with a non-finite centroid
+// the second-nearest bounds are not used.  prev_label and pinfo are per row,
+// in the visiting order.  Warps loop over point tiles.
 __global__ void __launch_bounds__(128) tile_mask_kernel(
-    int64_t rows, int k, int d, int tiles, int tile_cols,
+    int64_t rows, int k, int d, int tiles,
     const int* __restrict__ prev_label, float4* __restrict__ pinfo, const float4* __restrict__ cst,
     const float4* __restrict__ cst_old, const float4* __restrict__ tst, const float4* __restrict__ tst_old,
     const float* __restrict__ delta, const float* __restrict__ dmin, uint64_t* __restrict__ mask,
@@ -340,9 +444,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     uint64_t* __restrict__ cmask, const int* __restrict__ stop) {
     if (stop && *stop) return;
     const float inf = __int_as_float(0x7f800000);
-    // Whole-centroid-set terms of the second-nearest test (gs, below); usable
-    // when every tile is finite.
-    __shared__ float gs[8];
+    __shared__ SetTerms gs_s;
     __shared__ int g_ok;
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
@@ -364,113 +466,40 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
             bad = fmaxf(bad, __shfl_xor_sync(0xffffffffu, bad, o));
         }
         if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < 6; ++i) gs[i] = v[i];
-            gs[6] = sqrtf(v[1]), gs[7] = sqrtf(v[4]);  // roots of the max |c^|^2, current and previous
+            gs_s = SetTerms{v[0], v[1], v[2], v[3], v[4], v[5], sqrtf(v[1]), sqrtf(v[4])};
             g_ok = bad == 0.0f;
         }
     }
     __syncthreads();
+    const SetTerms gs = gs_s;
     const bool second = g_ok != 0;
     const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
     const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
     const int64_t ntiles = (rows + 127) / 128;
-    __shared__ uint64_t part[4];
-    __shared__ unsigned bits[4];
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int64_t row = tile * 128 + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    for (int64_t tile = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); tile < ntiles; tile += (int64_t)gridDim.x * 4) {
         uint64_t m = 0;
-        bool need = false;
-        // (bound on the row's nearest distance, its previous label, beta-free lower
-        // bound of the tiles its mask excludes, the row's position as int bits) for
-        // the GEMM's screen: (inf, label, inf, row) when no finite bound holds,
-        // (inf, -1, inf, row) without a valid previous label
-        float4 rb = make_float4(inf, __int_as_float(-1), inf, __int_as_float((int)row));
-        if (row < rows) {
-            const int a = prev_label[row];
-            m = all;
-            need = true;
-            if ((unsigned)a < (unsigned)k) {
-                rb.y = __int_as_float(a);  // the previous label, with or without a finite bound
-                const float4 pi = pinfo[row];  // (previous distance, second-nearest bound, alpha_x, |x^|^2)
-                const float dp = pi.x, sec = pi.y, al = pi.z, hx2 = pi.w;
-                // px + hx2 with px = |x|^2 >= fl(alpha + hx2) (1 - 1e-6) (alpha = |x|^2 - |x^|^2 in FP32)
-                const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
-                const float shx = sqrtf(hx2);
-                const float4 now = cst[a], old = cst_old[a];  // (beta, |c^|^2, |c|^2, |c^|)
-                const float r0 = dp - al - old.x + rho_bound(pxh, shx, old.z, old.y, old.w, kappa);
-                const float r = (sqrtf(fmaxf(r0, 0.0f)) * (1.0f + 1e-6f) + delta[a]) * (1.0f + 1e-6f);
-                const float u = r * r * (1.0f + 1e-6f) + al + now.x + rho_bound(pxh, shx, now.z, now.y, now.w, kappa);
-                const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(now.x)) + 1e-30f;
-                if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(al) < inf) {  // false for NaN too: keep every tile
-                    m = 1ull << (a / tile_cols);  // its own tile
-                    need = false;
-                    // The screen only needs some upper bound: a wider margin costs
-                    // nothing measurable and keeps it far from the rounding terms.
-                    const float us = um + 1e-3f * (fabsf(um) + fabsf(al) + fabsf(now.x));
-                    if (fabsf(us) < inf) rb.x = us;
-                    // second-nearest bound: every centroid other than a, from the
-                    // previous GEMM's sec (free of beta) moved by at most max delta;
-                    // hl bounds d(x, c), hf the beta-free d(x, c) - beta_c
-                    float hl = -inf, hf = -inf;
-                    if (second) {
-                        const float g = sec - al - rho_bound(pxh, shx, gs[5], gs[4], gs[7], kappa) -
-                                        1e-4f * (fabsf(sec) + fabsf(al));
-                        const float sx =
-                            fmaxf(sqrtf(fmaxf(g, 0.0f)) * (1.0f - 1e-6f) - gs[3] * (1.0f + 1e-6f), 0.0f);
-                        const float s2 = sx * sx * (1.0f - 1e-6f);
-                        const float rn = rho_bound(pxh, shx, gs[2], gs[1], gs[6], kappa);
-                        const float lb = s2 + al + gs[0] - rn;
-                        const float l = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(gs[0]));
-                        const float f = s2 + al - rn;
-                        const float lf = f - 1e-4f * (fabsf(f) + fabsf(al));
-                        if (l == l && lf == lf) hl = l, hf = lf;
-                    }
-                    float excl = inf;  // min over the tiles this row excludes of their beta-free lower bounds
-                    if (hl > um) {
-                        excl = hf;  // every other centroid strictly farther: no per-tile test
-                    } else {
-                        const float* dm = dmin + (int64_t)a * tiles;
-#pragma unroll 8
-                        for (int t = 0; t < tiles; ++t) {  // (unrolled: the tiles' loads issue together)
-                            const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
-                            const float gt = fmaxf(dm[t] - r, 0.0f);
-                            const float g2 = gt * gt * (1.0f - 1e-6f);
-                            const float rt = rho_bound(pxh, shx, ts.z, ts.y, tst[tiles + t].z, kappa);
-                            const float lb = g2 + al + ts.x - rt;
-                            const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(ts.x));
-                            if (!(lbm > um) || ts.w != 0.0f) {
-                                m |= 1ull << t;
-                                need = true;
-                            } else {
-                                const float f = g2 + al - rt;
-                                excl = fminf(excl, fmaxf(f - 1e-4f * (fabsf(f) + fabsf(al)), hf));
-                            }
-                        }
-                    }
-                    rb.z = excl;
-                    if (compact && !need)  // the label stands; its distance bounds for next time
-                        *reinterpret_cast<float2*>(pinfo + row) = make_float2(um, excl);
-                }
-            }
+        unsigned nb[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint64_t mr;
+            bool need;
+            row_tile_mask(tile * 128 + q * 32 + lane, rows, k, tiles, all, kappa, second, gs, prev_label, pinfo, cst,
+                          cst_old, tst, delta, dmin, row_bound, compact, mr, need);
+            m |= mr;
+            nb[q] = __ballot_sync(0xffffffffu, need);
         }
-        if (compact && !need) m = 0;
-        if (row_bound && row < rows) row_bound[row] = rb;
         // union over the 128 rows
         m = __reduce_or_sync(0xffffffffu, (unsigned)m) |
             ((uint64_t)__reduce_or_sync(0xffffffffu, (unsigned)(m >> 32)) << 32);
-        const unsigned nb = __ballot_sync(0xffffffffu, need);
-        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m, bits[threadIdx.x >> 5] = nb;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            mask[tile] = part[0] | part[1] | part[2] | part[3];
+        if (lane == 0) {
+            mask[tile] = m;
             if (compact) {
-                need_bits[tile] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
-                tile_count[tile] = __popc(bits[0]) + __popc(bits[1]) + __popc(bits[2]) + __popc(bits[3]);
+                need_bits[tile] = make_uint4(nb[0], nb[1], nb[2], nb[3]);
+                tile_count[tile] = __popc(nb[0]) + __popc(nb[1]) + __popc(nb[2]) + __popc(nb[3]);
                 cmask[tile] = 0ull;
             }
         }
-        __syncthreads();  // (part and bits are reused by the next tile)
     }
 }
 
@@ -621,14 +650,15 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
     MXK_REQUIRE(blocks < (1ll << 31), "tile mask: too many rows");
     if (blocks > 0) {
         LaunchScope scope("tile_mask", stream);
-        // one resident wave of blocks, each looping over point tiles
+        // one resident wave of blocks (four point tiles at a time), looping over the point tiles
         static int per_sm = 0;
         if (per_sm <= 0) {
             MXK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tile_mask_kernel, 128, 0));
             per_sm = std::max(per_sm, 1);
         }
-        tile_mask_kernel<<<(unsigned)std::min<int64_t>(blocks, (int64_t)sm_count() * per_sm), 128, 0, stream>>>(
-            rows, k, d, tiles, kCentroidTileRows, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
+        tile_mask_kernel<<<(unsigned)std::min<int64_t>((blocks + 3) / 4, (int64_t)sm_count() * per_sm), 128, 0,
+                           stream>>>(
+            rows, k, d, tiles, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
             row_bound, work ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
             work ? reinterpret_cast<uint64_t*>(work->cmask) : nullptr, stop);
         MXK_CUDA(cudaGetLastError());

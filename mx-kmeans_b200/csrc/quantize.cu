@@ -176,8 +176,8 @@ __global__ void __launch_bounds__(256) l2_norm_kernel(int64_t rows, int d, const
 // (16-byte stores and loads both conflict-free), then each lane walks its own
 // row in feature order.  kStats also produces, per row, the pruning pass's
 // MXFP8 terms in pinfo: (+inf and 0: the slots the GEMM writes the row's
-// distance and second-nearest bound into, |x|^2 - |x^|^2, |x^|^2) for the
-// row's MXFP8 round trip x^
+// distance and second-nearest bound into, |x|^2 - |x^|^2, |x^|) for the row's
+// MXFP8 round trip x^
 // (UE8M0 scale of each 32-feature block, E4M3 round-to-nearest-even,
 // saturating, as quantize_rows).
 constexpr int kNormPitch = 132;  // floats per staged row
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(64) norm_rows_staged_kernel(int64_t rows, int 
     const int64_t my = row0 + lane;
     if (my < rows) {
         norms[my] = sum;
-        if constexpr (kStats) pinfo[my] = make_float4(__int_as_float(0x7f800000), 0.0f, sum - h, h);
+        if constexpr (kStats) pinfo[my] = make_float4(__int_as_float(0x7f800000), 0.0f, sum - h, sqrtf(h));
     }
 }
 
