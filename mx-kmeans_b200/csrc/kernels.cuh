@@ -199,10 +199,19 @@ struct WorkRows {
 // its second-nearest bound the lower one); the other rows are compacted into
 // work (ids, records, masks of the compacted tiles, count), for a GEMM launched
 // on work->pid with rows_dev = work->rows.
+// fresh: pinfo's distances already bound the distance to the rows' current
+// centroids (launch_row_distance_bound), so no centroid move is added.
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float4* tst_old,
                      const float* delta, const float* dmin, uint64_t* mask, float4* row_bound, const int* stop,
-                     cudaStream_t stream, WorkRows* work = nullptr);
+                     cudaStream_t stream, WorkRows* work = nullptr, bool fresh = false);
+// Per row (in pid order, labels and pinfo per row as launch_tile_mask reads
+// them): pinfo.x = an upper bound on the row's distance to its label's current
+// centroid, from the point's row (MXFP8 round trip) and chat[label] -- one
+// pass over the points, for an iteration whose centroids moved far.
+int launch_row_distance_bound(int64_t rows, int k, int d, const int* pid, const int* label, float4* pinfo,
+                              const float* chat, const float4* cst, const float* points, const int* stop,
+                              cudaStream_t stream);
 
 // ---- fp32.cu -----------------------------------------------------------------
 int launch_gemm_fp32(int64_t m, int64_t n, int k, const float* a, const float* b, float* out,

@@ -546,9 +546,17 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             // iteration's GEMM recorded them (its tile stats, tst_old, describe
             // the centroids it used).
             const bool second_in = pruned_its > kSecondBoundFrom;
+            // In the first pruned iteration the centroids have just moved far
+            // from their initial rows (up to 30 at configs[3]), so the moved
+            // bound sqrt(d_prev) + delta proves little; one pass over the points
+            // gives every row its distance bound to its current centroid.
+            const bool fresh = pruned_its == 0;
+            if (fresh)
+                MXK_CHECK(launch_row_distance_bound(n, k, d, ord, rows_state.label, pinfo, chat, cst, points, loop,
+                                                    stream));
             MXK_CHECK(launch_tile_mask(n, k, d, ord, rows_state.label, pinfo, cst, cst_old, tst,
                                        second_in ? tst_old : nullptr, cdelta, dmin, tmask, rbound, loop, stream,
-                                       compact ? &work : nullptr));
+                                       compact ? &work : nullptr, fresh));
             ++pruned_its;
         }
         const bool traced = it < trace.max_iterations;

@@ -26,6 +26,7 @@ namespace mxk {
 int fail(int status, const std::string& message);
 void comm_attach_group_flag(void* comm, std::atomic<int>* flag);
 void comm_abort(void* comm);
+cudaMemPool_t workspace_pool();
 }
 
 namespace {
@@ -58,10 +59,15 @@ struct Shard {
         if (cudaSetDevice(device) != cudaSuccess) return;
         if (comm && status != MXK_OK) mxk::comm_abort(comm);  // a failed rank's communicator is not destroyed in order
         if (comm) mxk_comm_destroy(comm);
-        if (points) cudaFree(points);
-        if (centroids) cudaFree(centroids);
-        if (labels) cudaFree(labels);
-        if (stream) cudaStreamDestroy(stream);
+        // (stream-ordered frees into the library's pool, which keeps the blocks
+        // mapped for the next call)
+        if (points) cudaFreeAsync(points, stream);
+        if (centroids) cudaFreeAsync(centroids, stream);
+        if (labels) cudaFreeAsync(labels, stream);
+        if (stream) {
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+        }
         comm = nullptr;
         points = centroids = nullptr;
         labels = nullptr;
@@ -104,14 +110,28 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
         s.rows = n / G + (g < n % G ? 1 : 0);
     }
 
-    // Phase 1: allocate and upload the shard and the initial centroids.
+    // Phase 1: allocate (from the library's stream-ordered pool on each device,
+    // whose blocks stay mapped between calls) and upload the shard and the
+    // initial centroids.
     on_every_gpu(shards, [&](Shard& s) {
         const size_t rows = size_t(std::max<int64_t>(s.rows, 1));
         if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice") ||
-            !s.record_cuda(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
-            !s.record_cuda(cudaMalloc(&s.points, sizeof(float) * rows * size_t(d)), "cudaMalloc") ||
-            !s.record_cuda(cudaMalloc(&s.centroids, centroid_bytes), "cudaMalloc") ||
-            !s.record_cuda(cudaMalloc(&s.labels, sizeof(int) * rows), "cudaMalloc"))
+            !s.record_cuda(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "cudaStreamCreate"))
+            return;
+        cudaMemPool_t pool = mxk::workspace_pool();
+        if (!pool) {
+            s.record_cuda(cudaErrorMemoryAllocation, "workspace pool");
+            return;
+        }
+        if (!s.record_cuda(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&s.points),
+                                                   sizeof(float) * rows * size_t(d), pool, s.stream),
+                           "cudaMallocFromPoolAsync") ||
+            !s.record_cuda(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&s.centroids), centroid_bytes, pool,
+                                                   s.stream),
+                           "cudaMallocFromPoolAsync") ||
+            !s.record_cuda(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&s.labels), sizeof(int) * rows, pool,
+                                                   s.stream),
+                           "cudaMallocFromPoolAsync"))
             return;
         if (!s.record_cuda(cudaMemcpyAsync(s.points, points + size_t(s.row0) * size_t(d),
                                            sizeof(float) * size_t(s.rows) * size_t(d), cudaMemcpyHostToDevice,

@@ -338,7 +338,8 @@ struct SetTerms {
 // in the GEMM (need), its GEMM record rb, and (compact, proven rows) its pinfo
 // bounds for the next iteration.
 __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, int tiles, uint64_t all, float kappa,
-                                              bool second, const SetTerms& gs, const int* __restrict__ prev_label,
+                                              bool second, bool fresh, const SetTerms& gs,
+                                              const int* __restrict__ prev_label,
                                               float4* __restrict__ pinfo, const float4* __restrict__ cst,
                                               const float4* __restrict__ cst_old, const float4* __restrict__ tst,
                                               const float* __restrict__ delta, const float* __restrict__ dmin,
@@ -362,9 +363,11 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
         const float hx2 = shx * shx * (1.0f + 1e-6f);  // >= |x^|^2
         // px + hx2 with px = |x|^2 <= fl(alpha + hx2) (1 + 1e-6) (alpha = |x|^2 - |x^|^2 in FP32)
         const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
-        const float4 now = cst[a], old = cst_old[a];  // (beta, |c^|^2, |c|^2, |c^|)
+        // (fresh: dp bounds the distance to the current centroid, which has
+        // not moved since)
+        const float4 now = cst[a], old = fresh ? now : cst_old[a];  // (beta, |c^|^2, |c|^2, |c^|)
         const float r0 = dp - al - old.x + rho_bound(pxh, shx, old.z, old.y, old.w, kappa);
-        const float r = (sqrt_approx(fmaxf(r0, 0.0f)) * (1.0f + 4e-6f) + delta[a]) * (1.0f + 1e-6f);
+        const float r = (sqrt_approx(fmaxf(r0, 0.0f)) * (1.0f + 4e-6f) + (fresh ? 0.0f : delta[a])) * (1.0f + 1e-6f);
         const float u = r * r * (1.0f + 1e-6f) + al + now.x + rho_bound(pxh, shx, now.z, now.y, now.w, kappa);
         const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(now.x)) + 1e-30f;
         if (fabsf(um) < inf && fabsf(r0) < inf && fabsf(al) < inf) {  // false for NaN too: keep every tile
@@ -422,6 +425,85 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
     if (row_bound) row_bound[row] = rb;
 }
 
+// Each row's distance bound against its label's current centroid, from the
+// rows themselves: |x^ - c^_a|^2 summed in FP32 over the MXFP8 round trip x^
+// of the point's row (quantize_rows' arithmetic: UE8M0 scale of each 32-feature
+// block, E4M3 round to nearest even) and the dequantized centroid chat[a], plus
+// the rounding of that sum, alpha_x + beta_a and rho, written into pinfo[g].x
+// (+inf for a row without a valid label).  A warp stages 32 rows, 128
+// features at a time (one 512-byte chunk per load, all 32 in flight), in
+// shared memory with a 528-byte pitch; then each lane walks its own row.
+// tile_mask_kernel's `fresh` mode takes the result as the bound on d(x, c_a)
+// for the current centroids, with no centroid move added.
+constexpr int kRowPitch = 132;  // floats per staged row
+__global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, int k, int d, const int* __restrict__ pid,
+                                                                const int* __restrict__ label,
+                                                                float4* __restrict__ pinfo,
+                                                                const float* __restrict__ chat,
+                                                                const float4* __restrict__ cst,
+                                                                const float* __restrict__ points,
+                                                                const int* __restrict__ stop) {
+    if (stop && *stop) return;
+    __shared__ __align__(16) float tile[2][32][kRowPitch];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * 2 + w) * 32;
+    if (row0 >= rows) return;
+    float(*t)[kRowPitch] = tile[w];
+    const float inf = __int_as_float(0x7f800000);
+    const int64_t g = row0 + lane;
+    const int a = g < rows ? label[g] : -1;
+    const bool valid = (unsigned)a < (unsigned)k;
+    const float* c = chat + (int64_t)(valid ? a : 0) * d;
+    const int my_point = g < rows ? (pid ? pid[g] : (int)g) : -1;  // (point ids are below 2^31)
+    float sq = 0.0f;
+    for (int c0 = 0; c0 < d; c0 += 128) {
+#pragma unroll
+        for (int r = 0; r < 32; ++r) {
+            const int x = __shfl_sync(0xffffffffu, my_point, r);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (x >= 0) v = __ldg(reinterpret_cast<const float4*>(points + (int64_t)x * d + c0) + lane);
+            *reinterpret_cast<float4*>(&t[r][4 * lane]) = v;
+        }
+        __syncwarp();
+        const float4* own = reinterpret_cast<const float4*>(t[lane]);
+#pragma unroll 1
+        for (int b = 0; b < 4; ++b) {
+            float amax = 0.0f;  // fmaxf drops NaN, as the quantizer's maximum does
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = own[8 * b + q];
+                amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+            }
+            const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
+            const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
+            auto rt = [&](float e) { return dev::e4m3_decode(dev::e4m3x2_encode(e * rcp, 0.0f) & 0xffu) * scale; };
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = own[8 * b + q];
+                const float4 cv = __ldg(reinterpret_cast<const float4*>(c + c0 + 32 * b + 4 * q));
+                const float t0 = rt(v.x) - cv.x, t1 = rt(v.y) - cv.y, t2 = rt(v.z) - cv.z, t3 = rt(v.w) - cv.w;
+                sq = fmaf(t0, t0, fmaf(t1, t1, fmaf(t2, t2, fmaf(t3, t3, sq))));
+            }
+        }
+        __syncwarp();
+    }
+    if (g >= rows) return;
+    if (!valid) {
+        pinfo[g].x = inf;
+        return;
+    }
+    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
+    const float4 pi = pinfo[g];  // (-, -, alpha_x, |x^|)
+    const float al = pi.z, shx = pi.w;
+    const float hx2 = shx * shx * (1.0f + 1e-6f);
+    const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
+    const float4 cs = cst[a];  // (beta, |c^|^2, |c|^2, |c^|)
+    const float geo = sq * (1.0f + (float)(d + 8) * 1.2e-7f) * (1.0f + 1e-6f);
+    const float u = geo + al + cs.x + rho_bound(pxh, shx, cs.z, cs.y, cs.w, kappa);
+    const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(cs.x));
+    pinfo[g].x = um == um ? um : inf;
+}
+
 // Per 128-row point tile (one warp; lane l takes rows l, l + 32, l + 64 and
 // l + 96): the union over its rows of the centroid tiles the bounds cannot
 // exclude.  With `compact` (the fused path's row compaction) a row whose every
@@ -434,13 +516,15 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
 // work_scatter_kernel.  tst / tst_old: 2 x tiles stats of the current and
 // (optional) previous centroids; without tst_old or with a non-finite centroid
 // the second-nearest bounds are not used.  prev_label and pinfo are per row,
-// in the visiting order.  Warps loop over point tiles.
+// in the visiting order.  fresh: pinfo's distances bound the distance to the
+// rows' current centroids (row_distance_bound_kernel).  Warps loop over point
+// tiles.
 __global__ void __launch_bounds__(128) tile_mask_kernel(
     int64_t rows, int k, int d, int tiles,
     const int* __restrict__ prev_label, float4* __restrict__ pinfo, const float4* __restrict__ cst,
     const float4* __restrict__ cst_old, const float4* __restrict__ tst, const float4* __restrict__ tst_old,
     const float* __restrict__ delta, const float* __restrict__ dmin, uint64_t* __restrict__ mask,
-    float4* __restrict__ row_bound, int compact, uint4* __restrict__ need_bits, int* __restrict__ tile_count,
+    float4* __restrict__ row_bound, int compact, int fresh, uint4* __restrict__ need_bits, int* __restrict__ tile_count,
     uint64_t* __restrict__ cmask, const int* __restrict__ stop) {
     if (stop && *stop) return;
     const float inf = __int_as_float(0x7f800000);
@@ -484,8 +568,8 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
         for (int q = 0; q < 4; ++q) {
             uint64_t mr;
             bool need;
-            row_tile_mask(tile * 128 + q * 32 + lane, rows, k, tiles, all, kappa, second, gs, prev_label, pinfo, cst,
-                          cst_old, tst, delta, dmin, row_bound, compact, mr, need);
+            row_tile_mask(tile * 128 + q * 32 + lane, rows, k, tiles, all, kappa, second, fresh != 0, gs, prev_label,
+                          pinfo, cst, cst_old, tst, delta, dmin, row_bound, compact, mr, need);
             m |= mr;
             nb[q] = __ballot_sync(0xffffffffu, need);
         }
@@ -636,10 +720,23 @@ int launch_centroid_pairs_drift(int k, int d, const float* delta, const float4* 
     return MXK_OK;
 }
 
+int launch_row_distance_bound(int64_t rows, int k, int d, const int* pid, const int* label, float4* pinfo,
+                              const float* chat, const float4* cst, const float* points, const int* stop,
+                              cudaStream_t stream) {
+    if (rows <= 0) return MXK_OK;
+    MXK_REQUIRE(prune_supported(k, d) && label && pinfo && chat && cst && points, "row distance bound: bad arguments");
+    MXK_REQUIRE((rows + 63) / 64 < (1ll << 31), "row distance bound: too many rows");
+    LaunchScope scope("row_distance_bound", stream);
+    row_distance_bound_kernel<<<(unsigned)((rows + 63) / 64), 64, 0, stream>>>(rows, k, d, pid, label, pinfo, chat,
+                                                                               cst, points, stop);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
+}
+
 int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev_label, float4* pinfo,
                      const float4* cst, const float4* cst_old, const float4* tst, const float4* tst_old,
                      const float* delta, const float* dmin, uint64_t* mask, float4* row_bound, const int* stop,
-                     cudaStream_t stream, WorkRows* work) {
+                     cudaStream_t stream, WorkRows* work, bool fresh) {
     if (rows <= 0 && !work) return MXK_OK;
     const int tiles = (k + kCentroidTileRows - 1) / kCentroidTileRows;
     MXK_REQUIRE(tiles <= kMaxPruneTiles, "tile mask: at most 64 centroid tiles");
@@ -659,7 +756,7 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
         tile_mask_kernel<<<(unsigned)std::min<int64_t>((blocks + 3) / 4, (int64_t)sm_count() * per_sm), 128, 0,
                            stream>>>(
             rows, k, d, tiles, prev_label, pinfo, cst, cst_old, tst, tst_old, delta, dmin, mask,
-            row_bound, work ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
+            row_bound, work ? 1 : 0, fresh ? 1 : 0, work ? work->need_bits : nullptr, work ? work->counts : nullptr,
             work ? reinterpret_cast<uint64_t*>(work->cmask) : nullptr, stop);
         MXK_CUDA(cudaGetLastError());
     }
