@@ -29,12 +29,6 @@ inline int64_t scale_atom_bytes(int64_t rows, int d, int tile_rows = kPointTileR
     return (rows + tile_rows - 1) / tile_rows * (d / 128) * ((tile_rows + 127) / 128) * 512;
 }
 int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream_t stream);
-// launch_l2_norm's norms (bit-identical) and, per point, the pruning pass's
-// pinfo = (+inf and 0: the slots the GEMM writes the point's distance and its
-// second-nearest bound into, |x|^2 - |x^|^2, |x^|) for its MXFP8 round trip
-// x^, in one pass over the points.  d % 128 == 0, points 16-byte aligned.
-int launch_point_norm_stats(int64_t n, int d, const float* points, float* norms, float4* pinfo,
-                            cudaStream_t stream);
 // Rows of an MXFP8 matrix (d bytes per row, d / 32 row-major scale bytes)
 // gathered in the order pid (null: identity) into contiguous rows, scales in the
 // kPointTileRows atom layout.  stop: the Lloyd loop's stop word (optional).
@@ -66,10 +60,11 @@ int launch_group_compaction(int64_t n, const int* precision, const int* order, i
 int64_t label_sort_scratch_ints(int k);
 // Per-row state kept in the visiting order (the pruning pass's records and
 // the rows' labels), moved along when the order is rebuilt: state[g] is the
-// record and label[g] the current label of the point at position g; tmp_* are
-// n-entry scratch.  With it the sort reorders the current visiting order (the
-// order buffer must hold a permutation, e.g. launch_identity_order's) by
-// label[] instead of the points 0..n-1 by labels[]; k <= 16384.
+// record (not moved while null) and label[g] the current label of the point at
+// position g; tmp_* are n-entry scratch.  With it the sort reorders the
+// current visiting order (the order buffer must hold a permutation, e.g.
+// launch_identity_order's) by label[] instead of the points 0..n-1 by
+// labels[]; k <= 16384.
 struct RowState {
     float4* state = nullptr;
     int* label = nullptr;
@@ -206,9 +201,10 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
                      const float* delta, const float* dmin, uint64_t* mask, float4* row_bound, const int* stop,
                      cudaStream_t stream, WorkRows* work = nullptr, bool fresh = false);
 // Per row (in pid order, labels and pinfo per row as launch_tile_mask reads
-// them): pinfo.x = an upper bound on the row's distance to its label's current
-// centroid, from the point's row (MXFP8 round trip) and chat[label] -- one
-// pass over the points, for an iteration whose centroids moved far.
+// them): the whole pinfo record -- an upper bound on the row's distance to its
+// label's current centroid, 0, alpha_x, |x^| -- from the point's row (MXFP8
+// round trip) and chat[label]: one pass over the points, for the first pruned
+// iteration, whose centroids moved far.
 int launch_row_distance_bound(int64_t rows, int k, int d, const int* pid, const int* label, float4* pinfo,
                               const float* chat, const float4* cst, const float* points, const int* stop,
                               cudaStream_t stream);

@@ -422,7 +422,8 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     float *dmin = nullptr, *cdelta = nullptr, *chat = nullptr, *bmax32 = nullptr;
     // per row of the visiting order (RowState: moved along when the order is
     // rebuilt): (distance from the last GEMM, its bound on every other
-    // centroid's distance, alpha, |x^|) and the row's label
+    // centroid's distance, alpha, |x^|), written from the first pruned
+    // iteration on, and the row's label
     float4* pinfo = nullptr;
     RowState rows_state;
     // per-centroid stats [2][k] and per-tile stats [2][2][ctiles], by iteration parity
@@ -481,12 +482,10 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     }
 
     // Once per run (kmeans.cu:24-27).
-    if (prune) {  // the points' norms and their pruning terms in one pass, in point order (the first visiting order)
-        MXK_CHECK(launch_point_norm_stats(n, d, points, pnorm, pinfo, stream));
-        MXK_CHECK(launch_identity_order(n, order, stream));  // (the sort reorders the visiting order)
-    } else {
-        MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
-    }
+    MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
+    // (with pruning the sort reorders the visiting order, first the points' own;
+    // the first pruned iteration writes the rows' pruning records)
+    if (prune) MXK_CHECK(launch_identity_order(n, order, stream));
     if (cache) MXK_CHECK(launch_quantize(8, n, d, points, nullptr, qnat, snat, nullptr, nullptr, stream, 0));
     if (!forced8) MXK_CHECK(launch_point_bounds(n, d, points, pnorm, upper, stream));
     if (n) MXK_CUDA(cudaMemsetAsync(gaps, 0, sizeof(float) * n, stream));
@@ -609,7 +608,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             am.row_bound = prune_it ? (compacted ? work.rb : rbound) : nullptr;
             am.changes = prune_it ? chg : nullptr;
             am.change_count = prune_it ? chg_count : nullptr;
-            am.best_dist = prune ? reinterpret_cast<float*>(pinfo) : nullptr;
+            am.best_dist = prune_it ? reinterpret_cast<float*>(pinfo) : nullptr;
             am.best_dist_stride = 4;
             am.by_row = prune;  // (the rows' state follows the visiting order)
             am.row_labels = prune ? rows_state.label : nullptr;
@@ -689,8 +688,11 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             if (gated)
                 MXK_CHECK(launch_sort_gate(loop, chg_count, sort_ctl,
                                            (int)std::max<int64_t>(1, n / kResortChangeDiv), stream));
+            // (the records exist from the first pruned iteration on)
+            RowState rs = rows_state;
+            if (pruned_its == 0) rs.state = nullptr;
             MXK_CHECK(launch_label_sort(n, k, labels, order, sort_scratch, stream, gated ? sort_ctl + 1 : loop,
-                                        prune ? &rows_state : nullptr));
+                                        prune ? &rs : nullptr));
             cached_stale = true;
             ord = order;
         }

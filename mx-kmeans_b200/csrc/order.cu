@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(512) label_scatter_rows_kernel(int64_t n, int 
         if (key >= 0) {
             const int dst = pos + __popc(peers & ((1u << lane) - 1u));
             rs.tmp_order[dst] = order[g];
-            rs.tmp_state[dst] = rs.state[g];
+            if (rs.state) rs.tmp_state[dst] = rs.state[g];
             rs.tmp_label[dst] = label;
         }
     }
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(256) row_state_copy_kernel(int64_t n, RowState
     if (stop && *stop) return;
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (int64_t)gridDim.x * blockDim.x) {
         order[g] = rs.tmp_order[g];
-        rs.state[g] = rs.tmp_state[g];
+        if (rs.state) rs.state[g] = rs.tmp_state[g];
         rs.label[g] = rs.tmp_label[g];
     }
 }
@@ -244,7 +244,7 @@ int launch_label_sort(int64_t n, int k, const int* labels, int* order, int* scra
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(k > 0 && labels && order && scratch, "label_sort: bad arguments");
     const RowState rs = row_state ? *row_state : RowState{};
-    MXK_REQUIRE(!row_state || (rs.state && rs.label && rs.tmp_state && rs.tmp_label && rs.tmp_order && k <= kSmemBins),
+    MXK_REQUIRE(!row_state || (rs.label && rs.tmp_state && rs.tmp_label && rs.tmp_order && k <= kSmemBins),
                 "label_sort: incomplete row state, or k above the shared-memory cursors");
     MXK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int) * (size_t)k, stream));
     const int sms = sm_count();

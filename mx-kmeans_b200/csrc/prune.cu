@@ -425,16 +425,17 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
     if (row_bound) row_bound[row] = rb;
 }
 
-// Each row's distance bound against its label's current centroid, from the
-// rows themselves: |x^ - c^_a|^2 summed in FP32 over the MXFP8 round trip x^
-// of the point's row (quantize_rows' arithmetic: UE8M0 scale of each 32-feature
+// Each row's pruning record, from the rows themselves: pinfo[g] = (an upper
+// bound on d(x, c_a) for its label a's current centroid, 0, alpha_x, |x^|).
+// The bound is |x^ - c^_a|^2 summed in FP32 over the MXFP8 round trip x^ of
+// the point's row (quantize_rows' arithmetic: UE8M0 scale of each 32-feature
 // block, E4M3 round to nearest even) and the dequantized centroid chat[a], plus
-// the rounding of that sum, alpha_x + beta_a and rho, written into pinfo[g].x
-// (+inf for a row without a valid label).  A warp stages 32 rows, 128
-// features at a time (one 512-byte chunk per load, all 32 in flight), in
-// shared memory with a 528-byte pitch; then each lane walks its own row.
-// tile_mask_kernel's `fresh` mode takes the result as the bound on d(x, c_a)
-// for the current centroids, with no centroid move added.
+// the rounding of that sum, alpha_x + beta_a and rho (+inf for a row without
+// a valid label); alpha_x = |x|^2 - |x^|^2 with |x|^2 summed as compute_l2_norm
+// does.  A warp stages 32 rows, 128 features at a time (one 512-byte chunk per
+// load, all 32 in flight), in shared memory with a 528-byte pitch; then each
+// lane walks its own row.  tile_mask_kernel's `fresh` mode takes the bound on
+// d(x, c_a) for the current centroids, with no centroid move added.
 constexpr int kRowPitch = 132;  // floats per staged row
 __global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, int k, int d, const int* __restrict__ pid,
                                                                 const int* __restrict__ label,
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, in
     const bool valid = (unsigned)a < (unsigned)k;
     const float* c = chat + (int64_t)(valid ? a : 0) * d;
     const int my_point = g < rows ? (pid ? pid[g] : (int)g) : -1;  // (point ids are below 2^31)
-    float sq = 0.0f;
+    float sq = 0.0f, norm = 0.0f, h = 0.0f;
     for (int c0 = 0; c0 < d; c0 += 128) {
 #pragma unroll
         for (int r = 0; r < 32; ++r) {
@@ -473,6 +474,7 @@ __global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, in
             for (int q = 0; q < 8; ++q) {
                 const float4 v = own[8 * b + q];
                 amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+                norm = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, norm))));  // feature order
             }
             const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
             const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
@@ -481,27 +483,28 @@ __global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, in
             for (int q = 0; q < 8; ++q) {
                 const float4 v = own[8 * b + q];
                 const float4 cv = __ldg(reinterpret_cast<const float4*>(c + c0 + 32 * b + 4 * q));
-                const float t0 = rt(v.x) - cv.x, t1 = rt(v.y) - cv.y, t2 = rt(v.z) - cv.z, t3 = rt(v.w) - cv.w;
+                const float x0 = rt(v.x), x1 = rt(v.y), x2 = rt(v.z), x3 = rt(v.w);
+                h = fmaf(x0, x0, fmaf(x1, x1, fmaf(x2, x2, fmaf(x3, x3, h))));
+                const float t0 = x0 - cv.x, t1 = x1 - cv.y, t2 = x2 - cv.z, t3 = x3 - cv.w;
                 sq = fmaf(t0, t0, fmaf(t1, t1, fmaf(t2, t2, fmaf(t3, t3, sq))));
             }
         }
         __syncwarp();
     }
     if (g >= rows) return;
+    const float al = norm - h, shx = sqrtf(h);
     if (!valid) {
-        pinfo[g].x = inf;
+        pinfo[g] = make_float4(inf, 0.0f, al, shx);
         return;
     }
     const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
-    const float4 pi = pinfo[g];  // (-, -, alpha_x, |x^|)
-    const float al = pi.z, shx = pi.w;
     const float hx2 = shx * shx * (1.0f + 1e-6f);
     const float pxh = fabsf(al + hx2) * (1.0f + 1e-6f) + hx2;
     const float4 cs = cst[a];  // (beta, |c^|^2, |c|^2, |c^|)
     const float geo = sq * (1.0f + (float)(d + 8) * 1.2e-7f) * (1.0f + 1e-6f);
     const float u = geo + al + cs.x + rho_bound(pxh, shx, cs.z, cs.y, cs.w, kappa);
     const float um = u + 1e-4f * (fabsf(u) + fabsf(al) + fabsf(cs.x));
-    pinfo[g].x = um == um ? um : inf;
+    pinfo[g] = make_float4(um == um ? um : inf, 0.0f, al, shx);
 }
 
 // Per 128-row point tile (one warp; lane l takes rows l, l + 32, l + 64 and

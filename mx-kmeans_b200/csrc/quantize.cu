@@ -174,22 +174,16 @@ __global__ void __launch_bounds__(256) l2_norm_kernel(int64_t rows, int d, const
 // stages 32 consecutive rows, 128 features at a time (one 512-byte row chunk
 // per load, all 32 in flight), in shared memory with a 528-byte row pitch
 // (16-byte stores and loads both conflict-free), then each lane walks its own
-// row in feature order.  kStats also produces, per row, the pruning pass's
-// MXFP8 terms in pinfo: (+inf and 0: the slots the GEMM writes the row's
-// distance and second-nearest bound into, |x|^2 - |x^|^2, |x^|) for the row's
-// MXFP8 round trip x^
-// (UE8M0 scale of each 32-feature block, E4M3 round-to-nearest-even,
-// saturating, as quantize_rows).
+// row in feature order.
 constexpr int kNormPitch = 132;  // floats per staged row
-template <bool kStats>
 __global__ void __launch_bounds__(64) norm_rows_staged_kernel(int64_t rows, int d, const float* __restrict__ x,
-                                                              float* __restrict__ norms, float4* __restrict__ pinfo) {
+                                                              float* __restrict__ norms) {
     __shared__ __align__(16) float tile[2][32][kNormPitch];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row0 = ((int64_t)blockIdx.x * 2 + w) * 32;
     if (row0 >= rows) return;
     float(*t)[kNormPitch] = tile[w];
-    float sum = 0.0f, h = 0.0f;
+    float sum = 0.0f;
     for (int c = 0; c < d; c += 128) {
 #pragma unroll
         for (int r = 0; r < 32; ++r) {
@@ -208,33 +202,10 @@ __global__ void __launch_bounds__(64) norm_rows_staged_kernel(int64_t rows, int 
             sum = fmaf(v.z, v.z, sum);
             sum = fmaf(v.w, v.w, sum);
         }
-        if constexpr (kStats) {
-#pragma unroll 1
-            for (int b = 0; b < 4; ++b) {
-                float amax = 0.0f;  // fmaxf drops NaN, as the quantizer's maximum does
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 v = own[8 * b + q];
-                    amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
-                }
-                const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
-                const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
-                auto rt = [&](float e) { return dev::e4m3_decode(dev::e4m3x2_encode(e * rcp, 0.0f) & 0xffu) * scale; };
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 v = own[8 * b + q];
-                    const float a = rt(v.x), bb = rt(v.y), cc = rt(v.z), dd = rt(v.w);
-                    h = fmaf(a, a, fmaf(bb, bb, fmaf(cc, cc, fmaf(dd, dd, h))));
-                }
-            }
-        }
         __syncwarp();
     }
     const int64_t my = row0 + lane;
-    if (my < rows) {
-        norms[my] = sum;
-        if constexpr (kStats) pinfo[my] = make_float4(__int_as_float(0x7f800000), 0.0f, sum - h, sqrtf(h));
-    }
+    if (my < rows) norms[my] = sum;
 }
 
 // The same sums for a few rows (the centroids, every iteration): one thread per
@@ -482,23 +453,11 @@ int launch_l2_norm(int64_t rows, int d, const float* x, float* norms, cudaStream
         // few rows: spread them over the SMs, one per thread
         l2_norm_rows_kernel<<<(unsigned)((rows + 63) / 64), 64, 0, stream>>>(rows, d, x, norms);
     } else if (d % 128 == 0 && aligned) {
-        norm_rows_staged_kernel<false>
-            <<<(unsigned)((rows + 63) / 64), 64, 0, stream>>>(rows, d, x, norms, nullptr);
+        norm_rows_staged_kernel<<<(unsigned)((rows + 63) / 64), 64, 0, stream>>>(rows, d, x, norms);
     } else {
         const int64_t blocks = (rows + 255) / 256;
         l2_norm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, d, x, norms);
     }
-    MXK_CUDA(cudaGetLastError());
-    return MXK_OK;
-}
-
-int launch_point_norm_stats(int64_t n, int d, const float* points, float* norms, float4* pinfo,
-                            cudaStream_t stream) {
-    if (n <= 0) return MXK_OK;
-    MXK_REQUIRE(d % 128 == 0 && reinterpret_cast<uintptr_t>(points) % 16 == 0,
-                "point norm stats: d must be a multiple of 128 and the rows 16-byte aligned");
-    LaunchScope scope("point_norm_stats", stream);
-    norm_rows_staged_kernel<true><<<(unsigned)((n + 63) / 64), 64, 0, stream>>>(n, d, points, norms, pinfo);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
 }
