@@ -72,18 +72,19 @@ def parse():
     return p.parse_args()
 
 
-def measured_traffic(rows, cfg):
-    """dram__bytes_read.sum + dram__bytes_write.sum of one full-size fused-GEMM
-    launch at configs[3], from the committed summary of its ncu capture (scaled
-    to `rows`: every byte it counts is per point row); None for the other
+def measured_traffic(rows_per_launch, cfg):
+    """dram__bytes_read.sum + dram__bytes_write.sum per fused-GEMM launch at
+    the DRAM bytes per processed point row of every GEMM launch of
+    one 20-iteration call, from the committed summary of that ncu capture,
+    times the rows a launch processed here on average; None for the other
     configurations or if the summary is missing."""
     if cfg is not CONFIGS[HEADLINE]:
         return None
     path = os.path.join(ROOT, "profiles", "mx_gemm_argmin_config4.md")
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_full_launch:"):
-                return float(line.split(":")[1]) * rows / N_POINTS
+            if line.startswith("traffic_bytes_per_row:"):
+                return float(line.split(":")[1]) * rows_per_launch
     except OSError:
         pass
     return None
@@ -114,20 +115,22 @@ def update_roofline(stats, rows, d_pad, peak_gbs):
             "launches": launches, "kernel": "accumulate_runs"}
 
 
-def quantize_roofline(stats, rows, d_pad, peak_gbs):
+def quantize_roofline(stats, rows_total, d_pad, peak_gbs, iterations):
     """Achieved HBM bandwidth of the per-iteration point quantize
-    (quantize_rows on the group's rows in visiting order, MXFP8, the scale
-    atoms of the GEMM's point tiles) from its CUDA-event times: algorithmic
-    bytes per launch = rows * (4 D_pad read + D_pad values + D_pad / 32 scales
-    written + 4 for the row's point id).  None when the quantize is fused into
-    the GEMM (D = 128) and has no launch of its own."""
+    (quantize_rows on the rows the GEMM processes, in visiting order, MXFP8,
+    the scale atoms of the GEMM's point tiles) from its CUDA-event times:
+    algorithmic bytes = rows_total (all rows quantized in the timed region) *
+    (4 D_pad read + D_pad values + D_pad / 32 scales written + 4 for the row's
+    point id), over the launches' total time (launches enqueued after the loop
+    stopped do nothing and count only their few microseconds).  None when the
+    quantize is fused into the GEMM (D = 128) and has no launch of its own."""
     launches, total_ms = stats.get("quantize_points", (0, 0.0))
-    if not launches or total_ms <= 0.0:
+    if not launches or total_ms <= 0.0 or iterations <= 0:
         return None
-    alg_bytes = rows * (5.0 * d_pad + d_pad / 32.0 + 4.0)
-    gbs = alg_bytes * launches / (total_ms / 1e3) / 1e9
+    alg_bytes = rows_total * (5.0 * d_pad + d_pad / 32.0 + 4.0)
+    gbs = alg_bytes / (total_ms / 1e3) / 1e9
     return {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s", "frac": gbs / peak_gbs,
-            "algorithmic_bytes_per_launch": alg_bytes, "ms_per_launch": total_ms / launches,
+            "algorithmic_bytes_per_iteration": alg_bytes / iterations, "ms_per_iteration": total_ms / iterations,
             "launches": launches, "kernel": "quantize_points"}
 
 
@@ -584,14 +587,15 @@ def main():
         gbs = bytes_total / seconds / 1e9
         # the binding roofline is the one whose ideal time is longer
         hbm_bound = alg_bytes / (peak_gbs * 1e9) > (executed / max(iters, 1)) / (peak_tf * 1e12)
-        traffic = measured_traffic(rows, cfg)
+        traffic = measured_traffic(rows_done / max(iters, 1), cfg)
         roofline = {"bound": "hbm" if hbm_bound else "tensor",
                     "achieved": gbs if hbm_bound else tflops, "peak": peak_gbs if hbm_bound else peak_tf,
                     "unit": "GB/s" if hbm_bound else "TFLOP/s",
                     "frac": gbs / peak_gbs if hbm_bound else tflops / peak_tf, "traffic": traffic,
-                    "traffic_source": ("ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of one pruned "
-                                       "launch at N = 2,097,152 scaled by rows, profiles/mx_gemm_argmin_config4.md; "
-                                       "not measured in this run") if traffic else None,
+                    "traffic_source": ("ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of every GEMM "
+                                       "launch of one 20-iteration call at N = 2,097,152, per processed row, times "
+                                       "this run's rows per launch; profiles/mx_gemm_argmin_config4.md; not "
+                                       "measured in this run") if traffic else None,
                     "algorithmic_bytes_per_launch": alg_bytes,
                     "tensor_tflops_executed": tflops, "tensor_frac_executed": tflops / peak_tf,
                     "kernel": "mx_gemm_argmin", "ms_per_iteration": gemm[1] / max(iters, 1),
@@ -606,7 +610,7 @@ def main():
                  for kk, v in sorted(stats.items(), key=lambda kv: -kv[1][1])}
     update = update_roofline(stats, rows, d_pad, peak_gbs)
     # (the point quantize encodes the rows the GEMM processes)
-    quant = quantize_roofline(stats, rows_done / max(iters, 1), d_pad, peak_gbs)
+    quant = quantize_roofline(stats, rows_done, d_pad, peak_gbs, iters)
 
     cpu = None
     if rank == 0 and world == 1 and not args.quick:

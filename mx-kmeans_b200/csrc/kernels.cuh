@@ -225,8 +225,11 @@ int launch_assign_clusters(int64_t rows, int k, const float* point_norms, const 
 // driver, whose running sums also take label-change deltas).
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
                       float* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
+// switched: a launch launch_update_gate may turn into a no-op; its profile
+// records carry a "_switched" suffix.
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order,
-                      double* sums, int* counts, cudaStream_t stream, const int* stop = nullptr);
+                      double* sums, int* counts, cudaStream_t stream, const int* stop = nullptr,
+                      bool switched = false);
 // centroids = counts ? sums / counts : old.  If shift_scratch is not null
 // (shift_scratch_floats() floats, zeroed once before the first use by a Lloyd
 // loop), shift_scratch[shift_total_index()] receives sum((old - new)^2),
@@ -250,16 +253,23 @@ int64_t shift_total_index();
 // iterations, to which this iteration's sums / counts are added (full: which
 // they replace); the centroids come from the running values.  zero_word
 // (optional) is zeroed once the launch has read everything.
+// full_dev (optional): a device word read at run time in place of `full`.
 int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop = nullptr, float tolerance = 0.0f,
                     float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr,
                     double* acc_sums = nullptr, int* acc_counts = nullptr, bool full = true,
-                    int* zero_word = nullptr);
+                    int* zero_word = nullptr, const int* full_dev = nullptr);
 int launch_finalize(int d, int k, double* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop = nullptr, float tolerance = 0.0f,
                     float* prev_out = nullptr, bool zero_sums = false, int* host_state = nullptr,
                     double* acc_sums = nullptr, int* acc_counts = nullptr, bool full = true,
-                    int* zero_word = nullptr);
+                    int* zero_word = nullptr, const int* full_dev = nullptr);
+// Chooses between the incremental update and a fresh accumulation on the
+// device from this iteration's change count: words = (stop word for
+// launch_accumulate_changes, stop word for launch_accumulate, `full` word for
+// launch_finalize); fresh once *changes > threshold.  stop: the loop's stop
+// word (both skipped once it is set).
+int launch_update_gate(const int* stop, const int* changes, int threshold, int* words, cudaStream_t stream);
 // The label changes recorded by the GEMM (rec[i] = (point, old label, new
 // label, 0), *count of them): each moves its point's row and count from the old
 // cluster's to the new one's in sums / counts (this iteration's additions).

@@ -247,6 +247,11 @@ constexpr int64_t kResortChangeDiv = 32;
 // for those bounds to prove a row (measured at configs[3]: no effect on the
 // third and fourth iterations), and the record costs the GEMM ~10%.
 constexpr int kSecondBoundFrom = 2;
+// A pruned iteration with more than n / kFreshUpdateDiv label changes
+// accumulates every point afresh (one streaming pass) instead of moving the
+// changed rows (two FP64 reductions per feature and change): measured at
+// configs[4], 20 ms of incremental update against 8 ms for the fresh pass.
+constexpr int64_t kFreshUpdateDiv = 8;
 // Full centroid-pair bound computations: the first kPairsFullFirst pruned
 // iterations, then every kPairsFullEvery-th (drift updates in between).
 constexpr int kPairsFullFirst = 3;
@@ -409,7 +414,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
     MXK_CUDA(cudaMemsetAsync(sums, 0, sizeof(double) * kd, stream));
     MXK_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * k, stream));
     double* acc_sums = nullptr;
-    int *acc_counts = nullptr, *chg_count = nullptr;
+    int *acc_counts = nullptr, *chg_count = nullptr, *upd_gate = nullptr;
     int4* chg = nullptr;
     MXK_CHECK(ws.alloc(&acc_sums, kd));
     MXK_CHECK(ws.alloc(&acc_counts, k));
@@ -447,6 +452,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&rbound, n));
         MXK_CHECK(ws.alloc(&chg, n));
         MXK_CHECK(ws.alloc(&chg_count, 1));
+        MXK_CHECK(ws.alloc(&upd_gate, 3));
         MXK_CUDA(cudaMemsetAsync(chg_count, 0, sizeof(int), stream));
     }
     // Row compaction in pruned iterations (not with the point cache, whose GEMM
@@ -697,11 +703,20 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             ord = order;
         }
         // kmeans.cu:62-65 (sums and counts are zero: set before the loop, and
-        // left zero by every finalize)
+        // left zero by every finalize).  An incremental iteration of a
+        // single-GPU run whose labels changed for more than n / kFreshUpdateDiv
+        // rows accumulates every point afresh instead, decided on the device
+        // (a sharded run keeps the incremental update: its ranks must agree).
+        const bool switchable = incremental && !sharded;
+        if (switchable)
+            MXK_CHECK(launch_update_gate(loop, chg_count, (int)std::max<int64_t>(1, n / kFreshUpdateDiv), upd_gate,
+                                         stream));
         if (incremental)
-            MXK_CHECK(launch_accumulate_changes(d, k, points, chg, chg_count, sums, counts, stream, loop));
-        else
-            MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream, loop));
+            MXK_CHECK(launch_accumulate_changes(d, k, points, chg, chg_count, sums, counts, stream,
+                                                switchable ? upd_gate : loop));
+        if (!incremental || switchable)
+            MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream,
+                                        switchable ? upd_gate + 1 : loop, switchable));
         if (sharded) {
             NcclApi& api = nccl();
             ncclResult_t r = api.GroupStart();
@@ -718,7 +733,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         const int slot = it % (kLookahead + 1);
         MXK_CHECK(launch_finalize(d, k, sums, counts, centroids, centroids, shift, stream, loop, options->tolerance,
                                   prev, true, mirror->dev + 4 * slot, acc_sums, acc_counts, !incremental,
-                                  incremental ? chg_count : nullptr));
+                                  incremental ? chg_count : nullptr, switchable ? upd_gate + 2 : nullptr));
         MXK_CUDA(cudaEventRecord(mirror->ev[slot], stream));
         // Read the state of iteration it - lookahead.  FP32 iterations (whose
         // kernels do not consult the stop word) and verbose runs are read at once,

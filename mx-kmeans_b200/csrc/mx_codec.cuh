@@ -92,6 +92,14 @@ __device__ __forceinline__ float e4m3_decode(uint32_t code) {
     return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
 }
 
+// Values of the two E4M3 codes of e4m3x2_encode's result (low byte -> .x).
+__device__ __forceinline__ float2 e4m3x2_decode(uint32_t codes) {
+    uint32_t h2;
+    uint16_t c = (uint16_t)(codes & 0xffffu);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return __half22float2(*reinterpret_cast<const __half2*>(&h2));
+}
+
 // Software round-to-nearest-even encoder for a small IEEE-like format with
 // MB mantissa bits, bias BIAS, sign at bit SIGN and largest magnitude MAXV.
 template <int MB, int BIAS, int SIGN>

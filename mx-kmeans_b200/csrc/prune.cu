@@ -422,7 +422,7 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
         }
     }
     if (compact && !need) m = 0;
-    if (row_bound) row_bound[row] = rb;
+    if (row_bound && (need || !compact)) row_bound[row] = rb;  // (compaction copies only the kept rows' records)
 }
 
 // Each row's pruning record, from the rows themselves: pinfo[g] = (an upper
@@ -478,12 +478,13 @@ __global__ void __launch_bounds__(64) row_distance_bound_kernel(int64_t rows, in
             }
             const uint32_t sc = dev::ue8m0_mxfp8_scale(amax);
             const float rcp = dev::ue8m0_reciprocal(sc), scale = dev::ue8m0_value(sc);
-            auto rt = [&](float e) { return dev::e4m3_decode(dev::e4m3x2_encode(e * rcp, 0.0f) & 0xffu) * scale; };
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 v = own[8 * b + q];
                 const float4 cv = __ldg(reinterpret_cast<const float4*>(c + c0 + 32 * b + 4 * q));
-                const float x0 = rt(v.x), x1 = rt(v.y), x2 = rt(v.z), x3 = rt(v.w);
+                const float2 lo = dev::e4m3x2_decode(dev::e4m3x2_encode(v.x * rcp, v.y * rcp));
+                const float2 hi = dev::e4m3x2_decode(dev::e4m3x2_encode(v.z * rcp, v.w * rcp));
+                const float x0 = lo.x * scale, x1 = lo.y * scale, x2 = hi.x * scale, x3 = hi.y * scale;
                 h = fmaf(x0, x0, fmaf(x1, x1, fmaf(x2, x2, fmaf(x3, x3, h))));
                 const float t0 = x0 - cv.x, t1 = x1 - cv.y, t2 = x2 - cv.z, t3 = x3 - cv.w;
                 sq = fmaf(t0, t0, fmaf(t1, t1, fmaf(t2, t2, fmaf(t3, t3, sq))));

@@ -294,11 +294,13 @@ __global__ void __launch_bounds__(256) finalize_kernel(int d, int k, T* __restri
                                                        unsigned* __restrict__ done, float* __restrict__ total_out,
                                                        float tolerance, int zero_sums, int* __restrict__ host_state,
                                                        double* __restrict__ acc_sums, int* __restrict__ acc_counts,
-                                                       int full, int* __restrict__ zero_word) {
+                                                       int full_host, int* __restrict__ zero_word,
+                                                       const int* __restrict__ full_dev) {
     if (loop && *(volatile int*)loop) {  // converged: the centroids stay as they are
         if (blockIdx.x == 0 && threadIdx.x == 0) publish_state(loop, host_state);
         return;
     }
+    const int full = full_dev ? *full_dev : full_host;
     __shared__ float warp_sum[8];
     const int64_t total = (int64_t)k * d;
     float local = 0.0f;
@@ -403,8 +405,8 @@ __global__ void __launch_bounds__(256) shift_kernel(int64_t elements, const floa
 constexpr int kShiftBlocks = 256;  // fixed grid of the shift reduction (<= partial slots)
 
 template <class T>
-int accumulate_impl(int64_t n, int d, int k, const float* points, const int* labels, const int* order, T* sums,
-                    int* counts, cudaStream_t stream, const int* stop) {
+int accumulate_impl(bool switched, int64_t n, int d, int k, const float* points, const int* labels, const int* order,
+                    T* sums, int* counts, cudaStream_t stream, const int* stop) {
     if (n <= 0) return MXK_OK;
     MXK_REQUIRE(d > 0 && k > 0 && points && labels && sums && counts, "update_centroids: bad arguments");
     const int sms = sm_count();
@@ -421,7 +423,7 @@ int accumulate_impl(int64_t n, int d, int k, const float* points, const int* lab
     if (!order && aligned && d % 4 == 0 && priv_bytes <= max_smem && priv_bytes <= 200 * 1024 && n >= (int64_t)k * 64) {
         MXK_CUDA(cudaFuncSetAttribute(accumulate_private_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)priv_bytes));
-        LaunchScope scope("accumulate_private", stream);
+        LaunchScope scope(switched ? "accumulate_private_switched" : "accumulate_private", stream);
         accumulate_private_kernel<T><<<sms, 512, (size_t)priv_bytes, stream>>>(n, d, k, points, labels, order, sums,
                                                                                 counts, err, stop);
         MXK_CUDA(cudaGetLastError());
@@ -439,7 +441,7 @@ int accumulate_impl(int64_t n, int d, int k, const float* points, const int* lab
             if (per_warp < 16) per_warp = 16;
             const int64_t warps = (n + per_warp - 1) / per_warp;
             const int64_t blocks = (warps * 32 + 255) / 256;
-            LaunchScope scope("accumulate_runs", stream);
+            LaunchScope scope(switched ? "accumulate_runs_switched" : "accumulate_runs", stream);
             kernel<<<(unsigned)blocks, 256, 0, stream>>>(n, d, k, points, labels, order, sums, counts, per_warp, err,
                                                          stop);
             MXK_CUDA(cudaGetLastError());
@@ -456,7 +458,7 @@ int accumulate_impl(int64_t n, int d, int k, const float* points, const int* lab
             default: return launch(accumulate_runs_kernel<8, T>);
         }
     }
-    LaunchScope scope("accumulate_scalar", stream);
+    LaunchScope scope(switched ? "accumulate_scalar_switched" : "accumulate_scalar", stream);
     accumulate_scalar_kernel<T><<<sms * 8, 256, 0, stream>>>(n, d, k, points, labels, sums, counts, err, stop);
     MXK_CUDA(cudaGetLastError());
     return MXK_OK;
@@ -465,7 +467,8 @@ int accumulate_impl(int64_t n, int d, int k, const float* points, const int* lab
 template <class T>
 int finalize_impl(int d, int k, T* sums, int* counts, const float* old_centroids, float* centroids,
                   float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
-                  bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+                  bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word,
+                  const int* full_dev) {
     MXK_REQUIRE(!(zero_sums || host_state || acc_sums) || loop,
                 "finalize: zeroing, running sums and the host state need the loop words");
     MXK_REQUIRE(!acc_sums == !acc_counts, "finalize: running sums and counts go together");
@@ -479,7 +482,7 @@ int finalize_impl(int d, int k, T* sums, int* counts, const float* old_centroids
             d, k, sums, counts, old_centroids, centroids, prev_out, shift_scratch, loop,
             loop ? reinterpret_cast<unsigned*>(shift_scratch + kShiftBlocks + 1) : nullptr,
             loop ? shift_scratch + kShiftBlocks : nullptr, tolerance, zero_sums ? 1 : 0, host_state, acc_sums,
-            acc_counts, full ? 1 : 0, zero_word);
+            acc_counts, full ? 1 : 0, zero_word, full_dev);
         MXK_CUDA(cudaGetLastError());
     }
     if (shift_scratch && !loop) {  // (with loop the finalize kernel's last CTA sums the partials)
@@ -495,11 +498,34 @@ int finalize_impl(int d, int k, T* sums, int* counts, const float* old_centroids
 
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, float* sums,
                       int* counts, cudaStream_t stream, const int* stop) {
-    return accumulate_impl(n, d, k, points, labels, order, sums, counts, stream, stop);
+    return accumulate_impl(false, n, d, k, points, labels, order, sums, counts, stream, stop);
 }
 int launch_accumulate(int64_t n, int d, int k, const float* points, const int* labels, const int* order, double* sums,
-                      int* counts, cudaStream_t stream, const int* stop) {
-    return accumulate_impl(n, d, k, points, labels, order, sums, counts, stream, stop);
+                      int* counts, cudaStream_t stream, const int* stop, bool switched) {
+    return accumulate_impl(switched, n, d, k, points, labels, order, sums, counts, stream, stop);
+}
+
+namespace {
+// w = (skip the incremental update, skip the fresh accumulation, fresh): the
+// fresh accumulation of every point replaces the incremental one once more
+// than `threshold` labels changed; both are skipped once the loop has stopped.
+__global__ void update_gate_kernel(const int* __restrict__ stop, const int* __restrict__ changes, int threshold,
+                                   int* __restrict__ w) {
+    if (threadIdx.x != 0) return;
+    const bool stopped = stop && *stop;
+    const bool fresh = *changes > threshold;
+    w[0] = stopped || fresh;
+    w[1] = stopped || !fresh;
+    w[2] = fresh;
+}
+}  // namespace
+
+int launch_update_gate(const int* stop, const int* changes, int threshold, int* words, cudaStream_t stream) {
+    MXK_REQUIRE(changes && words, "update_gate: bad arguments");
+    LaunchScope scope("update_gate", stream);
+    update_gate_kernel<<<1, 32, 0, stream>>>(stop, changes, threshold, words);
+    MXK_CUDA(cudaGetLastError());
+    return MXK_OK;
 }
 
 int launch_accumulate_changes(int d, int k, const float* points, const int4* rec, const int* count, double* sums,
@@ -523,15 +549,17 @@ int64_t shift_total_index() { return kShiftBlocks; }
 
 int launch_finalize(int d, int k, float* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
-                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word,
+                    const int* full_dev) {
     return finalize_impl(d, k, sums, counts, old_centroids, centroids, shift_scratch, stream, loop, tolerance, prev_out,
-                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word);
+                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word, full_dev);
 }
 int launch_finalize(int d, int k, double* sums, int* counts, const float* old_centroids, float* centroids,
                     float* shift_scratch, cudaStream_t stream, int* loop, float tolerance, float* prev_out,
-                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word) {
+                    bool zero_sums, int* host_state, double* acc_sums, int* acc_counts, bool full, int* zero_word,
+                    const int* full_dev) {
     return finalize_impl(d, k, sums, counts, old_centroids, centroids, shift_scratch, stream, loop, tolerance, prev_out,
-                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word);
+                         zero_sums, host_state, acc_sums, acc_counts, full, zero_word, full_dev);
 }
 
 int launch_shift(int64_t elements, const float* previous, const float* current, float* shift_scratch,

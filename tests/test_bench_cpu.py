@@ -30,7 +30,7 @@ def test_update_roofline_arithmetic():
 def test_update_roofline_absent():
     assert bench.update_roofline({}, 1000, 128, 6535.4) is None
     assert bench.update_roofline({"accumulate_runs": (0, 0.0)}, 1000, 128, 6535.4) is None
-    assert bench.quantize_roofline({}, 1000, 128, 6535.4) is None  # fused into the GEMM at D = 128
+    assert bench.quantize_roofline({}, 1000, 128, 6535.4, 1) is None  # fused into the GEMM at D = 128
 
 
 def test_measured_traffic_and_peaks():
@@ -47,10 +47,11 @@ def test_measured_traffic_and_peaks():
 
 def test_quantize_roofline_arithmetic():
     rows, d = 4194304, 256
-    r = bench.quantize_roofline({"quantize_points": (30, 30 * 0.9)}, rows, d, 6535.4)
-    per_launch = rows * (5.0 * d + d / 32.0 + 4.0)
-    assert r["algorithmic_bytes_per_launch"] == per_launch
-    assert r["achieved"] == pytest.approx(per_launch / 0.0009 / 1e9)
+    # 30 iterations ran, 10 more were enqueued after the stop (no-op launches)
+    r = bench.quantize_roofline({"quantize_points": (40, 30 * 0.9 + 10 * 0.003)}, 30 * rows, d, 6535.4, 30)
+    per_iteration = rows * (5.0 * d + d / 32.0 + 4.0)
+    assert r["algorithmic_bytes_per_iteration"] == per_iteration
+    assert r["achieved"] == pytest.approx(30 * per_iteration / (27.03e-3) / 1e9)
     assert r["frac"] == pytest.approx(r["achieved"] / 6535.4)
 
 
