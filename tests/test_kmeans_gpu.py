@@ -357,3 +357,31 @@ def test_running_sums_over_a_long_run(torch_cuda, mxk, orc):
         assert_centroids_close(c_next, co)
     for t in sorted({1, 5, it // 2, it - 1}):
         gap_band_mismatches(orc, x, tc[t], tl[t])
+
+
+def test_many_label_changes_switch_to_a_fresh_accumulation(torch_cuda, mxk, orc):
+    """Pruned iterations move only the rows whose label changed, unless more than
+    n / 8 labels changed: then the device switches that iteration to a fresh
+    accumulation of every point (the running sums are replaced).  Points without
+    cluster structure (uniform in a cube) and random initial rows keep many
+    labels changing for several iterations, so both branches run within one
+    call; every iteration's next centroids must match the oracle's fresh update
+    from that iteration's labels (src/kernels/update.cu:7-31) within 1e-4, and
+    sampled iterations' labels follow the gap-band rule."""
+    torch = torch_cuda
+    n, d, k, iters = 40000, 128, 256, 12
+    g = np.random.default_rng(8)
+    x = np.zeros((n, d), np.float32)
+    x[:, :96] = g.uniform(-1.0, 1.0, size=(n, 96)).astype(np.float32)
+    c0 = x[g.choice(n, k, replace=False)].copy()
+    it, cg, lg, tc, tl, _ = traced_run(torch, mxk, x, c0, iters)
+    assert it == iters
+    changed = [int((tl[t] != tl[t - 1]).sum()) for t in range(1, it)]
+    assert max(changed) > n // 8, f"no iteration changed more than n / 8 labels: {changed}"
+    assert min(changed) < n // 8, f"every iteration changed more than n / 8 labels: {changed}"
+    for t in range(it):
+        c_next = tc[t + 1] if t + 1 < it else cg
+        co, _ = orc.update_centroids(x, tl[t], tc[t])
+        assert_centroids_close(c_next, co)
+    for t in (1, 2, it // 2, it - 1):
+        gap_band_mismatches(orc, x, tc[t], tl[t])
