@@ -232,12 +232,13 @@ constexpr int64_t kFp32ChunkBytes = 512ll << 20;  // dense product chunk of the 
 // About 40 ms of GPU work at the benchmark shape, so a host thread descheduled or
 // held in the driver for that long does not leave the GPU idle.
 constexpr int kLookahead = 8;
-// The label-sorted visiting order is rebuilt every kResortEvery iterations.  It
-// only shapes performance (assignments are per point; the update's FP64 sums
-// are order-dependent in their last bits, as the reference's FP32 atomics are), and
-// after the first iterations few labels change, so an order one iteration old
-// is nearly as good: measured at configs[3], every second iteration saves the
-// 0.21 ms sort on half of them and costs the GEMM < 0.02 ms.
+// Outside the pruned iterations of the fused path, the label-sorted visiting
+// order is rebuilt every kResortEvery iterations.  It only shapes performance
+// (assignments are per point; the update's FP64 sums are order-dependent in
+// their last bits, as the reference's FP32 atomics are), and after the first
+// iterations few labels change, so an order one iteration old is nearly as
+// good: measured at configs[3], every second iteration saved the 0.21 ms sort
+// on half of them and cost the GEMM < 0.02 ms.
 constexpr int kResortEvery = 2;
 // Pruned fused iterations rebuild the order once n / kResortChangeDiv labels
 // have changed since the last rebuild.
