@@ -232,6 +232,8 @@ constexpr int64_t kFp32ChunkBytes = 512ll << 20;  // dense product chunk of the 
 // About 40 ms of GPU work at the benchmark shape, so a host thread descheduled or
 // held in the driver for that long does not leave the GPU idle.
 constexpr int kLookahead = 8;
+// Row chunks of a host-buffer call's upload (bytes of points per chunk).
+constexpr int64_t kUploadChunkBytes = 256ll << 20;
 // Outside the pruned iterations of the fused path, the label-sorted visiting
 // order is rebuilt every kResortEvery iterations.  It only shapes performance
 // (assignments are per point; the update's FP64 sums are order-dependent in
@@ -334,8 +336,53 @@ struct MirrorLease {
     LoopMirror* operator->() const { return m; }
 };
 
+// Host-to-device copy of the points in row chunks on a side stream, an event
+// after each, so that work on the first chunks can start while the rest is
+// in flight.  The side stream first waits for the compute stream's prior work
+// (the destination may have just been allocated on it).  Destruction waits for
+// the copies.
+struct ChunkedUpload {
+    cudaStream_t side = nullptr;
+    cudaEvent_t ready = nullptr;  // the compute stream's prior work
+    std::vector<cudaEvent_t> ev;  // chunk c has landed
+    std::vector<int64_t> start;   // chunk c is rows [start[c], start[c + 1])
+    ~ChunkedUpload() {
+        for (cudaEvent_t e : ev) {
+            cudaEventSynchronize(e);
+            cudaEventDestroy(e);
+        }
+        if (ready) cudaEventDestroy(ready);
+        if (side) {
+            cudaStreamSynchronize(side);
+            cudaStreamDestroy(side);
+        }
+    }
+    int begin(float* dst, const float* src, int64_t n, int d, cudaStream_t compute) {
+        const int64_t chunk = std::max<int64_t>(kPointTileRows, (kUploadChunkBytes / (4 * (int64_t)d)) /
+                                                                    kPointTileRows * kPointTileRows);
+        for (int64_t r = 0; r < n; r += chunk) start.push_back(r);
+        start.push_back(n);
+        MXK_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+        MXK_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+        MXK_CUDA(cudaEventRecord(ready, compute));
+        MXK_CUDA(cudaStreamWaitEvent(side, ready, 0));
+        for (size_t c = 0; c + 1 < start.size(); ++c) {
+            cudaEvent_t e = nullptr;
+            MXK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            ev.push_back(e);
+            const int64_t r0 = start[c], rows = start[c + 1] - r0;
+            MXK_CUDA(cudaMemcpyAsync(dst + r0 * d, src + r0 * d, sizeof(float) * (size_t)(rows * d),
+                                     cudaMemcpyHostToDevice, side));
+            MXK_CUDA(cudaEventRecord(e, side));
+        }
+        return MXK_OK;
+    }
+    size_t chunks() const { return ev.size(); }
+};
+
 int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* centroids, int* labels,
-              const mxk_options* options, int* iterations, cudaStream_t stream, bool cache_points = false) {
+              const mxk_options* options, int* iterations, cudaStream_t stream, bool cache_points = false,
+              const float* host_points = nullptr) {
     MXK_REQUIRE(options && iterations, "kmeans_mixed: null options or iterations");
     PhaseRange call_range("kmeans_mixed");
     MXK_REQUIRE(k > 0 && d > 0 && n >= 0, "kmeans_mixed: require n >= 0, d > 0, k > 0");
@@ -488,8 +535,21 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         MXK_CHECK(ws.alloc(&dots, chunk_rows * k));
     }
 
-    // Once per run (kmeans.cu:24-27).
-    MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
+    // Host points (`points` is then the device buffer they go to): on the fused
+    // MX path the first iteration works chunk by chunk as the rows land (their
+    // norms, assignment and accumulation), overlapping the rest of the copy;
+    // otherwise one copy first.
+    const bool upload = host_points != nullptr && n > 0;
+    const bool overlap = upload && prune && !cache && d == 128 && options->fp32_iterations == 0;
+    ChunkedUpload up;
+    if (overlap)
+        MXK_CHECK(up.begin(const_cast<float*>(points), host_points, n, d, stream));
+    else if (upload)
+        MXK_CUDA(cudaMemcpyAsync(const_cast<float*>(points), host_points, sizeof(float) * (size_t)(n * d),
+                                 cudaMemcpyHostToDevice, stream));
+
+    // Once per run (kmeans.cu:24-27); with the chunked upload, per chunk below.
+    if (!overlap) MXK_CHECK(launch_l2_norm(n, d, points, pnorm, stream));
     // (with pruning the sort reorders the visiting order, first the points' own;
     // the first pruned iteration writes the rows' pruning records)
     if (prune) MXK_CHECK(launch_identity_order(n, order, stream));
@@ -622,8 +682,26 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
             // (pinfo's second slot; pruned_its counts this iteration already)
             am.second_bound = prune_it && pruned_its > kSecondBoundFrom;
             am.beta_max32 = bmax32;
-            MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows, stream,
-                                     true, fused_q ? points : nullptr, n));
+            if (overlap && it == 0) {
+                // each chunk as it lands: norms, assignment (points in their own
+                // order, no previous labels), fresh accumulation
+                for (size_t c = 0; c < up.chunks(); ++c) {
+                    const int64_t r0 = up.start[c], rows = up.start[c + 1] - r0;
+                    MXK_CUDA(cudaStreamWaitEvent(stream, up.ev[c], 0));
+                    MXK_CHECK(launch_l2_norm(rows, d, points + r0 * d, pnorm + r0, stream));
+                    MxArgmin ac = am;
+                    ac.point_norms = pnorm + r0;
+                    ac.labels = labels + r0;
+                    ac.row_labels = am.row_labels ? am.row_labels + r0 : nullptr;
+                    MXK_CHECK(launch_gemm_mx(8, rows, k, d, nullptr, nullptr, qcent, cscales, nullptr, &ac, nullptr,
+                                             stream, true, points + r0 * d, rows));
+                    MXK_CHECK(launch_accumulate(rows, d, k, points + r0 * d, labels + r0, nullptr, sums, counts,
+                                                stream, loop));
+                }
+            } else {
+                MXK_CHECK(launch_gemm_mx(8, n, k, d, qpoints, pscales, qcent, cscales, nullptr, &am, gemm_rows,
+                                         stream, true, fused_q ? points : nullptr, n));
+            }
             if (traced && trace.group_sizes)  // (0, 0, rows of the MXFP8 group)
                 MXK_CUDA(cudaMemcpyAsync(trace.group_sizes + 3 * it + 2, loop + 3, sizeof(int),
                                          cudaMemcpyDeviceToDevice, stream));
@@ -715,7 +793,7 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
         if (incremental)
             MXK_CHECK(launch_accumulate_changes(d, k, points, chg, chg_count, sums, counts, stream,
                                                 switchable ? upd_gate : loop));
-        if (!incremental || switchable)
+        if ((!incremental || switchable) && !(overlap && it == 0))  // (accumulated per chunk above)
             MXK_CHECK(launch_accumulate(n, d, k, points, labels, ord, sums, counts, stream,
                                         switchable ? upd_gate + 1 : loop, switchable));
         if (sharded) {
@@ -760,6 +838,17 @@ int run_lloyd(Comm* comm, int64_t n, int d, int k, const float* points, float* c
 }
 
 }  // namespace
+
+// For mxk_kmeans_mixed_multi (multi.cpp): kmeans_mixed (comm null) or
+// kmeans_mixed_sharded over points copied from the host into dev_points within
+// the call, the copy overlapping the first iteration where the path allows.
+int kmeans_mixed_from_host(void* comm, int64_t n, int d, int k, const float* host_points, float* dev_points,
+                           float* centroids, int* labels, const mxk_options* options, int* iterations,
+                           cudaStream_t stream) {
+    Comm* c = static_cast<Comm*>(comm);
+    MXK_REQUIRE(host_points || n == 0, "kmeans_mixed_multi: null points");
+    return run_lloyd(c, n, d, k, dev_points, centroids, labels, options, iterations, stream, false, host_points);
+}
 
 // For mxk_kmeans_mixed_multi (multi.cpp): the shared failure flag of its
 // in-process ranks, and the abort of a failed rank's communicator (frees it).

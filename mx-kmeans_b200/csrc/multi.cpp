@@ -5,10 +5,12 @@
 // Rows are split into contiguous shards (n / G rows each, the first n % G
 // shards one more), shard g lives on device g, centroids are replicated, and
 // every Lloyd iteration all-reduces the K x D sums and K counts over NCCL
-// (mxk_kmeans_mixed_sharded).  One host thread drives each GPU.  Uploads run
-// first on every GPU; the communicator is created only once all of them have
-// succeeded, so a failed upload or allocation cannot leave the other ranks
-// waiting in NCCL initialisation.  After that, a rank that fails raises a flag
+// (mxk_kmeans_mixed_sharded).  One host thread drives each GPU.  Allocations
+// and the centroids' upload run first on every GPU; the communicator is
+// created only once all of them have succeeded, so a failed allocation cannot
+// leave the other ranks waiting in NCCL initialisation.  Each shard's points
+// are then copied in row chunks by the Lloyd call itself, which starts the
+// first iteration on the chunks that have landed.  A rank that fails raises a flag
 // shared by the ranks; the others' host waits poll it, abort their
 // communicators (which ends the collectives that wait for the failed rank) and
 // return an error, so the call reports the failure instead of hanging.
@@ -27,6 +29,9 @@ int fail(int status, const std::string& message);
 void comm_attach_group_flag(void* comm, std::atomic<int>* flag);
 void comm_abort(void* comm);
 cudaMemPool_t workspace_pool();
+int kmeans_mixed_from_host(void* comm, int64_t n, int d, int k, const float* host_points, float* dev_points,
+                           float* centroids, int* labels, const mxk_options* options, int* iterations,
+                           cudaStream_t stream);
 }
 
 namespace {
@@ -111,8 +116,7 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
     }
 
     // Phase 1: allocate (from the library's stream-ordered pool on each device,
-    // whose blocks stay mapped between calls) and upload the shard and the
-    // initial centroids.
+    // whose blocks stay mapped between calls) and upload the initial centroids.
     on_every_gpu(shards, [&](Shard& s) {
         const size_t rows = size_t(std::max<int64_t>(s.rows, 1));
         if (!s.record_cuda(cudaSetDevice(s.device), "cudaSetDevice") ||
@@ -133,11 +137,9 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
                                                    s.stream),
                            "cudaMallocFromPoolAsync"))
             return;
-        if (!s.record_cuda(cudaMemcpyAsync(s.points, points + size_t(s.row0) * size_t(d),
-                                           sizeof(float) * size_t(s.rows) * size_t(d), cudaMemcpyHostToDevice,
-                                           s.stream),
-                           "cudaMemcpyAsync") ||
-            !s.record_cuda(cudaMemcpyAsync(s.centroids, centroids, centroid_bytes, cudaMemcpyHostToDevice, s.stream),
+        // (the shard's points are copied by the Lloyd call itself, overlapping its
+        // first iteration)
+        if (!s.record_cuda(cudaMemcpyAsync(s.centroids, centroids, centroid_bytes, cudaMemcpyHostToDevice, s.stream),
                            "cudaMemcpyAsync"))
             return;
         s.record_cuda(cudaStreamSynchronize(s.stream), "cudaStreamSynchronize");
@@ -159,15 +161,16 @@ extern "C" int mxk_kmeans_mixed_multi(int64_t n, int d, int k, const float* poin
             if (G > 1) {
                 if (!s.record(mxk_comm_init(&s.comm, G, s.device, uid))) return;
                 mxk::comm_attach_group_flag(s.comm, &group_failed);
-                if (!s.record(mxk_kmeans_mixed_sharded(s.comm, s.rows, d, k, s.points, s.centroids, s.labels, options,
-                                                       &s.iterations, s.stream))) {
+                if (!s.record(mxk::kmeans_mixed_from_host(s.comm, s.rows, d, k, points + size_t(s.row0) * size_t(d),
+                                                          s.points, s.centroids, s.labels, options, &s.iterations,
+                                                          s.stream))) {
                     int none = -1;
                     if (!group_failed.load()) first_failed.compare_exchange_strong(none, s.device);
                     group_failed.store(1);  // the other ranks stop waiting for this one
                     return;
                 }
-            } else if (!s.record(mxk_kmeans_mixed(s.rows, d, k, s.points, s.centroids, s.labels, options,
-                                                  &s.iterations, s.stream))) {
+            } else if (!s.record(mxk::kmeans_mixed_from_host(nullptr, s.rows, d, k, points, s.points, s.centroids,
+                                                             s.labels, options, &s.iterations, s.stream))) {
                 return;
             }
             if (!s.record_cuda(cudaMemcpyAsync(labels + s.row0, s.labels, sizeof(int) * size_t(s.rows),
