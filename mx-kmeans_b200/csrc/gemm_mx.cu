@@ -384,14 +384,19 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms
 // exact path when gaps are needed, one column at a time past n.  The chunk
 // holding column `forced` (the row's previous label, or -1) is always
 // evaluated exactly, so a row whose minimum starts at a bound finds a centroid.
+// screen: take the key screen first (else every chunk takes the exact path,
+// cheaper when most chunks would fail the screen anyway -- rows without a
+// sweep hint or bound, whose minima still improve often).
 template <bool kGaps, bool kSec, class Norms>
 __device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, float pn, float pc,
-                                           int cc, int64_t n, RowMin& m, int forced) {
+                                           int cc, int64_t n, RowMin& m, int forced, bool screen = true) {
     if (cc + 32 <= n) {
         if constexpr (kGaps)
             argmin_chunk32<true, false>(v, cn, pn2, cc, m);
-        else
+        else if (screen)
             argmin_chunk32_screened<kSec>(v, cn, pn2, pn, pc, cc, m, (unsigned)(forced - cc) < 32u);
+        else
+            argmin_chunk32<false, kSec>(v, cn, pn2, cc, m, (unsigned)(forced - cc) < 32u, pn);
     } else if (cc < n) {
         argmin_tail<kGaps, kSec>(v, cn, pn, cc, n, m, forced);
     }
@@ -980,6 +985,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // winner and rarely needs an index search.  With row bounds each row's
         // minimum starts at its bound instead, which needs no exchange.
         const bool seeding = kArgmin && tiles_n >= 2 && !p.row_bound;
+        // (no sweep hint and no row bounds: most chunks improve some row of the warp)
+        const bool screen = p.start_hint || p.row_bound;
         // One warp hands the tile's centroid-ring slots back to the producer:
         // acc_full means every MMA that read them has completed.
         const bool releaser = p.epi_release && q == 0 && j == 0 && lane == 0;
@@ -1091,9 +1098,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else if (p.cn_smem) {
                         fold_chunk<kGaps, kSec>(v[sub], NormSrc<true>{p.cn, cn_saddr}, pn2, pn, pc, cc, p.n, m,
-                                                forced);
+                                                forced, screen);
                     } else {
-                        fold_chunk<kGaps, kSec>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m, forced);
+                        fold_chunk<kGaps, kSec>(v[sub], NormSrc<false>{p.cn, 0u}, pn2, pn, pc, cc, p.n, m, forced,
+                                                screen);
                     }
                 }
                 if (seeding && i == 0 && (tmask & (tmask - 1ull)) != 0) {  // (more tiles follow in this row tile)

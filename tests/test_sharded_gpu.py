@@ -63,14 +63,17 @@ def test_two_gpu_sharded_matches_single_gpu(n, d, k, seed, iters):
     assert np.array_equal(labels, single_labels)
 
 
-@pytest.mark.parametrize("gpus", [1, 2])
-def test_multi_entry_matches_single_gpu(torch_cuda, mxk, gpus):
+@pytest.mark.parametrize("gpus,n", [(1, 20011), (2, 20011), (1, 1100011), (2, 1100011)])
+def test_multi_entry_matches_single_gpu(torch_cuda, mxk, gpus, n):
     """mxk_kmeans_mixed_multi (host buffers, one thread per GPU, NCCL inside the
-    library) against kmeans_mixed on one GPU: bit-identical on integer data."""
+    library) against kmeans_mixed on one GPU: bit-identical on integer data.
+    The larger n spans several of the 256 MB upload chunks on which the first
+    iteration starts while the rest of the copy is in flight (a partial last
+    chunk included)."""
     torch = torch_cuda
     if torch.cuda.device_count() < gpus:
         pytest.skip(f"needs {gpus} GPUs")
-    n, d, k, seed, iters = 20011, 128, 40, 9, 8
+    d, k, seed, iters = 128, 40, 9, 8
     x, c0 = _blob_data(n, d, k, seed)
     opts = mxk.Options(max_iterations=iters, tolerance=0.0)
     xf = torch.from_numpy(x).cuda()
