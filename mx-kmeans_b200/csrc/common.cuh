@@ -276,25 +276,15 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // --- packed FP32 pairs and 3-input min (sm_100) ----------------------------
 
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-
-// (d0, d1) = fmaf(-2, (v0, v1), pn2 + (c0, c1)) with .f32x2 add and fma; every
-// lane is rounded exactly as the scalar add and fmaf would round it.
-__device__ __forceinline__ void dist2(uint32_t v0, uint32_t v1, uint64_t pn2, float c0, float c1, float& d0,
+// (d0, d1) = fmaf(-2, (v0, v1), pn2 + (c0, c1)) with packed FP32 add and fma
+// (add.f32x2 / fma.f32x2); every lane is rounded exactly as the scalar add and
+// fmaf would round it.
+__device__ __forceinline__ void dist2(uint32_t v0, uint32_t v1, float2 pn2, float c0, float c1, float& d0,
                                       float& d1) {
-    asm("{\n\t.reg .b64 s, v, m, d;\n\t"
-        "mov.b64 s, {%3, %4};\n\t"
-        "add.rn.f32x2 s, %2, s;\n\t"
-        "mov.b64 v, {%5, %6};\n\t"
-        "mov.b64 m, {%7, %7};\n\t"
-        "fma.rn.f32x2 d, m, v, s;\n\t"
-        "mov.b64 {%0, %1}, d;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "l"(pn2), "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
+    const float2 s = __fadd2_rn(pn2, make_float2(c0, c1));
+    const float2 d = __ffma2_rn(make_float2(-2.0f, -2.0f), make_float2(__uint_as_float(v0), __uint_as_float(v1)), s);
+    d0 = d.x;
+    d1 = d.y;
 }
 
 // 16-byte shared-memory load through an explicit shared-window address.
@@ -315,27 +305,19 @@ __device__ __forceinline__ float lds_f1(uint32_t saddr) {
     return r;
 }
 
-// (k0, k1) = fmaf(-2, (v0, v1), (c0, c1)) with one .f32x2 fma.
+// (k0, k1) = fmaf(-2, (v0, v1), (c0, c1)) with one packed FP32 fma.
 __device__ __forceinline__ void key2(uint32_t v0, uint32_t v1, float c0, float c1, float& k0, float& k1) {
-    asm("{\n\t.reg .b64 c, v, m, d;\n\t"
-        "mov.b64 c, {%2, %3};\n\t"
-        "mov.b64 v, {%4, %5};\n\t"
-        "mov.b64 m, {%6, %6};\n\t"
-        "fma.rn.f32x2 d, m, v, c;\n\t"
-        "mov.b64 {%0, %1}, d;\n\t}"
-        : "=f"(k0), "=f"(k1)
-        : "f"(c0), "f"(c1), "r"(v0), "r"(v1), "f"(-2.0f));
+    const float2 k = __ffma2_rn(make_float2(-2.0f, -2.0f), make_float2(__uint_as_float(v0), __uint_as_float(v1)),
+                                make_float2(c0, c1));
+    k0 = k.x;
+    k1 = k.y;
 }
 
-// (x0, x1) *= s with one .f32x2 multiply; each lane is rounded like the scalar multiply.
+// (x0, x1) *= s with one packed FP32 multiply; each lane is rounded like the scalar multiply.
 __device__ __forceinline__ void mul2(float& x0, float& x1, float s) {
-    asm("{\n\t.reg .b64 v, m;\n\t"
-        "mov.b64 v, {%0, %1};\n\t"
-        "mov.b64 m, {%2, %2};\n\t"
-        "mul.rn.f32x2 v, v, m;\n\t"
-        "mov.b64 {%0, %1}, v;\n\t}"
-        : "+f"(x0), "+f"(x1)
-        : "f"(s));
+    const float2 x = __fmul2_rn(make_float2(x0, x1), make_float2(s, s));
+    x0 = x.x;
+    x1 = x.y;
 }
 
 __device__ __forceinline__ float min3f(float a, float b, float c) {

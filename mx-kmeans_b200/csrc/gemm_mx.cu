@@ -273,7 +273,7 @@ struct RowMin {
 // m holds no centroid yet (m.first is then only a bound).  kSec: the columns
 // that are not (or no longer) the minimum lower m.sec.
 template <bool kGaps, bool kSec, class Norms>
-__device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, int c0,
+__device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const Norms& cn, float2 pn2, int c0,
                                                RowMin& m, bool force = false, float pn = 0.0f) {
     float dist[32];
 #pragma unroll
@@ -332,7 +332,7 @@ __device__ __forceinline__ void argmin_chunk32(const uint32_t (&v)[32], const No
 // lowers m.sec to its k_min (each d_j >= pn + k_min - 2^-18 (pc + |k_min|) by
 // the same rounding argument).
 template <bool kSec, class Norms>
-__device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2,
+__device__ __forceinline__ void argmin_chunk32_screened(const uint32_t (&v)[32], const Norms& cn, float2 pn2,
                                                         float pn, float pc, int c0, RowMin& m, bool force) {
     // keys folded into two running 3-input minima as they are formed (few live registers)
     float ka = __int_as_float(0x7f800000), kb = ka;
@@ -388,7 +388,7 @@ __device__ __forceinline__ void argmin_tail(const uint32_t (&v)[32], const Norms
 // cheaper when most chunks would fail the screen anyway -- rows without a
 // sweep hint or bound, whose minima still improve often).
 template <bool kGaps, bool kSec, class Norms>
-__device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, uint64_t pn2, float pn, float pc,
+__device__ __forceinline__ void fold_chunk(const uint32_t (&v)[32], const Norms& cn, float2 pn2, float pn, float pc,
                                            int cc, int64_t n, RowMin& m, int forced, bool screen = true) {
     if (cc + 32 <= n) {
         if constexpr (kGaps)
@@ -1054,7 +1054,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 rb_nxt = bound_of(tile + step);
             const int forced = __float_as_int(rb.y);
             const int64_t id_nn = row_id(tile + 2 * step), lead_nn = lead_id(tile + 2 * step);
-            const uint64_t pn2 = dev::pack2(pn, pn);
+            const float2 pn2 = make_float2(pn, pn);
             const float pc = pn + cmax;
             RowMin m{rb.x, -1e38f, -1e38f, kNoLabel, __int_as_float(0x7f800000)};
             for (int i = 0; i < tiles_n; ++i) {
