@@ -341,7 +341,7 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
                                               bool second, bool fresh, const SetTerms& gs,
                                               const int* __restrict__ prev_label,
                                               float4* __restrict__ pinfo, const float4* __restrict__ cst,
-                                              const float4* __restrict__ cst_old, const float4* __restrict__ tst,
+                                              const float4* __restrict__ cst_old, const float4* tcs,
                                               const float* __restrict__ delta, const float* __restrict__ dmin,
                                               float4* __restrict__ row_bound, int compact, uint64_t& m, bool& need) {
     const float inf = __int_as_float(0x7f800000);
@@ -399,20 +399,25 @@ __device__ __forceinline__ void row_tile_mask(int64_t row, int64_t rows, int k, 
                 excl = hf;  // every other centroid strictly farther: no per-tile test
             } else {
                 const float* dm = dmin + (int64_t)a * tiles;
+                // rho of each tile's worst centroid: kp + tc.x + shx tc.y (the
+                // per-tile terms of rho_bound, scaled up by 2e-6 to cover the
+                // re-associated sum)
+                const float kp = kappa * (1.0f + 2e-6f) * pxh;
+                const float aal = fabsf(al);
 #pragma unroll 8
                 for (int t = 0; t < tiles; ++t) {  // (unrolled: the tiles' loads issue together)
-                    const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
+                    const float4 tc = tcs[t];
                     const float gt = fmaxf(dm[t] - r, 0.0f);
                     const float g2 = gt * gt * (1.0f - 1e-6f);
-                    const float rt = rho_bound(pxh, shx, ts.z, ts.y, tst[tiles + t].z, kappa);
-                    const float lb = g2 + al + ts.x - rt;
-                    const float lbm = lb - 1e-4f * (fabsf(lb) + fabsf(al) + fabsf(ts.x));
-                    if (!(lbm > um) || ts.w != 0.0f) {
+                    const float rt = fmaf(shx, tc.y, kp + tc.x);
+                    const float lb = g2 + al + tc.z - rt;
+                    const float lbm = lb - 1e-4f * (fabsf(lb) + aal + tc.w);
+                    if (!(lbm > um)) {  // (false for a non-finite tile: tc.z is NaN)
                         m |= 1ull << t;
                         need = true;
                     } else {
                         const float f = g2 + al - rt;
-                        excl = fminf(excl, fmaxf(f - 1e-4f * (fabsf(f) + fabsf(al)), hf));
+                        excl = fminf(excl, fmaxf(f - 1e-4f * (fabsf(f) + aal), hf));
                     }
                 }
             }
@@ -534,6 +539,17 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     const float inf = __int_as_float(0x7f800000);
     __shared__ SetTerms gs_s;
     __shared__ int g_ok;
+    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
+    // per centroid tile: (kappa' (max |c|^2 + max |c^|^2), 2 kappa' max |c^|,
+    // min beta -- NaN for a tile with a non-finite centroid --, |min beta|),
+    // kappa' = kappa (1 + 2e-6)
+    __shared__ float4 tcs[kMaxPruneTiles];
+    for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+        const float4 ts = tst[t];  // (min beta, max |c^|^2, max |c|^2, non-finite)
+        const float kq = kappa * (1.0f + 2e-6f);
+        const float bmin = ts.w != 0.0f ? __int_as_float(0x7fc00000) : ts.x;
+        tcs[t] = make_float4(kq * (ts.z + ts.y), 2.0f * kq * tst[tiles + t].z, bmin, fabsf(bmin));
+    }
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         // v = (min beta, max |c^|^2, max |c|^2, max delta; previous: max |c^|^2, max |c|^2)
@@ -562,7 +578,6 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     const SetTerms gs = gs_s;
     const bool second = g_ok != 0;
     const uint64_t all = tiles >= 64 ? ~0ull : ((1ull << tiles) - 1ull);
-    const float kappa = 3e-5f + (float)(d + 8) * 1.2e-7f;
     const int64_t ntiles = (rows + 127) / 128;
     const int lane = threadIdx.x & 31;
     for (int64_t tile = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); tile < ntiles; tile += (int64_t)gridDim.x * 4) {
@@ -573,7 +588,7 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
             uint64_t mr;
             bool need;
             row_tile_mask(tile * 128 + q * 32 + lane, rows, k, tiles, all, kappa, second, fresh != 0, gs, prev_label,
-                          pinfo, cst, cst_old, tst, delta, dmin, row_bound, compact, mr, need);
+                          pinfo, cst, cst_old, tcs, delta, dmin, row_bound, compact, mr, need);
             m |= mr;
             nb[q] = __ballot_sync(0xffffffffu, need);
         }
