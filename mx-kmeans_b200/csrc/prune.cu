@@ -644,6 +644,7 @@ __global__ void __launch_bounds__(kScanSeg) work_scan_kernel(int ntiles, const i
 // (at most two) compacted 128-row tiles its rows land in.
 // Block 0 also writes *work_rows, the number of rows that stay (0 once the loop
 // has stopped, so that the GEMM launches of later iterations do nothing).
+constexpr int kScatterTiles = 8;  // point tiles per work_scatter block (kScanSeg is a multiple)
 __global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const int* __restrict__ pid,
                                                            const float4* __restrict__ row_bound,
                                                            const uint4* __restrict__ need_bits,
@@ -654,10 +655,12 @@ __global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const i
                                                            int* __restrict__ work_pid, float4* __restrict__ work_rb,
                                                            unsigned long long* __restrict__ cmask,
                                                            int* __restrict__ work_rows, const int* __restrict__ stop) {
+    static_assert(kScanSeg % kScatterTiles == 0, "a block's tiles share one scan segment");
     const bool stopped = stop && *stop;
+    const int64_t tile0 = (int64_t)blockIdx.x * kScatterTiles;
     __shared__ int seg_base;
-    if (threadIdx.x < 32) {  // the totals of the segments before this tile's (all of them for block 0)
-        const int seg = blockIdx.x / kScanSeg;
+    if (threadIdx.x < 32) {  // the totals of the segments before this block's (all of them for block 0)
+        const int seg = (int)(tile0 / kScanSeg);
         const int upto = blockIdx.x == 0 ? nseg : seg;
         int acc = 0, mine = 0;
         if (!stopped)
@@ -675,27 +678,29 @@ __global__ void __launch_bounds__(128) work_scatter_kernel(int64_t rows, const i
             if (blockIdx.x == 0) *work_rows = stopped ? 0 : acc;
         }
     }
-    if (stopped || (int64_t)blockIdx.x * 128 >= rows) return;  // (block 0 of an empty shard: the count only)
+    if (stopped) return;
     __syncthreads();
-    const int cnt = counts[blockIdx.x];
-    if (cnt == 0) return;
-    const int64_t row = (int64_t)blockIdx.x * 128 + threadIdx.x;
-    const uint4 nb = need_bits[blockIdx.x];
-    const unsigned words[4] = {nb.x, nb.y, nb.z, nb.w};
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int off = seg_base + offsets[blockIdx.x];
-    if ((words[w] >> lane) & 1u) {
-        int before = __popc(words[w] & ((1u << lane) - 1u));
-        for (int v = 0; v < w; ++v) before += __popc(words[v]);
-        const int pos = off + before;
-        work_pid[pos] = pid ? pid[row] : (int)row;
-        work_rb[pos] = row_bound[row];
-    }
-    if (threadIdx.x == 0) {
-        const uint64_t m = mask[blockIdx.x];
-        const int j0 = off >> 7, j1 = (off + cnt - 1) >> 7;
-        atomicOr(cmask + j0, (unsigned long long)m);
-        if (j1 != j0) atomicOr(cmask + j1, (unsigned long long)m);
+    for (int64_t tile = tile0; tile < tile0 + kScatterTiles && tile * 128 < rows; ++tile) {
+        const int cnt = counts[tile];
+        if (cnt == 0) continue;
+        const int64_t row = tile * 128 + threadIdx.x;
+        const uint4 nb = need_bits[tile];
+        const unsigned words[4] = {nb.x, nb.y, nb.z, nb.w};
+        const int off = seg_base + offsets[tile];
+        if ((words[w] >> lane) & 1u) {
+            int before = __popc(words[w] & ((1u << lane) - 1u));
+            for (int v = 0; v < w; ++v) before += __popc(words[v]);
+            const int pos = off + before;
+            work_pid[pos] = pid ? pid[row] : (int)row;
+            work_rb[pos] = row_bound[row];
+        }
+        if (threadIdx.x == 0) {
+            const uint64_t m = mask[tile];
+            const int j0 = off >> 7, j1 = (off + cnt - 1) >> 7;
+            atomicOr(cmask + j0, (unsigned long long)m);
+            if (j1 != j0) atomicOr(cmask + j1, (unsigned long long)m);
+        }
     }
 }
 
@@ -789,7 +794,8 @@ int launch_tile_mask(int64_t rows, int k, int d, const int* pid, const int* prev
     }
     {  // (at least one block: it writes the row count)
         LaunchScope scope("work_scatter", stream);
-        work_scatter_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 128, 0, stream>>>(
+        work_scatter_kernel<<<(unsigned)std::max<int64_t>((blocks + kScatterTiles - 1) / kScatterTiles, 1), 128, 0,
+                              stream>>>(
             rows, pid, row_bound, work->need_bits, work->offsets, work->counts, work->seg_total, nseg, mask,
             work->pid, work->rb, work->cmask, work->rows, stop);
         MXK_CUDA(cudaGetLastError());
